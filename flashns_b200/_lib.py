@@ -1,0 +1,46 @@
+"""ctypes binding of ``libflashns_b200.so`` (the C ABI in ``include/flashns_b200.h``).
+
+There is no CPU or library fallback: every entry point needs the in-tree CUDA
+library, and loading fails loudly when it has not been built.
+"""
+
+import ctypes
+from pathlib import Path
+
+LIBRARY = Path(__file__).resolve().parent / "libflashns_b200.so"
+
+_c_int, _c_i64, _c_dbl, _c_ptr, _c_size = ctypes.c_int, ctypes.c_int64, ctypes.c_double, ctypes.c_void_p, ctypes.c_size_t
+
+# name -> (argtypes); every function returns int (a cudaError_t value)
+SIGNATURES = {
+    "flashns_b200_plan_create": [_c_int, _c_int, _c_int, _c_int, ctypes.POINTER(_c_int), _c_i64, _c_i64,
+                                 _c_dbl, _c_dbl, _c_dbl, ctypes.POINTER(_c_ptr)],
+    "flashns_b200_plan_destroy": [_c_ptr],
+    "flashns_b200_plan_workspace_bytes": [_c_ptr, ctypes.POINTER(_c_size)],
+    "flashns_b200_plan_parameter_count": [_c_ptr, ctypes.POINTER(_c_i64)],
+    "flashns_b200_plan_launch_count": [_c_ptr, ctypes.POINTER(_c_int)],
+    "flashns_b200_eval": [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_ptr],
+}
+
+_library = None
+
+
+def library():
+    """Load the CUDA library once; raise if it is missing."""
+    global _library
+    if _library is None:
+        if not LIBRARY.exists():
+            raise RuntimeError(f"{LIBRARY} is missing: build it with `python -m flashns_b200.build` "
+                               "(there is no CPU fallback)")
+        lib = ctypes.CDLL(str(LIBRARY))
+        for name, argtypes in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = argtypes
+            fn.restype = ctypes.c_int
+        _library = lib
+    return _library
+
+
+def check(status, what):
+    if status:
+        raise RuntimeError(f"{what} returned CUDA error {status}")

@@ -1,0 +1,1327 @@
+// Fused FP64 loss + parameter-gradient evaluation of a packed jet MLP (sm_100a).
+//
+// Replaces the evaluation behind PackedPINN.__call__ (src/flashns/pinn_packed.py:93-191)
+// and its per-stage CUDA hooks (experiments/pinn_v8/native.cu) with one chain of
+// persistent kernels per evaluation:
+//
+//   pack_params   flat [W_0..W_L, b_0..b_L] -> zero-padded per-layer buffers
+//   first_layer   coordinates -> layer-0 affine -> stable tanh jet  (H_1, a1_1)
+//   fwd_layer     H_l -> DMMA GEMM with W_l -> bias on order-0 rows -> tanh jet epilogue
+//   head_layer    output layer + residual seed + output-layer wgrad + dgrad + jet VJP
+//   bwd_layer     DMMA dgrad D_{l+1} W_l -> jet VJP epilogue (D_l); the layer-1 instance
+//                 contracts D_1 with the coordinate jets instead of storing it
+//   wgrad         dW_l = D_{l+1}^T H_l, split over rows, DMMA, deterministic partials
+//   reduce        fixed-order sum of all partials -> grad[P] and loss
+//
+// Layout in HBM: packed rows [interior points x Q ; boundary points x QB] x C,
+// FP64 row-major, C padded to 32/64/128 with zero weights (padded channels stay
+// exactly zero through the chain).
+#include <algorithm>
+#include <cstdint>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "common.cuh"
+#include "jets_generated.cuh"
+#include "residual_generated.cuh"
+#include "flashns_b200.h"
+
+namespace flashns_b200 {
+
+constexpr int kThreads = 256;
+constexpr int kStages = 3;
+constexpr int KC = 16;       // k-chunk (doubles) per pipeline stage
+constexpr int LDC = KC + 4;  // padded chunk row: conflict-free FP64 fragment loads
+constexpr int kMaxAffine = 16;
+
+struct Geometry {
+  int64_t ni, nb;  // interior (full-jet) and boundary points
+  int64_t rows;    // ni*Q + nb*QB
+};
+
+template <int DIM, int ORDER>
+struct Jet;
+#define FLASHNS_JET(D, O, N)                                                                  \
+  template <>                                                                                 \
+  struct Jet<D, O> {                                                                          \
+    static constexpr int n = N;                                                               \
+    __device__ static void fwd(const double* z, double* h, double& a) { jet_fwd_##D##d##O(z, h, a); } \
+    __device__ static void vjp(const double* h, double a, const double* hb, double* zb) {     \
+      jet_vjp_##D##d##O(h, a, hb, zb);                                                        \
+    }                                                                                         \
+  };
+FLASHNS_JET(2, 0, 1)
+FLASHNS_JET(2, 1, 3)
+FLASHNS_JET(2, 3, 10)
+FLASHNS_JET(3, 0, 1)
+FLASHNS_JET(3, 1, 4)
+FLASHNS_JET(3, 3, 20)
+#undef FLASHNS_JET
+
+// ----------------------------------------------------------------------------------
+// Tiles of the DMMA kernels.  The GEMM is computed transposed: MMA M = channels,
+// MMA N = packed rows, so a thread's accumulators hold, for two channels per m16 tile,
+// the rows 8j+2t and 8j+2t+1 of every n8 tile j.  Rows are permuted in shared memory
+// so that these S = Q rows are the Q jet coefficients of one point ("thread column").
+// The tanh-jet epilogue and its VJP then run entirely in registers.
+template <int DIM, int CP>
+struct MmaTile {
+  static constexpr int S = Basis<DIM>::Q;     // slots per thread column
+  static constexpr int NT = S / 2;            // n8 tiles per warp
+  static constexpr int MT = DIM == 2 ? 2 : 1; // m16 tiles per warp
+  static constexpr int WCH = 16 * MT;         // channels per warp
+  static constexpr int WC = CP / WCH;         // warps along channels
+  static constexpr int WR = 8 / WC;           // warp row groups
+  static constexpr int TC = 4 * WR;           // thread columns per tile
+  static constexpr int TR = TC * S;           // packed rows per tile
+  static_assert(CP % WCH == 0 && WC >= 1 && 8 % WC == 0, "unsupported padded width");
+};
+
+// Interior tiles carry TC points (Q rows each); boundary tiles carry TC*PS points of
+// QB rows (QB = 1 value rows, QB = DIM+1 first-order rows).
+template <int DIM, int BO, int TC>
+struct Tiles {
+  static constexpr int Q = Basis<DIM>::Q;
+  static constexpr int QB = BO ? DIM + 1 : 1;
+  static constexpr int PS = Q / QB;
+  __host__ __device__ static int64_t interior(int64_t ni) { return (ni + TC - 1) / TC; }
+  __host__ __device__ static int64_t boundary(int64_t nb) { return (nb + int64_t(TC) * PS - 1) / (int64_t(TC) * PS); }
+  __device__ static int64_t row(const Geometry& g, int64_t nint, int64_t tile, int tc, int s) {
+    if (tile < nint) {
+      const int64_t p = tile * TC + tc;
+      return p < g.ni ? p * Q + s : -1;
+    }
+    if (s >= PS * QB) return -1;
+    const int64_t b = (tile - nint) * (int64_t(TC) * PS) + int64_t(tc) * PS + s / QB;
+    return b < g.nb ? g.ni * Q + b * QB + s % QB : -1;
+  }
+};
+
+// smem row r -> (thread column, slot) for the permuted tile layout
+template <int S>
+__device__ __forceinline__ void tile_slot(int r, int& tc, int& s) {
+  const int wr = r / (4 * S), within = r % (4 * S);
+  const int j = within >> 3, rem = within & 7;
+  tc = wr * 4 + (rem >> 1);
+  s = 2 * j + (rem & 1);
+}
+
+template <int DIM, int CP>
+constexpr size_t fwd_smem_bytes() {
+  using T = MmaTile<DIM, CP>;
+  return sizeof(double) * kStages * (T::TR + CP) * LDC + sizeof(int64_t) * T::TR;
+}
+template <int DIM, int CP>
+constexpr size_t bwd_smem_bytes() {
+  using T = MmaTile<DIM, CP>;
+  constexpr size_t a = sizeof(double) * kStages * (size_t(T::TR) * LDC + size_t(KC) * (CP + 4)) + sizeof(int64_t) * T::TR;
+  constexpr size_t red = sizeof(double) * T::WR * CP * (DIM + 1);
+  return a > red ? a : red;
+}
+
+// ----------------------------------------------------------------------------------
+// forward hidden layer: H_{l+1} = tanh_jet(H_l W_l^T + b_l on order-0 rows)
+template <int DIM, int CP, int BO>
+__global__ void __launch_bounds__(kThreads, 2)
+    fwd_layer(const double* __restrict__ hin, int kin, const double* __restrict__ w,
+              const double* __restrict__ bias, double* __restrict__ hout, double* __restrict__ a1out,
+              Geometry geo) {
+  using T = MmaTile<DIM, CP>;
+  using TL = Tiles<DIM, BO, T::TC>;
+  constexpr int S = T::S, TR = T::TR, Q = TL::Q, QB = TL::QB;
+  extern __shared__ __align__(16) double smem[];
+  double* sB = smem;                     // activation chunks [stage][TR][LDC]
+  double* sA = sB + kStages * TR * LDC;  // weight chunks     [stage][CP][LDC]
+  int64_t* rowmap = reinterpret_cast<int64_t*>(sA + kStages * CP * LDC);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int wc = warp % T::WC, wr = warp / T::WC;
+  const int nk = kin / KC;
+  const int64_t nint = TL::interior(geo.ni);
+  const int64_t ntiles = nint + TL::boundary(geo.nb);
+
+  for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    __syncthreads();
+    for (int r = threadIdx.x; r < TR; r += kThreads) {
+      int tc, s;
+      tile_slot<S>(r, tc, s);
+      rowmap[r] = TL::row(geo, nint, tile, tc, s);
+    }
+    __syncthreads();
+    auto load = [&](int kc, int stage) {
+      double* dB = sB + stage * TR * LDC;
+      for (int i = threadIdx.x; i < TR * (KC / 2); i += kThreads) {
+        const int r = i / (KC / 2), p = i % (KC / 2);
+        const int64_t gr = rowmap[r];
+        cp_async16(dB + r * LDC + 2 * p, hin + (gr >= 0 ? gr : 0) * kin + kc * KC + 2 * p, gr >= 0);
+      }
+      double* dA = sA + stage * CP * LDC;
+      for (int i = threadIdx.x; i < CP * (KC / 2); i += kThreads) {
+        const int r = i / (KC / 2), p = i % (KC / 2);
+        cp_async16(dA + r * LDC + 2 * p, w + int64_t(r) * kin + kc * KC + 2 * p, true);
+      }
+    };
+    double acc[T::MT][T::NT][4];
+#pragma unroll
+    for (int i = 0; i < T::MT; ++i)
+#pragma unroll
+      for (int j = 0; j < T::NT; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0;
+#pragma unroll
+    for (int s = 0; s < kStages - 1; ++s) {
+      if (s < nk) load(s, s);
+      cp_async_commit();
+    }
+    for (int kc = 0; kc < nk; ++kc) {
+      cp_async_wait<kStages - 2>();
+      __syncthreads();
+      if (kc + kStages - 1 < nk) load(kc + kStages - 1, (kc + kStages - 1) % kStages);
+      cp_async_commit();
+      const double* cB = sB + (kc % kStages) * TR * LDC + wr * (4 * S) * LDC;
+      const double* cA = sA + (kc % kStages) * CP * LDC + wc * T::WCH * LDC;
+#pragma unroll
+      for (int kk = 0; kk < KC; kk += 8) {
+        double a[T::MT][4];
+#pragma unroll
+        for (int i = 0; i < T::MT; ++i) {
+          a[i][0] = cA[(16 * i + g) * LDC + kk + t];
+          a[i][1] = cA[(16 * i + g + 8) * LDC + kk + t];
+          a[i][2] = cA[(16 * i + g) * LDC + kk + t + 4];
+          a[i][3] = cA[(16 * i + g + 8) * LDC + kk + t + 4];
+        }
+#pragma unroll
+        for (int j = 0; j < T::NT; ++j) {
+          const double b0 = cB[(8 * j + g) * LDC + kk + t];
+          const double b1 = cB[(8 * j + g) * LDC + kk + t + 4];
+#pragma unroll
+          for (int i = 0; i < T::MT; ++i) mma_m16n8k8(acc[i][j], a[i], b0, b1);
+        }
+      }
+    }
+    // epilogue: bias on the order-0 coefficient, stable tanh jet, store H and a1
+    const int tc = wr * 4 + t;
+    const bool interior = tile < nint;
+#pragma unroll
+    for (int i = 0; i < T::MT; ++i) {
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int ch = wc * T::WCH + 16 * i + 8 * hh + g;
+        double z[S];
+#pragma unroll
+        for (int s = 0; s < S; ++s) z[s] = acc[i][s >> 1][2 * hh + (s & 1)];
+        const double bch = bias[ch];
+        if (interior) {
+          const int64_t p = tile * T::TC + tc;
+          if (p < geo.ni) {
+            double hv[Q], a1;
+            z[0] += bch;
+            Jet<DIM, 3>::fwd(z, hv, a1);
+            double* dst = hout + p * Q * CP + ch;
+#pragma unroll
+            for (int s = 0; s < Q; ++s) dst[int64_t(s) * CP] = hv[s];
+            a1out[p * CP + ch] = a1;
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < TL::PS; ++k) {
+            const int64_t b = (tile - nint) * (int64_t(T::TC) * TL::PS) + int64_t(tc) * TL::PS + k;
+            if (b < geo.nb) {
+              double zz[QB], hv[QB], a1;
+#pragma unroll
+              for (int c = 0; c < QB; ++c) zz[c] = z[k * QB + c];
+              zz[0] += bch;
+              Jet<DIM, BO ? 1 : 0>::fwd(zz, hv, a1);
+              double* dst = hout + (geo.ni * Q + b * QB) * CP + ch;
+#pragma unroll
+              for (int c = 0; c < QB; ++c) dst[int64_t(c) * CP] = hv[c];
+              a1out[(geo.ni + b) * CP + ch] = a1;
+            }
+          }
+        }
+      }
+    }
+  }
+  cp_async_wait<0>();
+}
+
+// ----------------------------------------------------------------------------------
+// backward hidden layer: D_l = jet_vjp(H_l, a1_l, D_{l+1} W_l).  FIRST: contract
+// D_1 with the coordinate jets (dW_0[c][a] += D[row0][c]*x[a] + D[unit(a)][c],
+// db_0[c] += D[row0][c]) into per-CTA partials instead of storing D_1.
+template <int DIM, int CP, int BO, bool FIRST>
+__global__ void __launch_bounds__(kThreads, 2)
+    bwd_layer(const double* __restrict__ dnext, int kout, const double* __restrict__ w,
+              const double* __restrict__ hcur, const double* __restrict__ a1cur, double* __restrict__ dcur,
+              const double* __restrict__ x, double* __restrict__ coord_partial, Geometry geo) {
+  using T = MmaTile<DIM, CP>;
+  using TL = Tiles<DIM, BO, T::TC>;
+  constexpr int S = T::S, TR = T::TR, Q = TL::Q, QB = TL::QB, LDA = CP + 4;
+  extern __shared__ __align__(16) double smem[];
+  double* sB = smem;                       // seed chunks   [stage][TR][LDC]
+  double* sA = sB + kStages * TR * LDC;    // weight chunks [stage][KC][CP+4]
+  int64_t* rowmap = reinterpret_cast<int64_t*>(sA + kStages * KC * LDA);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int wc = warp % T::WC, wr = warp / T::WC;
+  const int nk = kout / KC;
+  const int64_t nint = TL::interior(geo.ni);
+  const int64_t ntiles = nint + TL::boundary(geo.nb);
+  double cacc[T::MT][2][DIM + 1];
+#pragma unroll
+  for (int i = 0; i < T::MT; ++i)
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+      for (int a = 0; a <= DIM; ++a) cacc[i][hh][a] = 0.0;
+
+  for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    __syncthreads();
+    for (int r = threadIdx.x; r < TR; r += kThreads) {
+      int tc, s;
+      tile_slot<S>(r, tc, s);
+      rowmap[r] = TL::row(geo, nint, tile, tc, s);
+    }
+    __syncthreads();
+    auto load = [&](int kc, int stage) {
+      double* dB = sB + stage * TR * LDC;
+      for (int i = threadIdx.x; i < TR * (KC / 2); i += kThreads) {
+        const int r = i / (KC / 2), p = i % (KC / 2);
+        const int64_t gr = rowmap[r];
+        cp_async16(dB + r * LDC + 2 * p, dnext + (gr >= 0 ? gr : 0) * kout + kc * KC + 2 * p, gr >= 0);
+      }
+      double* dA = sA + stage * KC * LDA;
+      for (int i = threadIdx.x; i < KC * (CP / 2); i += kThreads) {
+        const int r = i / (CP / 2), p = i % (CP / 2);
+        cp_async16(dA + r * LDA + 2 * p, w + int64_t(kc * KC + r) * CP + 2 * p, true);
+      }
+    };
+    double acc[T::MT][T::NT][4];
+#pragma unroll
+    for (int i = 0; i < T::MT; ++i)
+#pragma unroll
+      for (int j = 0; j < T::NT; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0;
+#pragma unroll
+    for (int s = 0; s < kStages - 1; ++s) {
+      if (s < nk) load(s, s);
+      cp_async_commit();
+    }
+    for (int kc = 0; kc < nk; ++kc) {
+      cp_async_wait<kStages - 2>();
+      __syncthreads();
+      if (kc + kStages - 1 < nk) load(kc + kStages - 1, (kc + kStages - 1) % kStages);
+      cp_async_commit();
+      const double* cB = sB + (kc % kStages) * TR * LDC + wr * (4 * S) * LDC;
+      const double* cA = sA + (kc % kStages) * KC * LDA + wc * T::WCH;
+#pragma unroll
+      for (int kk = 0; kk < KC; kk += 8) {
+        double a[T::MT][4];
+#pragma unroll
+        for (int i = 0; i < T::MT; ++i) {
+          a[i][0] = cA[(kk + t) * LDA + 16 * i + g];
+          a[i][1] = cA[(kk + t) * LDA + 16 * i + g + 8];
+          a[i][2] = cA[(kk + t + 4) * LDA + 16 * i + g];
+          a[i][3] = cA[(kk + t + 4) * LDA + 16 * i + g + 8];
+        }
+#pragma unroll
+        for (int j = 0; j < T::NT; ++j) {
+          const double b0 = cB[(8 * j + g) * LDC + kk + t];
+          const double b1 = cB[(8 * j + g) * LDC + kk + t + 4];
+#pragma unroll
+          for (int i = 0; i < T::MT; ++i) mma_m16n8k8(acc[i][j], a[i], b0, b1);
+        }
+      }
+    }
+    const int tc = wr * 4 + t;
+    const bool interior = tile < nint;
+#pragma unroll
+    for (int i = 0; i < T::MT; ++i) {
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int ch = wc * T::WCH + 16 * i + 8 * hh + g;
+        double dh[S];
+#pragma unroll
+        for (int s = 0; s < S; ++s) dh[s] = acc[i][s >> 1][2 * hh + (s & 1)];
+        if (interior) {
+          const int64_t p = tile * T::TC + tc;
+          if (p < geo.ni) {
+            double hv[Q], zb[Q];
+            const double* src = hcur + p * Q * CP + ch;
+#pragma unroll
+            for (int s = 0; s < Q; ++s) hv[s] = src[int64_t(s) * CP];
+            Jet<DIM, 3>::vjp(hv, a1cur[p * CP + ch], dh, zb);
+            if constexpr (FIRST) {
+              cacc[i][hh][DIM] += zb[0];
+#pragma unroll
+              for (int a = 0; a < DIM; ++a) cacc[i][hh][a] += zb[0] * x[p * DIM + a] + zb[unit_row<DIM>(a)];
+            } else {
+              double* dst = dcur + p * Q * CP + ch;
+#pragma unroll
+              for (int s = 0; s < Q; ++s) dst[int64_t(s) * CP] = zb[s];
+            }
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < TL::PS; ++k) {
+            const int64_t b = (tile - nint) * (int64_t(T::TC) * TL::PS) + int64_t(tc) * TL::PS + k;
+            if (b < geo.nb) {
+              double hv[QB], zb[QB];
+              const double* src = hcur + (geo.ni * Q + b * QB) * CP + ch;
+#pragma unroll
+              for (int c = 0; c < QB; ++c) hv[c] = src[int64_t(c) * CP];
+              Jet<DIM, BO ? 1 : 0>::vjp(hv, a1cur[(geo.ni + b) * CP + ch], dh + k * QB, zb);
+              if constexpr (FIRST) {
+                cacc[i][hh][DIM] += zb[0];
+#pragma unroll
+                for (int a = 0; a < DIM; ++a) {
+                  double v = zb[0] * x[(geo.ni + b) * DIM + a];
+                  if constexpr (BO) v += zb[unit_row<DIM>(a)];
+                  cacc[i][hh][a] += v;
+                }
+              } else {
+                double* dst = dcur + (geo.ni * Q + b * QB) * CP + ch;
+#pragma unroll
+                for (int c = 0; c < QB; ++c) dst[int64_t(c) * CP] = zb[c];
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+  cp_async_wait<0>();
+  if constexpr (FIRST) {
+    // fixed-order reduction: the 4 thread columns of a warp, then the warp row groups
+#pragma unroll
+    for (int i = 0; i < T::MT; ++i)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+        for (int a = 0; a <= DIM; ++a) {
+          double v = cacc[i][hh][a];
+          v += __shfl_xor_sync(0xffffffffu, v, 1);
+          v += __shfl_xor_sync(0xffffffffu, v, 2);
+          cacc[i][hh][a] = v;
+        }
+    __syncthreads();
+    double* red = smem;  // [WR][CP][DIM+1]
+    if (t == 0) {
+#pragma unroll
+      for (int i = 0; i < T::MT; ++i)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int ch = wc * T::WCH + 16 * i + 8 * hh + g;
+#pragma unroll
+          for (int a = 0; a <= DIM; ++a) red[(wr * CP + ch) * (DIM + 1) + a] = cacc[i][hh][a];
+        }
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < CP * (DIM + 1); idx += kThreads) {
+      double s = 0.0;
+      for (int r = 0; r < T::WR; ++r) s += red[r * CP * (DIM + 1) + idx];
+      coord_partial[int64_t(blockIdx.x) * CP * (DIM + 1) + idx] = s;
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------------
+// wgrad: partial[split][o][i] = sum_{rows in split} D[row][o] H[row][i];
+// bias partial[split][o] = sum over order-0 rows of D[row][o] (column block 0 only).
+template <int BM, int BN>
+__global__ void __launch_bounds__(kThreads, 2)
+    wgrad_kernel(const double* __restrict__ d, int kout, const double* __restrict__ h, int kin,
+                 Geometry geo, int q, int qb, int64_t rows_per_split, double* __restrict__ wpart,
+                 double* __restrict__ bpart) {
+  constexpr int MT = BM / 32, NT = BN / 32, LDA = BM + 4, LDB = BN + 4;
+  extern __shared__ __align__(16) double smem[];
+  double* sA = smem;                     // [stage][KC rows][BM+4]
+  double* sB = sA + kStages * KC * LDA;  // [stage][KC rows][BN+4]
+  const int split = blockIdx.x;
+  const int nbn = kin / BN;
+  const int bm = blockIdx.y / nbn, bn = blockIdx.y % nbn;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int wm = warp & 1, wn = warp >> 1;  // 2 x 4 warps
+  const int64_t r0 = int64_t(split) * rows_per_split;
+  const int64_t r1 = (r0 + rows_per_split < geo.rows) ? r0 + rows_per_split : geo.rows;
+  const int nk = r1 > r0 ? int((r1 - r0 + KC - 1) / KC) : 0;
+  const int64_t full_rows = geo.ni * q;
+  auto load = [&](int kc, int stage) {
+    double* dA = sA + stage * KC * LDA;
+    for (int i = threadIdx.x; i < KC * (BM / 2); i += kThreads) {
+      const int r = i / (BM / 2), p = i % (BM / 2);
+      const int64_t gr = r0 + int64_t(kc) * KC + r;
+      const bool ok = gr < r1;
+      cp_async16(dA + r * LDA + 2 * p, d + (ok ? gr : 0) * kout + bm * BM + 2 * p, ok);
+    }
+    double* dB = sB + stage * KC * LDB;
+    for (int i = threadIdx.x; i < KC * (BN / 2); i += kThreads) {
+      const int r = i / (BN / 2), p = i % (BN / 2);
+      const int64_t gr = r0 + int64_t(kc) * KC + r;
+      const bool ok = gr < r1;
+      cp_async16(dB + r * LDB + 2 * p, h + (ok ? gr : 0) * kin + bn * BN + 2 * p, ok);
+    }
+  };
+  double acc[MT][NT][4];
+#pragma unroll
+  for (int i = 0; i < MT; ++i)
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0;
+  double bacc = 0.0;
+#pragma unroll
+  for (int s = 0; s < kStages - 1; ++s) {
+    if (s < nk) load(s, s);
+    cp_async_commit();
+  }
+  for (int kc = 0; kc < nk; ++kc) {
+    cp_async_wait<kStages - 2>();
+    __syncthreads();
+    if (kc + kStages - 1 < nk) load(kc + kStages - 1, (kc + kStages - 1) % kStages);
+    cp_async_commit();
+    const double* cA = sA + (kc % kStages) * KC * LDA + wm * (16 * MT);
+    const double* cB = sB + (kc % kStages) * KC * LDB + wn * (8 * NT);
+    if (bn == 0 && threadIdx.x < BM) {
+      const double* col = sA + (kc % kStages) * KC * LDA + threadIdx.x;
+      for (int r = 0; r < KC; ++r) {
+        const int64_t gr = r0 + int64_t(kc) * KC + r;
+        if (gr >= r1) break;
+        const bool zero = gr < full_rows ? (gr % q == 0) : ((gr - full_rows) % qb == 0);
+        if (zero) bacc += col[r * LDA];
+      }
+    }
+#pragma unroll
+    for (int kk = 0; kk < KC; kk += 8) {
+      double a[MT][4];
+#pragma unroll
+      for (int i = 0; i < MT; ++i) {
+        a[i][0] = cA[(kk + t) * LDA + 16 * i + g];
+        a[i][1] = cA[(kk + t) * LDA + 16 * i + g + 8];
+        a[i][2] = cA[(kk + t + 4) * LDA + 16 * i + g];
+        a[i][3] = cA[(kk + t + 4) * LDA + 16 * i + g + 8];
+      }
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        const double b0 = cB[(kk + t) * LDB + 8 * j + g];
+        const double b1 = cB[(kk + t + 4) * LDB + 8 * j + g];
+#pragma unroll
+        for (int i = 0; i < MT; ++i) mma_m16n8k8(acc[i][j], a[i], b0, b1);
+      }
+    }
+  }
+  cp_async_wait<0>();
+  double* out = wpart + int64_t(split) * kout * kin;
+#pragma unroll
+  for (int i = 0; i < MT; ++i)
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const int o = bm * BM + wm * (16 * MT) + 16 * i + g;
+      const int c = bn * BN + wn * (8 * NT) + 8 * j + 2 * t;
+      out[int64_t(o) * kin + c] = acc[i][j][0];
+      out[int64_t(o) * kin + c + 1] = acc[i][j][1];
+      out[int64_t(o + 8) * kin + c] = acc[i][j][2];
+      out[int64_t(o + 8) * kin + c + 1] = acc[i][j][3];
+    }
+  if (bn == 0 && threadIdx.x < BM) bpart[int64_t(split) * kout + bm * BM + threadIdx.x] = bacc;
+}
+
+// ----------------------------------------------------------------------------------
+// output layer + residual seed + output-layer gradients + jet VJP into the last hidden layer
+template <int HEAD>
+struct HeadTraits;
+template <>
+struct HeadTraits<FLASHNS_B200_HEAD_UVP> { static constexpr int NF = 3; };
+template <>
+struct HeadTraits<FLASHNS_B200_HEAD_PSI> { static constexpr int NF = 2; };
+
+template <int DIM, int HEAD>
+__device__ __forceinline__ double interior_seed(const double* y, double w, double nu, double gamma, double* dy) {
+  if constexpr (HEAD == FLASHNS_B200_HEAD_UVP) {
+    return seed_uvp_2d(y, w, nu, gamma, dy);
+  } else if constexpr (DIM == 2) {
+    return seed_psi_2d(y, w, nu, gamma, dy);
+  } else {
+    return seed_psi_3d(y, w, nu, gamma, dy);
+  }
+}
+
+constexpr int kHeadRows = 80;
+
+template <int DIM, int CP, int BO, int HEAD, bool FIRST>
+__global__ void __launch_bounds__(kThreads)
+    head_layer(const double* __restrict__ hL, const double* __restrict__ a1L, const double* __restrict__ wL,
+               const double* __restrict__ bL, const double* __restrict__ pde_w, const double* __restrict__ bnd_w,
+               const double* __restrict__ target, double nu, double gamma, double bc, double* __restrict__ dL,
+               const double* __restrict__ x, double* __restrict__ coord_partial, double* __restrict__ head_partial,
+               Geometry geo) {
+  constexpr int NF = HeadTraits<HEAD>::NF;
+  constexpr int Q = Basis<DIM>::Q, QB = BO ? DIM + 1 : 1;
+  constexpr int NFT = (HEAD == FLASHNS_B200_HEAD_PSI && BO) ? 3 : NF;  // boundary target fields
+  constexpr int TPI = kHeadRows / Q, TPB = kHeadRows / QB;
+  constexpr int LD = CP + 2;
+  constexpr int PARTIAL = NF * CP + NF + 1;
+  static_assert(kThreads % CP == 0, "channel ownership must be fixed per thread");
+  extern __shared__ __align__(16) double smem[];
+  double* sH = smem;                   // [kHeadRows][LD]
+  double* sW = sH + kHeadRows * LD;    // [NF][CP]
+  double* sY = sW + NF * CP;           // [kHeadRows][NF]
+  double* sD = sY + kHeadRows * NF;    // [kHeadRows][NF]
+  double* sRed = sD + kHeadRows * NF;  // [kThreads] reduction scratch
+  for (int i = threadIdx.x; i < NF * CP; i += kThreads) sW[i] = wL[i];
+
+  const int64_t nint = (geo.ni + TPI - 1) / TPI;
+  const int64_t ntiles = nint + (geo.nb + TPB - 1) / TPB;
+  constexpr int WPT = (NF * CP + kThreads - 1) / kThreads;
+  double wacc[WPT];
+#pragma unroll
+  for (int k = 0; k < WPT; ++k) wacc[k] = 0.0;
+  double bacc = 0.0, lacc = 0.0;
+  double cacc[DIM + 1];
+#pragma unroll
+  for (int a = 0; a <= DIM; ++a) cacc[a] = 0.0;
+  const int my_c = threadIdx.x % CP;
+
+  for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    const bool interior = tile < nint;
+    int64_t p0, row0;
+    int npts, nrows;
+    if (interior) {
+      p0 = tile * TPI;
+      npts = int((geo.ni - p0) < TPI ? (geo.ni - p0) : TPI);
+      row0 = p0 * Q;
+      nrows = npts * Q;
+    } else {
+      p0 = (tile - nint) * TPB;
+      npts = int((geo.nb - p0) < TPB ? (geo.nb - p0) : TPB);
+      row0 = geo.ni * Q + p0 * QB;
+      nrows = npts * QB;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < nrows * (CP / 2); i += kThreads) {
+      const int r = i / (CP / 2), p = i % (CP / 2);
+      cp_async16(sH + r * LD + 2 * p, hL + (row0 + r) * CP + 2 * p, true);
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+    // outputs Y[r][o] = H[r].W[o] (+ bias on order-0 rows)
+    for (int i = threadIdx.x; i < nrows * NF; i += kThreads) {
+      const int r = i / NF, o = i % NF;
+      const double* hr = sH + r * LD;
+      const double* wo = sW + o * CP;
+      double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
+#pragma unroll 4
+      for (int c = 0; c < CP; c += 4) {
+        s0 += hr[c] * wo[c];
+        s1 += hr[c + 1] * wo[c + 1];
+        s2 += hr[c + 2] * wo[c + 2];
+        s3 += hr[c + 3] * wo[c + 3];
+      }
+      double y = (s0 + s1) + (s2 + s3);
+      const bool zero = interior ? (r % Q == 0) : (r % QB == 0);
+      if (zero) y += bL[o];
+      sY[r * NF + o] = y;
+    }
+    __syncthreads();
+    // residual seeds, one point per thread
+    if (interior) {
+      if (threadIdx.x < npts) {
+        const int pt = threadIdx.x;
+        double y[Q * NF], dy[Q * NF];
+#pragma unroll
+        for (int k = 0; k < Q * NF; ++k) y[k] = sY[pt * Q * NF + k];
+        lacc += interior_seed<DIM, HEAD>(y, pde_w[p0 + pt], nu, gamma, dy);
+#pragma unroll
+        for (int k = 0; k < Q * NF; ++k) sD[pt * Q * NF + k] = dy[k];
+      }
+    } else {
+      for (int pt = threadIdx.x; pt < npts; pt += kThreads) {
+        const int64_t b = p0 + pt;
+        const double* yr = sY + pt * QB * NF;
+        double* dr = sD + pt * QB * NF;
+#pragma unroll
+        for (int k = 0; k < QB * NF; ++k) dr[k] = 0.0;
+        double f[NFT];
+        if constexpr (BO == 0) {
+#pragma unroll
+          for (int o = 0; o < NF; ++o) f[o] = yr[o];
+        } else {
+          f[0] = yr[unit_row<DIM>(1) * NF + 0];   // u = psi_y
+          f[1] = -yr[unit_row<DIM>(0) * NF + 0];  // v = -psi_x
+          f[2] = yr[1];                           // p
+        }
+        double gsd[NFT];
+#pragma unroll
+        for (int o = 0; o < NFT; ++o) {
+          const double err = f[o] - target[b * NFT + o];
+          const double wgt = bnd_w[b * NFT + o];
+          lacc += bc * wgt * err * err;
+          gsd[o] = 2.0 * bc * wgt * err;
+        }
+        if constexpr (BO == 0) {
+#pragma unroll
+          for (int o = 0; o < NF; ++o) dr[o] = gsd[o];
+        } else {
+          dr[unit_row<DIM>(1) * NF + 0] = gsd[0];
+          dr[unit_row<DIM>(0) * NF + 0] = -gsd[1];
+          dr[1] = gsd[2];
+        }
+      }
+    }
+    __syncthreads();
+    // output-layer gradients: dW_L[o][c] += sum_r D[r][o] H[r][c]; db_L[o] over order-0 rows
+#pragma unroll
+    for (int k = 0; k < WPT; ++k) {
+      const int idx = threadIdx.x + k * kThreads;
+      if (idx < NF * CP) {
+        const int o = idx / CP, c = idx % CP;
+        double s = 0.0;
+        for (int r = 0; r < nrows; ++r) s += sD[r * NF + o] * sH[r * LD + c];
+        wacc[k] += s;
+      }
+    }
+    if (threadIdx.x < NF) {
+      const int step = interior ? Q : QB;
+      for (int r = 0; r < nrows; r += step) bacc += sD[r * NF + threadIdx.x];
+    }
+    // dgrad through W_L and the jet VJP of the last hidden layer
+    if (interior) {
+      for (int idx = threadIdx.x; idx < npts * CP; idx += kThreads) {
+        const int pt = idx / CP, c = idx % CP;
+        double hv[Q], dh[Q], zb[Q];
+#pragma unroll
+        for (int s = 0; s < Q; ++s) {
+          const int r = pt * Q + s;
+          double v = 0.0;
+#pragma unroll
+          for (int o = 0; o < NF; ++o) v += sD[r * NF + o] * sW[o * CP + c];
+          dh[s] = v;
+          hv[s] = sH[r * LD + c];
+        }
+        const int64_t p = p0 + pt;
+        Jet<DIM, 3>::vjp(hv, a1L[p * CP + c], dh, zb);
+        if constexpr (FIRST) {
+          cacc[DIM] += zb[0];
+#pragma unroll
+          for (int a = 0; a < DIM; ++a) cacc[a] += zb[0] * x[p * DIM + a] + zb[unit_row<DIM>(a)];
+        } else {
+          double* dst = dL + p * Q * CP + c;
+#pragma unroll
+          for (int s = 0; s < Q; ++s) dst[int64_t(s) * CP] = zb[s];
+        }
+      }
+    } else {
+      for (int idx = threadIdx.x; idx < npts * CP; idx += kThreads) {
+        const int pt = idx / CP, c = idx % CP;
+        double hv[QB], dh[QB], zb[QB];
+#pragma unroll
+        for (int s = 0; s < QB; ++s) {
+          const int r = pt * QB + s;
+          double v = 0.0;
+#pragma unroll
+          for (int o = 0; o < NF; ++o) v += sD[r * NF + o] * sW[o * CP + c];
+          dh[s] = v;
+          hv[s] = sH[r * LD + c];
+        }
+        const int64_t b = p0 + pt;
+        Jet<DIM, BO ? 1 : 0>::vjp(hv, a1L[(geo.ni + b) * CP + c], dh, zb);
+        if constexpr (FIRST) {
+          cacc[DIM] += zb[0];
+#pragma unroll
+          for (int a = 0; a < DIM; ++a) {
+            double v = zb[0] * x[(geo.ni + b) * DIM + a];
+            if constexpr (BO) v += zb[unit_row<DIM>(a)];
+            cacc[a] += v;
+          }
+        } else {
+          double* dst = dL + (geo.ni * Q + b * QB) * CP + c;
+#pragma unroll
+          for (int s = 0; s < QB; ++s) dst[int64_t(s) * CP] = zb[s];
+        }
+      }
+    }
+  }
+  // per-CTA partials, fixed-order reductions
+  double* out = head_partial + int64_t(blockIdx.x) * PARTIAL;
+#pragma unroll
+  for (int k = 0; k < WPT; ++k) {
+    const int idx = threadIdx.x + k * kThreads;
+    if (idx < NF * CP) out[idx] = wacc[k];
+  }
+  if (threadIdx.x < NF) out[NF * CP + threadIdx.x] = bacc;
+  __syncthreads();
+  sRed[threadIdx.x] = lacc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double s = 0.0;
+    for (int i = 0; i < kThreads; ++i) s += sRed[i];
+    out[NF * CP + NF] = s;
+  }
+  if constexpr (FIRST) {
+    for (int a = 0; a <= DIM; ++a) {
+      __syncthreads();
+      sRed[threadIdx.x] = cacc[a];
+      __syncthreads();
+      if (threadIdx.x < CP) {
+        double s = 0.0;
+        for (int r = threadIdx.x; r < kThreads; r += CP) s += sRed[r];
+        coord_partial[(int64_t(blockIdx.x) * CP + threadIdx.x) * (DIM + 1) + a] = s;
+      }
+    }
+  }
+  (void)my_c;
+}
+
+template <int DIM, int CP, int NF>
+constexpr size_t head_smem_bytes() {
+  return sizeof(double) * (size_t(kHeadRows) * (CP + 2) + NF * CP + 2 * kHeadRows * NF + kThreads);
+}
+
+// ----------------------------------------------------------------------------------
+// first layer: coordinates -> affine jet -> stable tanh jet
+template <int DIM, int BO>
+__global__ void __launch_bounds__(kThreads)
+    first_layer(const double* __restrict__ x, const double* __restrict__ w0, const double* __restrict__ b0,
+                double* __restrict__ h1, double* __restrict__ a1, int cp, Geometry geo) {
+  constexpr int Q = Basis<DIM>::Q, QB = BO ? DIM + 1 : 1;
+  const int64_t total = (geo.ni + geo.nb) * cp;
+  for (int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t p = idx / cp;
+    const int c = int(idx % cp);
+    const double* wr = w0 + int64_t(c) * DIM;
+    const double* xp = x + p * DIM;
+    double z0 = xp[0] * wr[0];
+#pragma unroll
+    for (int a = 1; a < DIM; ++a) z0 += xp[a] * wr[a];
+    z0 += b0[c];
+    if (p < geo.ni) {
+      double z[Q], h[Q], aa;
+#pragma unroll
+      for (int s = 0; s < Q; ++s) z[s] = 0.0;
+      z[0] = z0;
+#pragma unroll
+      for (int a = 0; a < DIM; ++a) z[unit_row<DIM>(a)] = wr[a];
+      Jet<DIM, 3>::fwd(z, h, aa);
+      double* dst = h1 + p * Q * cp + c;
+#pragma unroll
+      for (int s = 0; s < Q; ++s) dst[int64_t(s) * cp] = h[s];
+      a1[p * cp + c] = aa;
+    } else {
+      const int64_t b = p - geo.ni;
+      double z[QB], h[QB], aa;
+      z[0] = z0;
+      if constexpr (BO) {
+#pragma unroll
+        for (int a = 0; a < DIM; ++a) z[unit_row<DIM>(a)] = wr[a];
+      }
+      Jet<DIM, BO ? 1 : 0>::fwd(z, h, aa);
+      double* dst = h1 + (geo.ni * Q + b * QB) * cp + c;
+#pragma unroll
+      for (int s = 0; s < QB; ++s) dst[int64_t(s) * cp] = h[s];
+      a1[p * cp + c] = aa;
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------------
+// parameters: flat [W_0..W_L (row-major, true widths), b_0..b_L] <-> padded buffers
+struct LayerDesc {
+  int cout, cin;          // true widths
+  int coutp, cinp;        // padded widths of the stored buffers
+  int64_t w_flat, b_flat; // offsets in the flat parameter vector
+  int64_t w_buf, b_buf;   // offsets (doubles) of the padded buffers in the workspace
+  // gradient partials: element (k, o, i) at part[k*ws + o*wo + i]; bias (k, o) at bpart[k*bs + o*bo]
+  int64_t wpart, bpart, ws, wo, bs, bo;
+  int count;
+};
+struct LayerTable {
+  int n;
+  int64_t params;
+  int64_t loss_part, loss_stride;
+  int loss_count;
+  LayerDesc l[kMaxAffine];
+};
+
+__global__ void pack_params(const double* __restrict__ flat, double* __restrict__ ws, const __grid_constant__ LayerTable tab) {
+  int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (int k = 0; k < tab.n; ++k) {
+    const LayerDesc& L = tab.l[k];
+    const int64_t nw = int64_t(L.coutp) * L.cinp;
+    if (idx < nw) {
+      const int o = int(idx / L.cinp), i = int(idx % L.cinp);
+      ws[L.w_buf + idx] = (o < L.cout && i < L.cin) ? flat[L.w_flat + int64_t(o) * L.cin + i] : 0.0;
+      return;
+    }
+    idx -= nw;
+    if (idx < L.coutp) {
+      ws[L.b_buf + idx] = idx < L.cout ? flat[L.b_flat + idx] : 0.0;
+      return;
+    }
+    idx -= L.coutp;
+  }
+}
+
+__global__ void reduce_grads(const double* __restrict__ ws, double* __restrict__ out, const __grid_constant__ LayerTable tab) {
+  const int64_t f = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (f > tab.params) return;
+  if (f == tab.params) {
+    double s = 0.0;
+    for (int k = 0; k < tab.loss_count; ++k) s += ws[tab.loss_part + int64_t(k) * tab.loss_stride];
+    out[f] = s;
+    return;
+  }
+  for (int k = 0; k < tab.n; ++k) {
+    const LayerDesc& L = tab.l[k];
+    const int64_t nw = int64_t(L.cout) * L.cin;
+    if (f >= L.w_flat && f < L.w_flat + nw) {
+      const int64_t e = f - L.w_flat;
+      const int o = int(e / L.cin), i = int(e % L.cin);
+      double s = 0.0;
+      for (int c = 0; c < L.count; ++c) s += ws[L.wpart + c * L.ws + o * L.wo + i];
+      out[f] = s;
+      return;
+    }
+    if (f >= L.b_flat && f < L.b_flat + L.cout) {
+      const int o = int(f - L.b_flat);
+      double s = 0.0;
+      for (int c = 0; c < L.count; ++c) s += ws[L.bpart + c * L.bs + o * L.bo];
+      out[f] = s;
+      return;
+    }
+  }
+}
+
+}  // namespace flashns_b200
+
+// ======================================================================================
+// host side: plan + dispatch
+using namespace flashns_b200;
+
+struct flashns_b200_plan {
+  int dim, head, bo, n_aff, nf, nft;
+  int widths[kMaxAffine + 1];
+  int padded[kMaxAffine + 1];
+  int64_t ni, nb, rows, points;
+  double nu, gamma, bc;
+  int device, sms;
+  Geometry geo;
+  LayerTable tab;
+  // workspace offsets in doubles
+  int64_t off_h[kMaxAffine + 1], off_a1[kMaxAffine + 1], off_d[2], off_coord, off_head;
+  int64_t off_wg[kMaxAffine], off_bg[kMaxAffine];
+  int64_t workspace_doubles;
+  int grid_fwd[kMaxAffine], grid_bwd[kMaxAffine], grid_head, grid_first, grid_coord;
+  int wg_splits[kMaxAffine];
+  int64_t wg_rows[kMaxAffine];
+  int wg_bm[kMaxAffine], wg_bn[kMaxAffine];
+};
+
+namespace {
+
+int pad_width(int c) {
+  if (c <= 32) return 32;
+  if (c <= 64) return 64;
+  if (c <= 128) return 128;
+  return -1;
+}
+
+template <typename K>
+int occupancy(K kernel, size_t smem, int threads) {
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem) != cudaSuccess) return 1;
+  return std::max(n, 1);
+}
+
+template <typename K>
+cudaError_t allow_smem(K kernel, size_t smem) {
+  if (smem <= 48 * 1024) return cudaSuccess;
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+}
+
+// ---- dispatch tables: runtime (dim, width, boundary order, head) -> template instance
+template <int DIM, int CP, int BO>
+struct FwdOps {
+  static cudaError_t setup(int& occ) {
+    constexpr size_t smem = fwd_smem_bytes<DIM, CP>();
+    cudaError_t e = allow_smem(fwd_layer<DIM, CP, BO>, smem);
+    occ = occupancy(fwd_layer<DIM, CP, BO>, smem, kThreads);
+    return e;
+  }
+  static int64_t tiles(const Geometry& g) {
+    using T = MmaTile<DIM, CP>;
+    using TL = Tiles<DIM, BO, T::TC>;
+    return TL::interior(g.ni) + TL::boundary(g.nb);
+  }
+  static void launch(int grid, cudaStream_t st, const double* hin, int kin, const double* w, const double* b,
+                     double* hout, double* a1, Geometry g) {
+    fwd_layer<DIM, CP, BO><<<grid, kThreads, fwd_smem_bytes<DIM, CP>(), st>>>(hin, kin, w, b, hout, a1, g);
+  }
+};
+
+template <int DIM, int CP, int BO, bool FIRST>
+struct BwdOps {
+  static cudaError_t setup(int& occ) {
+    constexpr size_t smem = bwd_smem_bytes<DIM, CP>();
+    cudaError_t e = allow_smem(bwd_layer<DIM, CP, BO, FIRST>, smem);
+    occ = occupancy(bwd_layer<DIM, CP, BO, FIRST>, smem, kThreads);
+    return e;
+  }
+  static int64_t tiles(const Geometry& g) {
+    using T = MmaTile<DIM, CP>;
+    using TL = Tiles<DIM, BO, T::TC>;
+    return TL::interior(g.ni) + TL::boundary(g.nb);
+  }
+  static void launch(int grid, cudaStream_t st, const double* dn, int kout, const double* w, const double* h,
+                     const double* a1, double* dc, const double* x, double* cp, Geometry g) {
+    bwd_layer<DIM, CP, BO, FIRST><<<grid, kThreads, bwd_smem_bytes<DIM, CP>(), st>>>(dn, kout, w, h, a1, dc, x, cp, g);
+  }
+};
+
+template <int DIM, int CP, int BO, int HEAD, bool FIRST>
+struct HeadOps {
+  static constexpr int NF = HeadTraits<HEAD>::NF;
+  static cudaError_t setup(int& occ) {
+    constexpr size_t smem = head_smem_bytes<DIM, CP, NF>();
+    cudaError_t e = allow_smem(head_layer<DIM, CP, BO, HEAD, FIRST>, smem);
+    occ = occupancy(head_layer<DIM, CP, BO, HEAD, FIRST>, smem, kThreads);
+    return e;
+  }
+  static int64_t tiles(const Geometry& g) {
+    constexpr int Q = Basis<DIM>::Q, QB = BO ? DIM + 1 : 1;
+    constexpr int TPI = kHeadRows / Q, TPB = kHeadRows / QB;
+    return (g.ni + TPI - 1) / TPI + (g.nb + TPB - 1) / TPB;
+  }
+  static void launch(int grid, cudaStream_t st, const double* h, const double* a1, const double* w, const double* b,
+                     const double* pw, const double* bw, const double* tg, double nu, double gm, double bc, double* dl,
+                     const double* x, double* cpart, double* hpart, Geometry g) {
+    head_layer<DIM, CP, BO, HEAD, FIRST><<<grid, kThreads, head_smem_bytes<DIM, CP, NF>(), st>>>(
+        h, a1, w, b, pw, bw, tg, nu, gm, bc, dl, x, cpart, hpart, g);
+  }
+};
+
+// Generic visitor over the runtime parameters.
+template <template <int, int, int> class Ops, typename F>
+bool with_fwd(int dim, int cp, int bo, F&& f) {
+#define FLASHNS_CASE(D, C, B) \
+  if (dim == D && cp == C && bo == B) { f(Ops<D, C, B>{}); return true; }
+  FLASHNS_CASE(2, 32, 0) FLASHNS_CASE(2, 64, 0) FLASHNS_CASE(2, 128, 0)
+  FLASHNS_CASE(2, 32, 1) FLASHNS_CASE(2, 64, 1) FLASHNS_CASE(2, 128, 1)
+  FLASHNS_CASE(3, 32, 0) FLASHNS_CASE(3, 64, 0) FLASHNS_CASE(3, 128, 0)
+  FLASHNS_CASE(3, 32, 1) FLASHNS_CASE(3, 64, 1) FLASHNS_CASE(3, 128, 1)
+#undef FLASHNS_CASE
+  return false;
+}
+
+template <bool FIRST, typename F>
+bool with_bwd(int dim, int cp, int bo, F&& f) {
+#define FLASHNS_CASE(D, C, B) \
+  if (dim == D && cp == C && bo == B) { f(BwdOps<D, C, B, FIRST>{}); return true; }
+  FLASHNS_CASE(2, 32, 0) FLASHNS_CASE(2, 64, 0) FLASHNS_CASE(2, 128, 0)
+  FLASHNS_CASE(2, 32, 1) FLASHNS_CASE(2, 64, 1) FLASHNS_CASE(2, 128, 1)
+  FLASHNS_CASE(3, 32, 0) FLASHNS_CASE(3, 64, 0) FLASHNS_CASE(3, 128, 0)
+  FLASHNS_CASE(3, 32, 1) FLASHNS_CASE(3, 64, 1) FLASHNS_CASE(3, 128, 1)
+#undef FLASHNS_CASE
+  return false;
+}
+
+template <bool FIRST, typename F>
+bool with_head(int dim, int cp, int bo, int head, F&& f) {
+#define FLASHNS_CASE(D, C, B, H) \
+  if (dim == D && cp == C && bo == B && head == H) { f(HeadOps<D, C, B, H, FIRST>{}); return true; }
+  FLASHNS_CASE(2, 32, 0, 0) FLASHNS_CASE(2, 64, 0, 0) FLASHNS_CASE(2, 128, 0, 0)
+  FLASHNS_CASE(2, 32, 0, 1) FLASHNS_CASE(2, 64, 0, 1) FLASHNS_CASE(2, 128, 0, 1)
+  FLASHNS_CASE(2, 32, 1, 1) FLASHNS_CASE(2, 64, 1, 1) FLASHNS_CASE(2, 128, 1, 1)
+  FLASHNS_CASE(3, 32, 0, 1) FLASHNS_CASE(3, 64, 0, 1) FLASHNS_CASE(3, 128, 0, 1)
+  FLASHNS_CASE(3, 32, 1, 1) FLASHNS_CASE(3, 64, 1, 1) FLASHNS_CASE(3, 128, 1, 1)
+#undef FLASHNS_CASE
+  return false;
+}
+
+template <int BM, int BN>
+struct WgradOps {
+  static size_t smem() { return sizeof(double) * kStages * KC * ((BM + 4) + (BN + 4)); }
+  static cudaError_t setup() { return allow_smem(wgrad_kernel<BM, BN>, smem()); }
+  static void launch(dim3 grid, cudaStream_t st, const double* d, int kout, const double* h, int kin, Geometry g,
+                     int q, int qb, int64_t rps, double* wp, double* bp) {
+    wgrad_kernel<BM, BN><<<grid, kThreads, smem(), st>>>(d, kout, h, kin, g, q, qb, rps, wp, bp);
+  }
+};
+
+template <typename F>
+bool with_wgrad(int bm, int bn, F&& f) {
+  if (bm == 32 && bn == 32) { f(WgradOps<32, 32>{}); return true; }
+  if (bm == 32 && bn == 64) { f(WgradOps<32, 64>{}); return true; }
+  if (bm == 64 && bn == 32) { f(WgradOps<64, 32>{}); return true; }
+  if (bm == 64 && bn == 64) { f(WgradOps<64, 64>{}); return true; }
+  return false;
+}
+
+int first_launch(int dim, int bo, int grid, cudaStream_t st, const double* x, const double* w, const double* b,
+                 double* h, double* a1, int cp, Geometry g) {
+  if (dim == 2 && bo == 0) first_layer<2, 0><<<grid, kThreads, 0, st>>>(x, w, b, h, a1, cp, g);
+  else if (dim == 2) first_layer<2, 1><<<grid, kThreads, 0, st>>>(x, w, b, h, a1, cp, g);
+  else if (bo == 0) first_layer<3, 0><<<grid, kThreads, 0, st>>>(x, w, b, h, a1, cp, g);
+  else first_layer<3, 1><<<grid, kThreads, 0, st>>>(x, w, b, h, a1, cp, g);
+  return int(cudaGetLastError());
+}
+
+}  // namespace
+
+// ======================================================================================
+extern "C" {
+
+int flashns_b200_plan_create(int dim, int head, int boundary_order, int n_affine, const int* widths,
+                             int64_t interior_points, int64_t boundary_points, double viscosity,
+                             double gradient_weight, double boundary_weight, flashns_b200_plan** out) {
+  if (!out || !widths) return int(cudaErrorInvalidValue);
+  *out = nullptr;
+  if ((dim != 2 && dim != 3) || (head != FLASHNS_B200_HEAD_UVP && head != FLASHNS_B200_HEAD_PSI) ||
+      (boundary_order != 0 && boundary_order != 1) || n_affine < 2 || n_affine > kMaxAffine ||
+      interior_points < 0 || boundary_points < 0)
+    return int(cudaErrorInvalidValue);
+  const int nf = head == FLASHNS_B200_HEAD_UVP ? 3 : 2;
+  if (head == FLASHNS_B200_HEAD_UVP && (dim != 2 || boundary_order != 0)) return int(cudaErrorInvalidValue);
+  if (widths[0] != dim || widths[n_affine] != nf) return int(cudaErrorInvalidValue);
+  if (!(viscosity >= 0) || !(gradient_weight >= 0) || !(boundary_weight >= 0)) return int(cudaErrorInvalidValue);
+  flashns_b200_plan* p = new (std::nothrow) flashns_b200_plan();
+  if (!p) return int(cudaErrorMemoryAllocation);
+  std::memset(p, 0, sizeof(*p));
+  p->dim = dim; p->head = head; p->bo = boundary_order; p->n_aff = n_affine; p->nf = nf;
+  p->nft = (head == FLASHNS_B200_HEAD_PSI && boundary_order) ? 3 : nf;
+  p->nu = viscosity; p->gamma = gradient_weight; p->bc = boundary_weight;
+  for (int l = 0; l <= n_affine; ++l) p->widths[l] = widths[l];
+  p->padded[0] = dim;
+  p->padded[n_affine] = nf;
+  for (int l = 1; l < n_affine; ++l) {
+    p->padded[l] = widths[l] >= 1 ? pad_width(widths[l]) : -1;
+    if (p->padded[l] < 0) { delete p; return int(cudaErrorInvalidValue); }
+  }
+  const int q = dim == 2 ? 10 : 20, qb = boundary_order ? dim + 1 : 1;
+  if (interior_points > (INT64_C(1) << 40) || boundary_points > (INT64_C(1) << 40)) { delete p; return int(cudaErrorInvalidValue); }
+  p->ni = interior_points; p->nb = boundary_points;
+  p->rows = interior_points * q + boundary_points * qb;
+  p->points = interior_points + boundary_points;
+  p->geo = Geometry{p->ni, p->nb, p->rows};
+  if (cudaGetDevice(&p->device) != cudaSuccess ||
+      cudaDeviceGetAttribute(&p->sms, cudaDevAttrMultiProcessorCount, p->device) != cudaSuccess) {
+    delete p; return int(cudaErrorInvalidDevice);
+  }
+  const int nh = n_affine - 1;  // hidden layers
+  int maxc = 0;
+  for (int l = 1; l <= nh; ++l) maxc = std::max(maxc, p->padded[l]);
+  if (p->rows > INT64_MAX / 8 / std::max(maxc, 1) / (nh + 4)) { delete p; return int(cudaErrorInvalidValue); }
+
+  // ---- grids (persistent kernels: one wave of resident CTAs)
+  cudaError_t err = cudaSuccess;
+  for (int l = 1; l < nh; ++l) {  // forward layer l: H_l (width padded[l]) -> H_{l+1}
+    const int cp = p->padded[l + 1];
+    with_fwd<FwdOps>(dim, cp, boundary_order, [&](auto ops) {
+      int occ = 1;
+      cudaError_t e = ops.setup(occ);
+      if (e != cudaSuccess) err = e;
+      const int64_t t = ops.tiles(p->geo);
+      p->grid_fwd[l] = int(std::max<int64_t>(1, std::min<int64_t>(t, int64_t(occ) * p->sms)));
+    });
+  }
+  for (int l = 1; l < nh; ++l) {  // backward layer l: D_{l+1} -> D_l (width padded[l])
+    const int cp = p->padded[l];
+    auto f = [&](auto ops) {
+      int occ = 1;
+      cudaError_t e = ops.setup(occ);
+      if (e != cudaSuccess) err = e;
+      const int64_t t = ops.tiles(p->geo);
+      p->grid_bwd[l] = int(std::max<int64_t>(1, std::min<int64_t>(t, int64_t(occ) * p->sms)));
+    };
+    if (l == 1) with_bwd<true>(dim, cp, boundary_order, f);
+    else with_bwd<false>(dim, cp, boundary_order, f);
+  }
+  {
+    auto f = [&](auto ops) {
+      int occ = 1;
+      cudaError_t e = ops.setup(occ);
+      if (e != cudaSuccess) err = e;
+      const int64_t t = ops.tiles(p->geo);
+      p->grid_head = int(std::max<int64_t>(1, std::min<int64_t>(t, int64_t(occ) * p->sms)));
+    };
+    const bool ok = nh == 1 ? with_head<true>(dim, p->padded[nh], boundary_order, head, f)
+                            : with_head<false>(dim, p->padded[nh], boundary_order, head, f);
+    if (!ok) { delete p; return int(cudaErrorInvalidValue); }
+  }
+  if (err != cudaSuccess) { delete p; return int(err); }
+  p->grid_first = int(std::max<int64_t>(1, std::min<int64_t>((p->points * p->padded[1] + kThreads - 1) / kThreads,
+                                                             int64_t(p->sms) * 8)));
+  p->grid_coord = nh == 1 ? p->grid_head : p->grid_bwd[1];
+
+  // ---- workspace layout (doubles)
+  int64_t off = 0;
+  auto take = [&](int64_t n) { const int64_t o = off; off += (n + 31) / 32 * 32; return o; };
+  LayerTable& tab = p->tab;
+  tab.n = n_affine;
+  int64_t flat = 0;
+  for (int l = 0; l < n_affine; ++l) flat += int64_t(widths[l]) * widths[l + 1];
+  int64_t fb = flat;
+  for (int l = 0; l < n_affine; ++l) fb += widths[l + 1];
+  tab.params = fb;
+  int64_t fw = 0, fbias = flat;
+  for (int l = 0; l < n_affine; ++l) {
+    LayerDesc& L = tab.l[l];
+    L.cout = widths[l + 1]; L.cin = widths[l];
+    L.coutp = p->padded[l + 1]; L.cinp = p->padded[l];
+    L.w_flat = fw; L.b_flat = fbias;
+    fw += int64_t(L.cout) * L.cin; fbias += L.cout;
+    L.w_buf = take(int64_t(L.coutp) * L.cinp);
+    L.b_buf = take(L.coutp);
+  }
+  for (int l = 1; l <= nh; ++l) {
+    p->off_h[l] = take(p->rows * p->padded[l]);
+    p->off_a1[l] = take(p->points * p->padded[l]);
+  }
+  p->off_d[0] = take(p->rows * maxc);
+  p->off_d[1] = take(p->rows * maxc);
+  // layer 0 partials: [grid_coord][CP1][dim+1]
+  p->off_coord = take(int64_t(p->grid_coord) * p->padded[1] * (dim + 1));
+  {
+    LayerDesc& L = tab.l[0];
+    L.wpart = p->off_coord; L.ws = int64_t(p->padded[1]) * (dim + 1); L.wo = dim + 1;
+    L.bpart = p->off_coord + dim; L.bs = L.ws; L.bo = dim + 1;
+    L.count = p->grid_coord;
+  }
+  // hidden-layer wgrad partials
+  for (int l = 1; l < nh; ++l) {
+    const int kout = p->padded[l + 1], kin = p->padded[l];
+    const int bm = std::min(kout, 64), bn = std::min(kin, 64);
+    const int blocks = (kout / bm) * (kin / bn);
+    const int target = 2 * p->sms;
+    int64_t splits = std::max<int64_t>(1, target / blocks);
+    int64_t rps = (p->rows + splits - 1) / splits;
+    rps = std::max<int64_t>(KC, (rps + KC - 1) / KC * KC);
+    splits = std::max<int64_t>(1, (p->rows + rps - 1) / rps);
+    p->wg_splits[l] = int(splits); p->wg_rows[l] = rps; p->wg_bm[l] = bm; p->wg_bn[l] = bn;
+    p->off_wg[l] = take(splits * kout * kin);
+    p->off_bg[l] = take(splits * kout);
+    LayerDesc& L = tab.l[l];
+    L.wpart = p->off_wg[l]; L.ws = int64_t(kout) * kin; L.wo = kin;
+    L.bpart = p->off_bg[l]; L.bs = kout; L.bo = 1;
+    L.count = int(splits);
+    with_wgrad(bm, bn, [&](auto ops) {
+      cudaError_t e = ops.setup();
+      if (e != cudaSuccess) err = e;
+    });
+  }
+  // head partials: [grid_head][NF*CP + NF + 1]
+  {
+    const int cp = p->padded[nh];
+    const int64_t stride = int64_t(nf) * cp + nf + 1;
+    p->off_head = take(int64_t(p->grid_head) * stride);
+    LayerDesc& L = tab.l[nh];
+    L.wpart = p->off_head; L.ws = stride; L.wo = cp;
+    L.bpart = p->off_head + int64_t(nf) * cp; L.bs = stride; L.bo = 1;
+    L.count = p->grid_head;
+    tab.loss_part = p->off_head + int64_t(nf) * cp + nf;
+    tab.loss_stride = stride;
+    tab.loss_count = p->grid_head;
+  }
+  if (err != cudaSuccess) { delete p; return int(err); }
+  if (p->rows == 0) {  // nothing to evaluate: every partial count is zero, outputs are zeros
+    for (int l = 0; l < n_affine; ++l) tab.l[l].count = 0;
+    tab.loss_count = 0;
+  }
+  p->workspace_doubles = off;
+  *out = p;
+  return int(cudaSuccess);
+}
+
+int flashns_b200_plan_destroy(flashns_b200_plan* plan) {
+  delete plan;
+  return int(cudaSuccess);
+}
+
+int flashns_b200_plan_workspace_bytes(const flashns_b200_plan* plan, size_t* bytes) {
+  if (!plan || !bytes) return int(cudaErrorInvalidValue);
+  *bytes = size_t(plan->workspace_doubles) * sizeof(double);
+  return int(cudaSuccess);
+}
+
+int flashns_b200_plan_parameter_count(const flashns_b200_plan* plan, int64_t* count) {
+  if (!plan || !count) return int(cudaErrorInvalidValue);
+  *count = plan->tab.params;
+  return int(cudaSuccess);
+}
+
+int flashns_b200_plan_launch_count(const flashns_b200_plan* plan, int* count) {
+  if (!plan || !count) return int(cudaErrorInvalidValue);
+  const int nh = plan->n_aff - 1;
+  *count = plan->rows == 0 ? 2 : 1 /*pack*/ + 1 /*first*/ + (nh - 1) /*fwd*/ + 1 /*head*/ + (nh - 1) /*bwd*/ +
+                                 (nh - 1) /*wgrad*/ + 1 /*reduce*/;
+  return int(cudaSuccess);
+}
+
+int flashns_b200_eval(const flashns_b200_plan* p, const double* coordinates, const double* parameters,
+                      const double* pde_weights, const double* boundary_weights, const double* target,
+                      double* gradient_and_loss, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  if (!p || !parameters || !gradient_and_loss || !workspace) return int(cudaErrorInvalidValue);
+  if (workspace_bytes < size_t(p->workspace_doubles) * sizeof(double)) return int(cudaErrorInvalidValue);
+  if (p->points && !coordinates) return int(cudaErrorInvalidValue);
+  if (p->ni && !pde_weights) return int(cudaErrorInvalidValue);
+  if (p->nb && (!boundary_weights || !target)) return int(cudaErrorInvalidValue);
+  if ((reinterpret_cast<uintptr_t>(workspace) & 15) != 0) return int(cudaErrorInvalidValue);
+  double* ws = static_cast<double*>(workspace);
+  const LayerTable& tab = p->tab;
+  int64_t packed = 0;
+  for (int l = 0; l < p->n_aff; ++l) packed += int64_t(tab.l[l].coutp) * tab.l[l].cinp + tab.l[l].coutp;
+  pack_params<<<unsigned((packed + kThreads - 1) / kThreads), kThreads, 0, stream>>>(parameters, ws, tab);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return int(e);
+  const int nh = p->n_aff - 1;
+  const Geometry g = p->geo;
+  if (p->rows > 0) {
+    const LayerDesc& L0 = tab.l[0];
+    int r = first_launch(p->dim, p->bo, p->grid_first, stream, coordinates, ws + L0.w_buf, ws + L0.b_buf,
+                         ws + p->off_h[1], ws + p->off_a1[1], p->padded[1], g);
+    if (r) return r;
+    for (int l = 1; l < nh; ++l) {
+      const LayerDesc& L = tab.l[l];
+      with_fwd<FwdOps>(p->dim, p->padded[l + 1], p->bo, [&](auto ops) {
+        ops.launch(p->grid_fwd[l], stream, ws + p->off_h[l], p->padded[l], ws + L.w_buf, ws + L.b_buf,
+                   ws + p->off_h[l + 1], ws + p->off_a1[l + 1], g);
+      });
+      if ((e = cudaGetLastError()) != cudaSuccess) return int(e);
+    }
+    {
+      const LayerDesc& L = tab.l[nh];
+      auto f = [&](auto ops) {
+        ops.launch(p->grid_head, stream, ws + p->off_h[nh], ws + p->off_a1[nh], ws + L.w_buf, ws + L.b_buf,
+                   pde_weights, boundary_weights, target, p->nu, p->gamma, p->bc, ws + p->off_d[nh % 2],
+                   coordinates, ws + p->off_coord, ws + p->off_head, g);
+      };
+      if (nh == 1) with_head<true>(p->dim, p->padded[nh], p->bo, p->head, f);
+      else with_head<false>(p->dim, p->padded[nh], p->bo, p->head, f);
+      if ((e = cudaGetLastError()) != cudaSuccess) return int(e);
+    }
+    const int q = p->dim == 2 ? 10 : 20, qb = p->bo ? p->dim + 1 : 1;
+    for (int l = nh - 1; l >= 1; --l) {
+      const LayerDesc& L = tab.l[l];
+      const double* dn = ws + p->off_d[(l + 1) % 2];
+      auto f = [&](auto ops) {
+        ops.launch(p->grid_bwd[l], stream, dn, p->padded[l + 1], ws + L.w_buf, ws + p->off_h[l], ws + p->off_a1[l],
+                   ws + p->off_d[l % 2], coordinates, ws + p->off_coord, g);
+      };
+      if (l == 1) with_bwd<true>(p->dim, p->padded[l], p->bo, f);
+      else with_bwd<false>(p->dim, p->padded[l], p->bo, f);
+      if ((e = cudaGetLastError()) != cudaSuccess) return int(e);
+      const int kout = p->padded[l + 1], kin = p->padded[l];
+      const dim3 grid(unsigned(p->wg_splits[l]), unsigned((kout / p->wg_bm[l]) * (kin / p->wg_bn[l])));
+      with_wgrad(p->wg_bm[l], p->wg_bn[l], [&](auto ops) {
+        ops.launch(grid, stream, dn, kout, ws + p->off_h[l], kin, g, q, qb, p->wg_rows[l], ws + p->off_wg[l],
+                   ws + p->off_bg[l]);
+      });
+      if ((e = cudaGetLastError()) != cudaSuccess) return int(e);
+    }
+  }
+  reduce_grads<<<unsigned((tab.params + 1 + kThreads - 1) / kThreads), kThreads, 0, stream>>>(ws, gradient_and_loss, tab);
+  return int(cudaGetLastError());
+}
+
+}  // extern "C"

@@ -1,0 +1,68 @@
+/* C ABI of the FlashNS B200 (sm_100a) FP64 PINN loss + parameter-gradient library.
+ *
+ * Conventions (kept from the reference bindings, experiments/pinn_v8/native.py:53-68 and
+ * experiments/pinn_v8/native.cu:47-62,97-107):
+ *   - FP64, contiguous, device pointers on the current device; the caller allocates every
+ *     output and scratch buffer; no call allocates device memory.
+ *   - every call is asynchronous on `stream` and returns a cudaError_t value as int
+ *     (0 = success); argument errors return cudaErrorInvalidValue (1).
+ *   - sizes are int64_t; empty inputs succeed and write zeros where gradients are owned.
+ */
+#ifndef FLASHNS_B200_H
+#define FLASHNS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FLASHNS_B200_HEAD_UVP 0 /* outputs (u, v, p): src/flashns/ns_seed.py:26-87 objective */
+#define FLASHNS_B200_HEAD_PSI 1 /* outputs (psi, p): u = psi_y, v = -psi_x (no reference counterpart) */
+
+typedef struct flashns_b200_plan flashns_b200_plan;
+
+/* Plan of one packed evaluation.  Replaces the construction of
+ * PackedPINN(x, interior_count, ..., layout="compact", loss=NSLoss(...))
+ * (src/flashns/pinn_packed.py:16-88) for a fixed geometry.  Host-only; reads the
+ * current device's SM count; allocates no device memory.
+ *   dim             2 (x, y) or 3 (x, y, t)
+ *   head            FLASHNS_B200_HEAD_UVP (dim 2) or FLASHNS_B200_HEAD_PSI
+ *   boundary_order  0: boundary points carry value rows (reference layout,
+ *                   src/flashns/jet_packed.py:12-41); 1: first-order rows (psi head:
+ *                   boundary targets are (u, v, p))
+ *   widths          n_affine+1 entries: dim, hidden widths (1..128), outputs (3 uvp / 2 psi)
+ *   viscosity, gradient_weight, boundary_weight: NSLoss (src/flashns/ns_seed.py:13-23) */
+int flashns_b200_plan_create(int dim, int head, int boundary_order, int n_affine, const int* widths,
+                             int64_t interior_points, int64_t boundary_points, double viscosity,
+                             double gradient_weight, double boundary_weight, flashns_b200_plan** plan);
+int flashns_b200_plan_destroy(flashns_b200_plan* plan);
+/* bytes of caller-allocated device workspace (16-byte aligned) one evaluation needs */
+int flashns_b200_plan_workspace_bytes(const flashns_b200_plan* plan, size_t* bytes);
+/* P = sum over layers of (in*out + out) */
+int flashns_b200_plan_parameter_count(const flashns_b200_plan* plan, int64_t* count);
+/* number of kernels one flashns_b200_eval launches */
+int flashns_b200_plan_launch_count(const flashns_b200_plan* plan, int* count);
+
+/* One complete loss + parameter-gradient evaluation.  Replaces
+ * PackedPINN.__call__(weights, biases) -> (loss, [dW_0..dW_L, db_0..db_L])
+ * (src/flashns/pinn_packed.py:93-191) together with the Engine's flattening
+ * (experiments/pinn_v8/runtime.py:114-117).
+ *   coordinates       [interior + boundary, dim]   interior points first
+ *   parameters        [P]  flat [W_0 .. W_L (row-major [out, in]), b_0 .. b_L]
+ *   pde_weights       [interior]                   globally normalized
+ *   boundary_weights  [boundary, F], target [boundary, F]
+ *                     F = 3 for (uvp head) and (psi head, boundary_order 1): (u, v, p);
+ *                     F = 2 for (psi head, boundary_order 0): (psi, p)
+ *   gradient_and_loss [P + 1]  gradient in the flat order, then the loss
+ * Deterministic: fixed-order reductions, no floating-point atomics. */
+int flashns_b200_eval(const flashns_b200_plan* plan, const double* coordinates, const double* parameters,
+                      const double* pde_weights, const double* boundary_weights, const double* target,
+                      double* gradient_and_loss, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
