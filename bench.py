@@ -1,0 +1,360 @@
+"""Benchmark: FP64 loss + parameter-gradient evaluations per second on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg1] [--impl ours|reference]
+
+Workload: the Kovasznay stream-function net
+2->64x4->2 on 16,384 interior points with full third-order Q10 jets plus 4,096
+boundary points with first-order rows, FP64, seeded synthetic points and
+Xavier-normal weights (seed 0).  One step is one complete loss + gradient
+evaluation of a cfg1-sized point set per GPU.  With N GPUs (torchrun, one rank
+per GPU) the global point set is N x cfg1, each rank evaluates its shard and one
+NCCL all-reduce of the packed [gradient, loss] buffer completes the step (weak
+scaling); ``value`` counts cfg1-sized shard evaluations of all ranks per second.
+
+``--impl reference`` times the reference algorithm's CPU path (the oracle port of
+``PackedPINN``, all host threads) on the same workload; rank 0 alone prints.
+"""
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "FP64 loss+param-gradient evals/sec"
+UNIT = "evals/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--config", default="cfg1", choices=["cfg0", "cfg1", "cfg2", "cfg3"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="only W warm-up and K timed steps (for ncu launch lists); prints a short line")
+    return ap.parse_args()
+
+
+def workload(config):
+    from flashns_b200.problems import CONFIGS
+    c = CONFIGS[config]
+    net = "-".join(str(w) for w in c["widths"][:2]) + f"x{len(c['widths']) - 2}-{c['widths'][-1]}"
+    return {"workload": f"{config}: {c['kind']} {c['interior']}+{c['boundary']} points per GPU, psi head, "
+                        f"Q{10 if c['widths'][0] == 2 else 20} interior jets, first-order boundary rows",
+            "net": net, "interior_points_per_gpu": c["interior"], "boundary_points_per_gpu": c["boundary"],
+            "head": "psi", "boundary_order": 1}
+
+
+# ---------------------------------------------------------------------------- CPU side
+def cpu_port_rate(config, steps, warmup, workers):
+    """Oracle port of the reference CPU path on 1/8-point chunks over a process pool;
+    returns (evals/s of the full set, median s/step, sample description)."""
+    from flashns_b200.problems import CONFIGS, config_points
+    from flashns_b200.evaluator import xavier_normal
+    from oracle.cpu_baseline import timed_rate
+
+    c = CONFIGS[config]
+    pts = config_points(config)
+    ws, bs = xavier_normal(c["widths"], 0)
+    problem = dict(x=pts.x.numpy(), ni=pts.interior_count, pw=pts.pde_weights.numpy(),
+                   bw=pts.boundary_weights.numpy(), target=pts.target.numpy(), ws=[w.numpy() for w in ws],
+                   bs=[b.numpy() for b in bs],
+                   options=dict(head="psi", nu=pts.viscosity, gamma=0.2, bc=5.0, boundary_order=1))
+    parts = 8
+    rate, med = timed_rate(problem, workers, steps, warmup, parts=parts)
+    ni, nb = pts.interior_count, len(pts.x) - pts.interior_count
+    sample = (f"{steps} timed steps; each evaluates one of {parts} point chunks ({ni // parts}+{nb // parts} points) "
+              f"of the {config} set split over {workers} single-threaded NumPy processes; "
+              f"evals/s = (1/{parts}) / median step time")
+    return rate, med, sample
+
+
+# ---------------------------------------------------------------------------- clocks
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index, path):
+        self.path = path
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=open(path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            f = [v.strip() for v in line.split(",")]
+            if len(f) < 10:
+                continue
+            try:
+                rows.append(dict(sm=float(f[1]), max=float(f[2]), power=float(f[3]), util=float(f[4]),
+                                 hw=f[6], hwt=f[7], swt=f[8], swp=f[9]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        load = [r for r in rows if r["util"] >= 50] or rows
+        reasons = set()
+        for r in load:
+            for key, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"), ("swt", "sw_thermal_slowdown"),
+                              ("swp", "sw_power_cap")):
+                if r[key].lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r["sm"] for r in load), "sm_max_mhz": max(r["max"] for r in rows),
+                "power_w_max": max(r["power"] for r in rows), "samples_under_load": len(load),
+                "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------- GPU side
+def fp64_peak(device_stream, torch):
+    from flashns_b200 import _lib
+    lib = _lib.library()
+    sink = torch.zeros(1, dtype=torch.float64, device="cuda")
+    flops = ctypes.c_double()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    run = lambda it: _lib.check(lib.flashns_b200_fp64_peak_probe(4 * sms, it, ctypes.c_void_p(sink.data_ptr()),
+                                                                 ctypes.byref(flops),
+                                                                 ctypes.c_void_p(device_stream.cuda_stream)),
+                                "peak probe")
+    run(64)
+    best = 0.0
+    for _ in range(3):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(device_stream)
+        run(4096)
+        e1.record(device_stream)
+        e1.synchronize()
+        best = max(best, flops.value / (e0.elapsed_time(e1) * 1e-3) / 1e12)
+    return best
+
+
+def kernel_times(ev, params, out, steps, stream, torch):
+    """Per-kind average launch duration (ms) from events recorded between launches."""
+    from flashns_b200 import _lib
+    lib = ev.plan._lib
+    n = ctypes.c_int()
+    _lib.check(lib.flashns_b200_plan_launch_kinds(ev.plan.handle, None, 0, ctypes.byref(n)), "launch_kinds")
+    kinds = (ctypes.c_int * n.value)()
+    _lib.check(lib.flashns_b200_plan_launch_kinds(ev.plan.handle, kinds, n.value, ctypes.byref(n)), "launch_kinds")
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(n.value + 1)] for _ in range(steps)]
+    for row in events:  # torch creates the CUDA event at its first record
+        for e in row:
+            e.record(stream)
+    torch.cuda.synchronize()
+    ptr = lambda t: ctypes.c_void_p(t.data_ptr()) if t.numel() else None
+    for s in range(steps):
+        handles = (ctypes.c_void_p * (n.value + 1))(*[ctypes.c_void_p(e.cuda_event) for e in events[s]])
+        rec = ctypes.c_int()
+        _lib.check(lib.flashns_b200_eval_marked(ev.plan.handle, ptr(ev.x), ptr(params), ptr(ev.pde_weights),
+                                                ptr(ev.boundary_weights), ptr(ev.target), ptr(out),
+                                                ptr(ev.workspace), ev.workspace.numel() * 8,
+                                                ctypes.c_void_p(stream.cuda_stream), handles, n.value + 1,
+                                                ctypes.byref(rec)), "eval_marked")
+    torch.cuda.synchronize()
+    per = {}
+    for s in range(steps):
+        for i, k in enumerate(kinds):
+            name = _lib.KERNEL_KINDS[k]
+            per.setdefault(name, []).append(events[s][i].elapsed_time(events[s][i + 1]))
+    counts = {}
+    for k in kinds:
+        counts[_lib.KERNEL_KINDS[k]] = counts.get(_lib.KERNEL_KINDS[k], 0) + 1
+    return {k: {"launches_per_eval": counts[k], "avg_ms": statistics.mean(v), "total_ms_per_eval": sum(v) / steps}
+            for k, v in per.items()}
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    cfg = workload(args.config)
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        threads = os.cpu_count() or 1
+        rate, med, sample = cpu_port_rate(args.config, args.steps, args.warmup, threads)
+        line = {"metric": METRIC, "value": rate, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": med * 1e3, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic", "config": cfg,
+                "cpu_baseline": {"value": rate, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+                "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    from flashns_b200.costs import checkpoint_bytes, evaluation_costs
+    from flashns_b200.evaluator import PackedEvaluator, flat_parameters, xavier_normal
+    from flashns_b200.ns_seed import NSLoss
+    from flashns_b200.problems import CONFIGS, config_points
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    c = CONFIGS[args.config]
+    widths = c["widths"]
+    # weak scaling: the global set is `world` x the config; each rank owns one config-sized shard
+    pts = config_points(args.config, scale=world).shard(world, rank) if world > 1 else config_points(args.config)
+    loss = NSLoss(viscosity=pts.viscosity, gradient_weight=0.2, boundary_weight=5.0)
+    ev = PackedEvaluator(pts.x, pts.interior_count, pts.pde_weights, pts.boundary_weights, pts.target, widths,
+                         head="psi", boundary_order=1, loss=loss, device=device)
+    ws, bs = xavier_normal(widths, 0)
+    params_host = flat_parameters(ws, bs)
+    params = params_host.to(device)
+    out = torch.empty(ev.parameters + 1, dtype=torch.float64, device=device)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        ev(params, out)
+        if world > 1:
+            dist.all_reduce(out)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    if args.profile:
+        for _ in range(args.warmup):
+            step()
+        barrier()
+        for _ in range(args.steps):
+            step()
+        barrier()
+        if world > 1:
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps({"profile": True, "config": args.config, "launches_per_step": ev.launches_per_call,
+                              "warmup": args.warmup, "steps": args.steps}), flush=True)
+        return
+
+    sampler = ClockSampler(local, f"/tmp/flashns_clocks_{rank}.csv")
+    t_end = time.perf_counter() + 1.0  # settle clocks under load before timing
+    while time.perf_counter() < t_end:
+        for _ in range(20):
+            step()
+        torch.cuda.synchronize()
+    for _ in range(max(args.warmup, 3)):
+        step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    barrier()
+    elapsed = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(elapsed, op=dist.ReduceOp.MAX)
+    ms_step = float(elapsed) / args.steps
+    clocks = sampler.stop()
+
+    # end to end: host (pinned) inputs -> device, evaluation, all-reduce, result -> host, every step
+    hx = ev.x.cpu().pin_memory(); hpw = ev.pde_weights.cpu().pin_memory()
+    hbw = ev.boundary_weights.cpu().pin_memory(); htg = ev.target.cpu().pin_memory()
+    hp = params_host.pin_memory(); hout = torch.empty(ev.parameters + 1, dtype=torch.float64).pin_memory()
+    h2d = sum(t.numel() * 8 for t in (hx, hpw, hbw, htg, hp))
+    d2h = hout.numel() * 8
+
+    def e2e_step():
+        ev.x.copy_(hx, non_blocking=True)
+        ev.pde_weights.copy_(hpw, non_blocking=True)
+        ev.boundary_weights.copy_(hbw, non_blocking=True)
+        ev.target.copy_(htg, non_blocking=True)
+        params.copy_(hp, non_blocking=True)
+        step()
+        hout.copy_(out, non_blocking=True)
+        stream.synchronize()
+
+    e2e_steps = max(1, min(args.steps, 200))
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1) / e2e_steps], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+
+    # per-kernel roofline (events between launches, separate from the headline timing)
+    ktimes = kernel_times(ev, params, out, 20, stream, torch)
+    peak = fp64_peak(stream, torch)
+    costs = evaluation_costs(widths, ev.ni, ev.nb, head="psi", boundary_order=1)
+    dominant = max(ktimes, key=lambda k: ktimes[k]["total_ms_per_eval"])
+    dom_flops = statistics.mean(costs["per_kind"][dominant])
+    achieved = dom_flops / (ktimes[dominant]["avg_ms"] * 1e-3) / 1e12
+    traffic = None
+    tfile = ROOT / "profiles" / "traffic.json"
+    if tfile.exists():
+        try:
+            traffic = json.loads(tfile.read_text()).get(args.config, {}).get(dominant)
+        except (ValueError, AttributeError):
+            traffic = None
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        rate, med, sample = cpu_port_rate(args.config, 16, 2, threads)
+        cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
+    step_tflops = costs["total"] / (ms_step * 1e-3) / 1e12
+    line = {
+        "metric": METRIC, "value": world * 1e3 / ms_step, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic (seeded uniform Kovasznay points, analytic boundary targets, Xavier-normal weights seed 0)",
+        "config": dict(cfg, parallelism=f"dp{world}" if world > 1 else "single",
+                       l2="working set (checkpoints + seeds) %.2f GB > 126 MB L2; no flush needed"
+                          % (checkpoint_bytes(widths, ev.ni, ev.nb, boundary_order=1) / 1e9)),
+        "e2e": {"value": world * 1e3 / float(e2e_ms), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": ev.launches_per_call * args.steps,
+        "roofline": {"bound": "tensor", "kernel": dominant, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": traffic,
+                     "peak_source": "in-run FP64 DMMA m16n8k8 register-only probe (no FP64 entry in MEASURED_PEAKS.json)",
+                     "flops_per_launch": dom_flops},
+        "step_roofline": {"algorithmic_tflop_per_step": costs["total"] / 1e12, "achieved": step_tflops,
+                          "frac": step_tflops / peak},
+        "kernels": ktimes,
+        "clocks": clocks,
+    }
+    if cpu:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -20,7 +20,13 @@ SIGNATURES = {
     "flashns_b200_plan_parameter_count": [_c_ptr, ctypes.POINTER(_c_i64)],
     "flashns_b200_plan_launch_count": [_c_ptr, ctypes.POINTER(_c_int)],
     "flashns_b200_eval": [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_ptr],
+    "flashns_b200_eval_marked": [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_ptr,
+                                 _c_ptr, _c_int, ctypes.POINTER(_c_int)],
+    "flashns_b200_plan_launch_kinds": [_c_ptr, ctypes.POINTER(_c_int), _c_int, ctypes.POINTER(_c_int)],
+    "flashns_b200_fp64_peak_probe": [_c_int, _c_int, _c_ptr, ctypes.POINTER(_c_dbl), _c_ptr],
 }
+
+KERNEL_KINDS = {0: "pack", 1: "first", 2: "forward", 3: "head", 4: "backward", 5: "wgrad", 6: "reduce"}
 
 _library = None
 

@@ -1072,6 +1072,8 @@ int first_launch(int dim, int bo, int grid, cudaStream_t st, const double* x, co
 // ======================================================================================
 extern "C" {
 
+int flashns_b200_plan_launch_kinds(const flashns_b200_plan* p, int* kinds, int capacity, int* count);
+
 int flashns_b200_plan_create(int dim, int head, int boundary_order, int n_affine, const int* widths,
                              int64_t interior_points, int64_t boundary_points, double viscosity,
                              double gradient_weight, double boundary_weight, flashns_b200_plan** out) {
@@ -1251,26 +1253,29 @@ int flashns_b200_plan_parameter_count(const flashns_b200_plan* plan, int64_t* co
 }
 
 int flashns_b200_plan_launch_count(const flashns_b200_plan* plan, int* count) {
-  if (!plan || !count) return int(cudaErrorInvalidValue);
-  const int nh = plan->n_aff - 1;
-  *count = plan->rows == 0 ? 2 : 1 /*pack*/ + 1 /*first*/ + (nh - 1) /*fwd*/ + 1 /*head*/ + (nh - 1) /*bwd*/ +
-                                 (nh - 1) /*wgrad*/ + 1 /*reduce*/;
-  return int(cudaSuccess);
+  return flashns_b200_plan_launch_kinds(plan, nullptr, 0, count);
 }
 
-int flashns_b200_eval(const flashns_b200_plan* p, const double* coordinates, const double* parameters,
-                      const double* pde_weights, const double* boundary_weights, const double* target,
-                      double* gradient_and_loss, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+static int run_eval(const flashns_b200_plan* p, const double* coordinates, const double* parameters,
+                    const double* pde_weights, const double* boundary_weights, const double* target,
+                    double* gradient_and_loss, void* workspace, size_t workspace_bytes, cudaStream_t stream,
+                    cudaEvent_t* events, int capacity, int* recorded) {
   if (!p || !parameters || !gradient_and_loss || !workspace) return int(cudaErrorInvalidValue);
   if (workspace_bytes < size_t(p->workspace_doubles) * sizeof(double)) return int(cudaErrorInvalidValue);
   if (p->points && !coordinates) return int(cudaErrorInvalidValue);
   if (p->ni && !pde_weights) return int(cudaErrorInvalidValue);
   if (p->nb && (!boundary_weights || !target)) return int(cudaErrorInvalidValue);
   if ((reinterpret_cast<uintptr_t>(workspace) & 15) != 0) return int(cudaErrorInvalidValue);
+  int marks = 0;
+  auto mark = [&]() {
+    if (events && marks < capacity) cudaEventRecord(events[marks], stream);
+    ++marks;
+  };
   double* ws = static_cast<double*>(workspace);
   const LayerTable& tab = p->tab;
   int64_t packed = 0;
   for (int l = 0; l < p->n_aff; ++l) packed += int64_t(tab.l[l].coutp) * tab.l[l].cinp + tab.l[l].coutp;
+  mark();
   pack_params<<<unsigned((packed + kThreads - 1) / kThreads), kThreads, 0, stream>>>(parameters, ws, tab);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return int(e);
@@ -1278,11 +1283,13 @@ int flashns_b200_eval(const flashns_b200_plan* p, const double* coordinates, con
   const Geometry g = p->geo;
   if (p->rows > 0) {
     const LayerDesc& L0 = tab.l[0];
+    mark();
     int r = first_launch(p->dim, p->bo, p->grid_first, stream, coordinates, ws + L0.w_buf, ws + L0.b_buf,
                          ws + p->off_h[1], ws + p->off_a1[1], p->padded[1], g);
     if (r) return r;
     for (int l = 1; l < nh; ++l) {
       const LayerDesc& L = tab.l[l];
+      mark();
       with_fwd<FwdOps>(p->dim, p->padded[l + 1], p->bo, [&](auto ops) {
         ops.launch(p->grid_fwd[l], stream, ws + p->off_h[l], p->padded[l], ws + L.w_buf, ws + L.b_buf,
                    ws + p->off_h[l + 1], ws + p->off_a1[l + 1], g);
@@ -1296,6 +1303,7 @@ int flashns_b200_eval(const flashns_b200_plan* p, const double* coordinates, con
                    pde_weights, boundary_weights, target, p->nu, p->gamma, p->bc, ws + p->off_d[nh % 2],
                    coordinates, ws + p->off_coord, ws + p->off_head, g);
       };
+      mark();
       if (nh == 1) with_head<true>(p->dim, p->padded[nh], p->bo, p->head, f);
       else with_head<false>(p->dim, p->padded[nh], p->bo, p->head, f);
       if ((e = cudaGetLastError()) != cudaSuccess) return int(e);
@@ -1308,11 +1316,13 @@ int flashns_b200_eval(const flashns_b200_plan* p, const double* coordinates, con
         ops.launch(p->grid_bwd[l], stream, dn, p->padded[l + 1], ws + L.w_buf, ws + p->off_h[l], ws + p->off_a1[l],
                    ws + p->off_d[l % 2], coordinates, ws + p->off_coord, g);
       };
+      mark();
       if (l == 1) with_bwd<true>(p->dim, p->padded[l], p->bo, f);
       else with_bwd<false>(p->dim, p->padded[l], p->bo, f);
       if ((e = cudaGetLastError()) != cudaSuccess) return int(e);
       const int kout = p->padded[l + 1], kin = p->padded[l];
       const dim3 grid(unsigned(p->wg_splits[l]), unsigned((kout / p->wg_bm[l]) * (kin / p->wg_bn[l])));
+      mark();
       with_wgrad(p->wg_bm[l], p->wg_bn[l], [&](auto ops) {
         ops.launch(grid, stream, dn, kout, ws + p->off_h[l], kin, g, q, qb, p->wg_rows[l], ws + p->off_wg[l],
                    ws + p->off_bg[l]);
@@ -1320,8 +1330,48 @@ int flashns_b200_eval(const flashns_b200_plan* p, const double* coordinates, con
       if ((e = cudaGetLastError()) != cudaSuccess) return int(e);
     }
   }
+  mark();
   reduce_grads<<<unsigned((tab.params + 1 + kThreads - 1) / kThreads), kThreads, 0, stream>>>(ws, gradient_and_loss, tab);
-  return int(cudaGetLastError());
+  e = cudaGetLastError();
+  mark();
+  if (recorded) *recorded = marks;
+  return int(e);
+}
+
+int flashns_b200_eval(const flashns_b200_plan* p, const double* coordinates, const double* parameters,
+                      const double* pde_weights, const double* boundary_weights, const double* target,
+                      double* gradient_and_loss, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  return run_eval(p, coordinates, parameters, pde_weights, boundary_weights, target, gradient_and_loss, workspace,
+                  workspace_bytes, stream, nullptr, 0, nullptr);
+}
+
+int flashns_b200_eval_marked(const flashns_b200_plan* p, const double* coordinates, const double* parameters,
+                             const double* pde_weights, const double* boundary_weights, const double* target,
+                             double* gradient_and_loss, void* workspace, size_t workspace_bytes, cudaStream_t stream,
+                             cudaEvent_t* events, int capacity, int* recorded) {
+  if (!events || capacity < 1 || !recorded) return int(cudaErrorInvalidValue);
+  return run_eval(p, coordinates, parameters, pde_weights, boundary_weights, target, gradient_and_loss, workspace,
+                  workspace_bytes, stream, events, capacity, recorded);
+}
+
+int flashns_b200_plan_launch_kinds(const flashns_b200_plan* p, int* kinds, int capacity, int* count) {
+  if (!p || !count) return int(cudaErrorInvalidValue);
+  std::vector<int> k;
+  const int nh = p->n_aff - 1;
+  k.push_back(FLASHNS_B200_KERNEL_PACK);
+  if (p->rows > 0) {
+    k.push_back(FLASHNS_B200_KERNEL_FIRST);
+    for (int l = 1; l < nh; ++l) k.push_back(FLASHNS_B200_KERNEL_FORWARD);
+    k.push_back(FLASHNS_B200_KERNEL_HEAD);
+    for (int l = nh - 1; l >= 1; --l) {
+      k.push_back(FLASHNS_B200_KERNEL_BACKWARD);
+      k.push_back(FLASHNS_B200_KERNEL_WGRAD);
+    }
+  }
+  k.push_back(FLASHNS_B200_KERNEL_REDUCE);
+  *count = int(k.size());
+  if (kinds) for (int i = 0; i < int(k.size()) && i < capacity; ++i) kinds[i] = k[i];
+  return int(cudaSuccess);
 }
 
 }  // extern "C"

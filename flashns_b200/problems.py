@@ -1,0 +1,153 @@
+"""Seeded synthetic point sets of the benchmark configurations.
+
+Kovasznay flow (steady 2-D NS, Re = 20 unless given): on [-0.5, 1] x [-0.5, 1.5],
+``lambda = Re/2 - sqrt(Re^2/4 + 4 pi^2)``, ``nu = 1/Re`` and
+
+    u = 1 - e^{lambda x} cos 2 pi y,   v = lambda/(2 pi) e^{lambda x} sin 2 pi y,
+    p = (1 - e^{2 lambda x}) / 2,      psi = y - e^{lambda x} sin(2 pi y) / (2 pi)
+
+Taylor-Green vortex (unsteady 2-D NS): on (x, y, t) in [0, 2 pi]^2 x [0, 1] with
+``F = e^{-2 nu t}``: ``u = -cos x sin y F``, ``v = sin x cos y F``,
+``p = -(cos 2x + cos 2y) F^2 / 4``, ``psi = cos x cos y F``.
+
+Interior points are uniform; boundary points are uniform on the edges (Kovasznay:
+equal counts per edge) or, for Taylor-Green, half on the initial slice t = 0 and
+half on the four periodic faces.  The pressure gauge follows the reference solver
+(experiments/pinn_solver/problem.py:101-107): exact p is imposed on the x = 1
+outflow edge only for Kovasznay; for Taylor-Green on every boundary point.
+Weights are globally normalized: 1/Ni for the PDE, 1/Nb for boundary velocity,
+1/(points carrying the p target) for pressure.
+"""
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from flashns_b200.distributed_contract import shard_bounds
+
+
+@dataclass
+class PointSet:
+    x: torch.Tensor            # [ni + nb, dim], interior first
+    interior_count: int
+    pde_weights: torch.Tensor  # [ni]
+    boundary_weights: torch.Tensor  # [nb, F]
+    target: torch.Tensor       # [nb, F]
+    dim: int
+    viscosity: float
+    name: str
+
+    def shard(self, world, rank):
+        """Rank's contiguous share of interior and of boundary points (weights stay global)."""
+        ni = self.interior_count
+        nb = len(self.x) - ni
+        i0, i1 = shard_bounds(ni, world, rank)
+        b0, b1 = shard_bounds(nb, world, rank)
+        x = torch.cat((self.x[i0:i1], self.x[ni + b0:ni + b1]))
+        return PointSet(x, i1 - i0, self.pde_weights[i0:i1], self.boundary_weights[b0:b1], self.target[b0:b1],
+                        self.dim, self.viscosity, f"{self.name}[{rank}/{world}]")
+
+
+def kovasznay_lambda(re):
+    return re / 2 - math.sqrt(re * re / 4 + 4 * math.pi ** 2)
+
+
+def kovasznay_exact(x, re=20.0):
+    lam = kovasznay_lambda(re)
+    e = torch.exp(lam * x[:, 0])
+    a = 2 * math.pi * x[:, 1]
+    u = 1 - e * torch.cos(a)
+    v = lam / (2 * math.pi) * e * torch.sin(a)
+    p = 0.5 * (1 - e * e)
+    psi = x[:, 1] - e * torch.sin(a) / (2 * math.pi)
+    return u, v, p, psi
+
+
+def kovasznay(interior, boundary, *, re=20.0, seed=1, boundary_order=1):
+    gen = torch.Generator(device="cpu").manual_seed(seed)
+    lo = torch.tensor([-0.5, -0.5], dtype=torch.float64)
+    span = torch.tensor([1.5, 2.0], dtype=torch.float64)
+    xi = lo + span * torch.rand(interior, 2, generator=gen, dtype=torch.float64)
+    counts = [boundary // 4 + (1 if k < boundary % 4 else 0) for k in range(4)]
+    edges = []
+    for k, n in enumerate(counts):
+        s = torch.rand(n, generator=gen, dtype=torch.float64)
+        if k == 0:
+            e = torch.stack((-0.5 + 1.5 * s, torch.full_like(s, -0.5)), 1)
+        elif k == 1:
+            e = torch.stack((-0.5 + 1.5 * s, torch.full_like(s, 1.5)), 1)
+        elif k == 2:
+            e = torch.stack((torch.full_like(s, -0.5), -0.5 + 2.0 * s), 1)
+        else:
+            e = torch.stack((torch.full_like(s, 1.0), -0.5 + 2.0 * s), 1)
+        edges.append(e)
+    xb = torch.cat(edges)
+    u, v, p, psi = kovasznay_exact(xb, re)
+    outflow = torch.zeros(boundary, dtype=torch.bool)
+    outflow[boundary - counts[3]:] = True
+    wv = 1.0 / max(boundary, 1)
+    wp = torch.zeros(boundary, dtype=torch.float64)
+    wp[outflow] = 1.0 / max(counts[3], 1)
+    if boundary_order == 1:
+        target = torch.stack((u, v, p), 1)
+        weights = torch.stack((torch.full_like(u, wv), torch.full_like(u, wv), wp), 1)
+    else:
+        target = torch.stack((psi, p), 1)
+        weights = torch.stack((torch.full_like(u, wv), wp), 1)
+    pde = torch.full((interior,), 1.0 / max(interior, 1), dtype=torch.float64)
+    return PointSet(torch.cat((xi, xb)), interior, pde, weights, target, 2, 1.0 / re,
+                    f"kovasznay Re={re:g} {interior}+{boundary}")
+
+
+def taylor_green_exact(x, nu=0.01):
+    f = torch.exp(-2 * nu * x[:, 2])
+    u = -torch.cos(x[:, 0]) * torch.sin(x[:, 1]) * f
+    v = torch.sin(x[:, 0]) * torch.cos(x[:, 1]) * f
+    p = -0.25 * (torch.cos(2 * x[:, 0]) + torch.cos(2 * x[:, 1])) * f * f
+    psi = torch.cos(x[:, 0]) * torch.cos(x[:, 1]) * f
+    return u, v, p, psi
+
+
+def taylor_green(interior, boundary, *, nu=0.01, seed=1, boundary_order=1):
+    gen = torch.Generator(device="cpu").manual_seed(seed)
+    two_pi = 2 * math.pi
+    xi = torch.rand(interior, 3, generator=gen, dtype=torch.float64) * torch.tensor([two_pi, two_pi, 1.0],
+                                                                                   dtype=torch.float64)
+    n0 = boundary // 2
+    init = torch.rand(n0, 3, generator=gen, dtype=torch.float64) * torch.tensor([two_pi, two_pi, 0.0],
+                                                                               dtype=torch.float64)
+    side = torch.rand(boundary - n0, 3, generator=gen, dtype=torch.float64) * torch.tensor([two_pi, two_pi, 1.0],
+                                                                                          dtype=torch.float64)
+    face = torch.arange(boundary - n0) % 4
+    side[face == 0, 0] = 0.0
+    side[face == 1, 0] = two_pi
+    side[face == 2, 1] = 0.0
+    side[face == 3, 1] = two_pi
+    xb = torch.cat((init, side))
+    u, v, p, psi = taylor_green_exact(xb, nu)
+    w = 1.0 / max(boundary, 1)
+    if boundary_order == 1:
+        target = torch.stack((u, v, p), 1)
+        weights = torch.full((boundary, 3), w, dtype=torch.float64)
+    else:
+        target = torch.stack((psi, p), 1)
+        weights = torch.full((boundary, 2), w, dtype=torch.float64)
+    pde = torch.full((interior,), 1.0 / max(interior, 1), dtype=torch.float64)
+    return PointSet(torch.cat((xi, xb)), interior, pde, weights, target, 3, nu,
+                    f"taylor-green nu={nu:g} {interior}+{boundary}")
+
+
+# BASELINE configurations: (builder, interior, boundary, widths)
+CONFIGS = {
+    "cfg0": dict(kind="kovasznay", interior=2048, boundary=512, widths=[2, 64, 64, 64, 64, 2]),
+    "cfg1": dict(kind="kovasznay", interior=16384, boundary=4096, widths=[2, 64, 64, 64, 64, 2]),
+    "cfg2": dict(kind="kovasznay", interior=65536, boundary=16384, widths=[2] + [128] * 6 + [2]),
+    "cfg3": dict(kind="taylor_green", interior=262144, boundary=65536, widths=[3] + [128] * 5 + [2]),
+}
+
+
+def config_points(name, *, scale=1, seed=1, boundary_order=1):
+    c = CONFIGS[name]
+    build = kovasznay if c["kind"] == "kovasznay" else taylor_green
+    return build(c["interior"] * scale, c["boundary"] * scale, seed=seed, boundary_order=boundary_order)

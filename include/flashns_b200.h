@@ -46,6 +46,16 @@ int flashns_b200_plan_parameter_count(const flashns_b200_plan* plan, int64_t* co
 /* number of kernels one flashns_b200_eval launches */
 int flashns_b200_plan_launch_count(const flashns_b200_plan* plan, int* count);
 
+/* kernel kinds of one evaluation, in launch order (for per-kernel timing) */
+#define FLASHNS_B200_KERNEL_PACK 0     /* flat parameters -> padded layer buffers */
+#define FLASHNS_B200_KERNEL_FIRST 1    /* coordinates -> first affine -> tanh jet */
+#define FLASHNS_B200_KERNEL_FORWARD 2  /* DMMA GEMM + bias + tanh-jet epilogue */
+#define FLASHNS_B200_KERNEL_HEAD 3     /* output layer + residual seed + output gradients + jet VJP */
+#define FLASHNS_B200_KERNEL_BACKWARD 4 /* DMMA dgrad + jet-VJP epilogue (+ coordinate contraction) */
+#define FLASHNS_B200_KERNEL_WGRAD 5    /* DMMA weight gradient, split over rows */
+#define FLASHNS_B200_KERNEL_REDUCE 6   /* fixed-order partial reduction -> grad, loss */
+int flashns_b200_plan_launch_kinds(const flashns_b200_plan* plan, int* kinds, int capacity, int* count);
+
 /* One complete loss + parameter-gradient evaluation.  Replaces
  * PackedPINN.__call__(weights, biases) -> (loss, [dW_0..dW_L, db_0..db_L])
  * (src/flashns/pinn_packed.py:93-191) together with the Engine's flattening
@@ -61,6 +71,18 @@ int flashns_b200_plan_launch_count(const flashns_b200_plan* plan, int* count);
 int flashns_b200_eval(const flashns_b200_plan* plan, const double* coordinates, const double* parameters,
                       const double* pde_weights, const double* boundary_weights, const double* target,
                       double* gradient_and_loss, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* flashns_b200_eval that also records events[i] before the i-th launch and one after the
+ * last (count+1 events); *recorded = events written.  Used for per-kernel timing. */
+int flashns_b200_eval_marked(const flashns_b200_plan* plan, const double* coordinates, const double* parameters,
+                             const double* pde_weights, const double* boundary_weights, const double* target,
+                             double* gradient_and_loss, void* workspace, size_t workspace_bytes, cudaStream_t stream,
+                             cudaEvent_t* events, int capacity, int* recorded);
+
+/* FP64 tensor-core throughput probe: `blocks` CTAs of 256 threads run `iters` rounds of
+ * 8 independent DMMA m16n8k8 per warp from registers; *flops = floating-point operations
+ * issued.  Time it with events on `stream` for the FP64 roofline denominator. */
+int flashns_b200_fp64_peak_probe(int blocks, int iters, double* sink, double* flops, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,91 @@
+"""CPU: host-side contracts mirrored from the reference tests
+(tests/test_jet_spec.py, tests/test_distributed_contract.py, tests/test_pinn_v8.py:128-134)."""
+
+import math
+
+import numpy as np
+import pytest
+
+from flashns_b200.distributed_contract import global_normalization, parameter_count, shard_bounds
+from flashns_b200.jet_spec import JetSpec
+
+
+@pytest.mark.parametrize("dim,q", [(2, 10), (3, 20)])
+def test_full_jet_recovery_and_cotangent_duality(dim, q):
+    spec = JetSpec(dim)
+    assert spec.q == q and spec.coefficient_order[0] == (0,) * dim
+    coefficients = np.zeros(q)
+    cube = (3,) + (0,) * (dim - 1)
+    mixed = (1, 2) + (0,) * (dim - 2)
+    coefficients[spec.coefficient_order.index(cube)] = 1
+    coefficients[spec.coefficient_order.index(mixed)] = 2
+    derivatives = spec.recover_raw_derivatives(coefficients)
+    assert derivatives[spec.coefficient_order.index(cube)] == 6
+    assert derivatives[spec.coefficient_order.index(mixed)] == 4
+    raw_seed = np.arange(q) / 7
+    assert np.dot(raw_seed, derivatives) == pytest.approx(np.dot(spec.pullback_raw_derivative_seed(raw_seed), coefficients))
+    assert spec.truncated_q(1) == dim + 1 and spec.truncated_q(0) == 1
+
+
+@pytest.mark.parametrize("operation", ["hvp", "double_backward", "c13", "nonlocal_loss"])
+def test_unsupported_transforms_are_explicit(operation):
+    with pytest.raises(NotImplementedError, match=operation):
+        JetSpec(3).require_operation(operation)
+
+
+def test_basis_matches_device_unit_rows():
+    from flashns_b200 import codegen
+    for dim in (2, 3):
+        basis = JetSpec(dim).coefficient_order
+        assert basis == codegen.basis(dim)
+        for axis in range(dim):
+            unit = tuple(int(j == axis) for j in range(dim))
+            assert basis.index(unit) == dim - axis  # unit_row<DIM>(axis) in csrc/common.cuh
+
+
+@pytest.mark.parametrize("points,world", [(17, 1), (17, 2), (17, 4), (3, 4), (0, 4)])
+def test_shards_cover_global_ids_once_including_empty_ranks(points, world):
+    shards = [list(range(*shard_bounds(points, world, rank))) for rank in range(world)]
+    assert [i for shard in shards for i in shard] == list(range(points))
+    assert max(map(len, shards)) - min(map(len, shards)) <= 1
+
+
+@pytest.mark.parametrize("points,world", [(17, 4), (3, 4)])
+def test_weighted_local_sums_have_one_global_denominator(points, world):
+    weights = [0.5 + (i % 7) / 8 for i in range(points)]
+    derivative = [math.cos(i / 3) for i in range(points)]
+    z = global_normalization(weights)
+    expected = math.fsum(w * d for w, d in zip(weights, derivative)) / z
+    partials = [math.fsum(weights[i] * derivative[i] for i in range(*shard_bounds(points, world, r))) / z
+                for r in range(world)]
+    assert math.fsum(partials) == pytest.approx(expected, abs=1e-15)
+
+
+def test_model_gradient_payload_comes_from_parameters():
+    assert parameter_count([2, 64, 64, 3]) == 4547
+    assert parameter_count([2, 64, 64, 64, 64, 2]) == 12802
+    assert parameter_count([2] + [128] * 6 + [2]) == 83202
+    assert parameter_count([3] + [128] * 5 + [2]) == 66818
+
+
+@pytest.mark.parametrize("weights", [[0, 0], [1, -1], [float("nan")], [float("inf")]])
+def test_invalid_global_weights_rejected(weights):
+    with pytest.raises(ValueError):
+        global_normalization(weights)
+
+
+def test_problem_generators_and_shards():
+    from flashns_b200.problems import config_points, kovasznay, taylor_green
+    k = kovasznay(100, 40)
+    assert k.x.shape == (140, 2) and k.target.shape == (40, 3)
+    assert abs(float(k.pde_weights.sum()) - 1) < 1e-14
+    assert abs(float(k.boundary_weights[:, 0].sum()) - 1) < 1e-14
+    assert abs(float(k.boundary_weights[:, 2].sum()) - 1) < 1e-14
+    assert bool((k.x[:100, 0] >= -0.5).all() and (k.x[:100, 0] <= 1.0).all())
+    t = taylor_green(64, 32)
+    assert t.x.shape == (96, 3) and bool((t.x[64:64 + 16, 2] == 0).all())
+    g = config_points("cfg1", scale=4)
+    parts = [g.shard(4, r) for r in range(4)]
+    assert sum(p.interior_count for p in parts) == g.interior_count
+    assert sum(len(p.x) for p in parts) == len(g.x)
+    assert abs(sum(float(p.pde_weights.sum()) for p in parts) - 1) < 1e-12
