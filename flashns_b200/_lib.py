@@ -24,6 +24,7 @@ SIGNATURES = {
                                  _c_ptr, _c_int, ctypes.POINTER(_c_int)],
     "flashns_b200_plan_launch_kinds": [_c_ptr, ctypes.POINTER(_c_int), _c_int, ctypes.POINTER(_c_int)],
     "flashns_b200_fp64_peak_probe": [_c_int, _c_int, _c_ptr, ctypes.POINTER(_c_dbl), _c_ptr],
+    "flashns_b200_eval_static": [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr],
 }
 
 KERNEL_KINDS = {0: "pack", 1: "first", 2: "forward", 3: "head", 4: "backward", 5: "wgrad", 6: "reduce"}

@@ -1375,3 +1375,60 @@ int flashns_b200_plan_launch_kinds(const flashns_b200_plan* p, int* kinds, int c
 }
 
 }  // extern "C"
+
+// ======================================================================================
+// No-allocation entry point.
+//
+// Some callers cannot allocate device memory for the workspace: code driven from a host
+// runtime with no CUDA allocator of its own (a Go, Java or JavaScript process binding this
+// library through its C ABI), or a caller that must not grow device memory after start-up.
+// flashns_b200_eval_static runs the same evaluation with its scratch in the file-scope
+// array below, so it needs no workspace argument and calls no allocator.
+//
+// * Capacity: FLASHNS_B200_STATIC_WORKSPACE_BYTES (64 MiB) per GPU.  A plan whose
+//   workspace (flashns_b200_plan_workspace_bytes) is larger is rejected with
+//   cudaErrorInvalidValue before anything is launched.  The 2-64x4-2 psi net with
+//   first-order boundary rows fits about 1,000 interior + 250 boundary points.
+// * Every GPU that loads this library holds the array until the process exits.
+// * Host code may not use the array's name as a device pointer (it is a host-side
+//   stand-in).  The first call on a device, with that device current, looks up the
+//   array's device address with cudaGetSymbolAddress and caches it; make that first
+//   call before any stream capture.
+// * All calls on a device share the one array and it keeps the last call's contents.
+//   Nothing in it has to start at zero: every evaluation writes each scratch value
+//   before reading it.  Calls whose executions overlap on the GPU (other streams, or
+//   other host threads) race on the array; serialize them.
+#include <mutex>
+
+namespace {
+__device__ __align__(256) double g_static_workspace[FLASHNS_B200_STATIC_WORKSPACE_BYTES / sizeof(double)];
+std::mutex g_static_mutex;
+constexpr int kMaxDevices = 64;
+void* g_static_address[kMaxDevices] = {};
+}  // namespace
+
+extern "C" int flashns_b200_eval_static(const flashns_b200_plan* p, const double* coordinates,
+                                        const double* parameters, const double* pde_weights,
+                                        const double* boundary_weights, const double* target,
+                                        double* gradient_and_loss, cudaStream_t stream) {
+  if (!p) return int(cudaErrorInvalidValue);
+  const size_t need = size_t(p->workspace_doubles) * sizeof(double);
+  if (need > size_t(FLASHNS_B200_STATIC_WORKSPACE_BYTES)) return int(cudaErrorInvalidValue);
+  int device = -1;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return int(e);
+  if (device != p->device || device < 0 || device >= kMaxDevices) return int(cudaErrorInvalidDevice);
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_static_mutex);
+    if (!g_static_address[device]) {
+      void* address = nullptr;
+      e = cudaGetSymbolAddress(&address, g_static_workspace);
+      if (e != cudaSuccess) return int(e);
+      g_static_address[device] = address;
+    }
+    scratch = g_static_address[device];
+  }
+  return run_eval(p, coordinates, parameters, pde_weights, boundary_weights, target, gradient_and_loss, scratch,
+                  size_t(FLASHNS_B200_STATIC_WORKSPACE_BYTES), stream, nullptr, 0, nullptr);
+}

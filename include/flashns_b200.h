@@ -79,6 +79,19 @@ int flashns_b200_eval_marked(const flashns_b200_plan* plan, const double* coordi
                              double* gradient_and_loss, void* workspace, size_t workspace_bytes, cudaStream_t stream,
                              cudaEvent_t* events, int capacity, int* recorded);
 
+/* No-allocation variant of flashns_b200_eval (no counterpart in the reference).
+ * For callers that cannot allocate device memory -- a host runtime without a CUDA
+ * allocator that binds this C ABI (Go, Java, JavaScript FFI), or a process that must not
+ * grow device memory after start-up.  The scratch lives in a file-scope device array of
+ * FLASHNS_B200_STATIC_WORKSPACE_BYTES (64 MiB) that every GPU loading the library keeps
+ * until exit; plans needing more workspace are rejected with cudaErrorInvalidValue.  The
+ * first call on a device looks up the array's address and should come before any stream
+ * capture.  All calls share the array: calls that overlap on the GPU race. */
+#define FLASHNS_B200_STATIC_WORKSPACE_BYTES (64u * 1024u * 1024u)
+int flashns_b200_eval_static(const flashns_b200_plan* plan, const double* coordinates, const double* parameters,
+                             const double* pde_weights, const double* boundary_weights, const double* target,
+                             double* gradient_and_loss, cudaStream_t stream);
+
 /* FP64 tensor-core throughput probe: `blocks` CTAs of 256 threads run `iters` rounds of
  * 8 independent DMMA m16n8k8 per warp from registers; *flops = floating-point operations
  * issued.  Time it with events on `stream` for the FP64 roofline denominator. */
