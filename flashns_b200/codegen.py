@@ -49,30 +49,56 @@ def _lit(v):
 
 # --------------------------------------------------------------------------- jets
 
+def _sym_sum(terms, value):
+    """Sum of value(i, j) over ordered pairs, each unordered pair computed once."""
+    seen, parts = set(), []
+    for i, j in terms:
+        key = (min(i, j), max(i, j))
+        if key in seen:
+            continue
+        seen.add(key)
+        parts.append(value(i, j) if i == j else f"2.0 * ({value(i, j)})")
+    return " + ".join(parts)
+
+
+# Stable tanh and a1 from one exponential (all FP64 units are shared with the DMMA
+# main loop, so every instruction of the epilogue counts):
+#   r = exp(-|z0|), inv = 1/(1+r^2):  a1 = (2 r inv)^2 = sech^2 z0,  tanh|z0| = (1 - r^2) inv.
+# (1 - r^2) carries an absolute rounding error of a few ulp(1); below |z0| = 2^-10 the odd
+# Taylor series z (1 - z^2/3 + 2 z^4/15) (next term 17 z^7/315 < 1e-22 |z|) is used instead.
+_STABLE = """  const double z0 = z[0];
+  const double az = fabs(z0);
+  const double r = exp(-az);
+  const double r2 = r * r;
+  const double inv = 1.0 / (1.0 + r2);
+  const double v = 2.0 * r * inv;
+  a1 = v * v;
+  double ta = (1.0 - r2) * inv;
+  if (az < 0x1p-10) {
+    const double q = az * az;
+    ta = az * (1.0 - q * (1.0 / 3.0 - q * (2.0 / 15.0)));
+  }
+  const double t = copysign(ta, z0);"""
+
+
 def jet_forward(dim, order):
     b = basis(dim, order)
     q = len(b)
     name = f"jet_fwd_{dim}d{order}"
     L = [f"// tanh jet, dim {dim}, order {order}: {q} coefficients",
          f"__device__ __forceinline__ void {name}(const double* z, double* h, double& a1) {{",
-         "  const double z0 = z[0];",
-         "  const double t = tanh(z0);",
-         "  const double r = exp(-fabs(z0));",
-         "  const double v = (2.0 * r) / (1.0 + r * r);",
-         "  a1 = v * v;",
+         _STABLE,
          "  h[0] = t;"]
-    if order >= 1:
+    if order >= 2:
         L.append("  const double a2 = -(t * a1);")
     if order >= 3:
         L.append("  const double a3 = a1 * (t * t - (1.0 / 3.0));")
     if order >= 2:
         pr = pairs(dim, order)
-        # delta^2 at |gamma| in {2,3}: pairs with both factors nonzero
         for g, a in enumerate(b):
             if sum(a) >= 2:
                 terms = [(i, j) for i, j in pr[g] if i != 0 and j != 0]
-                expr = " + ".join(f"z[{i}] * z[{j}]" for i, j in terms)
-                L.append(f"  const double p2_{g} = {expr};")
+                L.append(f"  const double p2_{g} = {_sym_sum(terms, lambda i, j: f'z[{i}] * z[{j}]')};")
         for g, a in enumerate(b):
             if sum(a) == 3:
                 terms = [(i, j) for i, j in pr[g] if sum(b[i]) == 2 and sum(b[j]) == 1]
@@ -102,9 +128,7 @@ def jet_vjp(dim, order):
         return "\n".join(L)
     # g_gamma = -(H*H)_gamma for |gamma|>=1
     for g in range(1, q):
-        terms = pr[g]
-        expr = " + ".join(f"h[{i}] * h[{j}]" for i, j in terms)
-        L.append(f"  const double g{g} = -({expr});")
+        L.append(f"  const double g{g} = -({_sym_sum(pr[g], lambda i, j: f'h[{i}] * h[{j}]')});")
     L.append("  const double g0 = a1;")
     for beta in range(q):
         # zbar_beta = sum_{alpha >= beta} hb[alpha] * g[alpha - beta]

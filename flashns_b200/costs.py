@@ -34,6 +34,15 @@ def seed_flops(head, dim):
     return _ops(text)
 
 
+def padded_width(c):
+    return 32 if c <= 32 else 64 if c <= 64 else 128
+
+
+def fused_backward(widths, layer):
+    """Mirror of the plan: square 64-wide hidden layers run dgrad + VJP + wgrad in one kernel."""
+    return padded_width(widths[layer]) == 64 and padded_width(widths[layer + 1]) == 64
+
+
 def evaluation_costs(widths, ni, nb, *, head, boundary_order):
     """Dict kind -> list of per-launch FLOPs, in launch order, plus totals."""
     dim = widths[0]
@@ -57,8 +66,13 @@ def evaluation_costs(widths, ni, nb, *, head, boundary_order):
     for l in range(nh - 1, 0, -1):
         cin, cout = widths[l], widths[l + 1]
         extra = points * cin * (2 * dim + 1) if l == 1 else 0
-        out["backward"].append(2 * rows * cout * cin + ni * cin * v3 + nb * cin * vb + extra)
-        out["wgrad"].append(2 * rows * cout * cin + points * cout)
+        wgrad = 2 * rows * cout * cin
+        bwd = 2 * rows * cout * cin + ni * cin * v3 + nb * cin * vb + extra + points * cin
+        if fused_backward(widths, l):
+            out["backward"].append(bwd + wgrad)
+        else:
+            out["backward"].append(bwd)
+            out["wgrad"].append(wgrad)
     if nh == 1:
         out["head"][0] += points * c1 * (2 * dim + 1)
     total = sum(sum(v) for v in out.values())

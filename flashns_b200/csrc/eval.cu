@@ -30,8 +30,8 @@
 namespace flashns_b200 {
 
 constexpr int kThreads = 256;
-constexpr int kStages = 3;
-constexpr int KC = 16;       // k-chunk (doubles) per pipeline stage
+constexpr int kStages = 2;
+constexpr int KC = 32;       // k-chunk (doubles) per pipeline stage
 constexpr int LDC = KC + 4;  // padded chunk row: conflict-free FP64 fragment loads
 constexpr int kMaxAffine = 16;
 
@@ -65,17 +65,22 @@ FLASHNS_JET(3, 3, 20)
 // the rows 8j+2t and 8j+2t+1 of every n8 tile j.  Rows are permuted in shared memory
 // so that these S = Q rows are the Q jet coefficients of one point ("thread column").
 // The tanh-jet epilogue and its VJP then run entirely in registers.
-template <int DIM, int CP>
+// One m16 tile of channels per warp keeps 20 (2-D) or 40 (3-D) accumulators per thread,
+// so 16 warps fit a CTA and share one operand ring: latency is hidden by warps, not by
+// duplicated pipelines.
+template <int DIM, int CP, int WARPS = (CP >= 64 ? 16 : 8)>
 struct MmaTile {
   static constexpr int S = Basis<DIM>::Q;     // slots per thread column
   static constexpr int NT = S / 2;            // n8 tiles per warp
-  static constexpr int MT = DIM == 2 ? 2 : 1; // m16 tiles per warp
+  static constexpr int MT = 1;                // m16 tiles per warp
   static constexpr int WCH = 16 * MT;         // channels per warp
+  static constexpr int NWARPS = WARPS;
+  static constexpr int THREADS = 32 * WARPS;
   static constexpr int WC = CP / WCH;         // warps along channels
-  static constexpr int WR = 8 / WC;           // warp row groups
+  static constexpr int WR = WARPS / WC;       // warp row groups
   static constexpr int TC = 4 * WR;           // thread columns per tile
   static constexpr int TR = TC * S;           // packed rows per tile
-  static_assert(CP % WCH == 0 && WC >= 1 && 8 % WC == 0, "unsupported padded width");
+  static_assert(CP % WCH == 0 && WC >= 1 && WARPS % WC == 0, "unsupported padded width");
 };
 
 // Interior tiles carry TC points (Q rows each); boundary tiles carry TC*PS points of
@@ -108,22 +113,36 @@ __device__ __forceinline__ void tile_slot(int r, int& tc, int& s) {
 }
 
 template <int DIM, int CP>
-constexpr size_t fwd_smem_bytes() {
+constexpr size_t fwd_group_doubles() {
   using T = MmaTile<DIM, CP>;
-  return sizeof(double) * kStages * (T::TR + CP) * LDC + sizeof(int64_t) * T::TR;
+  return size_t(kStages) * (T::TR + CP) * LDC + 2 * T::TR;  // ring + rowmap[2][TR] (int64)
+}
+template <int DIM, int CP>
+constexpr size_t fwd_smem_bytes() {
+  return sizeof(double) * fwd_group_doubles<DIM, CP>();
+}
+template <int DIM, int CP>
+constexpr size_t bwd_group_doubles() {
+  using T = MmaTile<DIM, CP>;
+  return size_t(kStages) * (size_t(T::TR) * LDC + size_t(KC) * (CP + 4)) + 2 * T::TR;
 }
 template <int DIM, int CP>
 constexpr size_t bwd_smem_bytes() {
   using T = MmaTile<DIM, CP>;
-  constexpr size_t a = sizeof(double) * kStages * (size_t(T::TR) * LDC + size_t(KC) * (CP + 4)) + sizeof(int64_t) * T::TR;
+  constexpr size_t a = sizeof(double) * bwd_group_doubles<DIM, CP>();
   constexpr size_t red = sizeof(double) * T::WR * CP * (DIM + 1);
   return a > red ? a : red;
+}
+
+// number of tiles of this CTA (grid-stride over tiles)
+__device__ __forceinline__ int64_t cta_iterations(int64_t ntiles) {
+  return int64_t(blockIdx.x) < ntiles ? (ntiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
 }
 
 // ----------------------------------------------------------------------------------
 // forward hidden layer: H_{l+1} = tanh_jet(H_l W_l^T + b_l on order-0 rows)
 template <int DIM, int CP, int BO>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(MmaTile<DIM, CP>::THREADS, 1)
     fwd_layer(const double* __restrict__ hin, int kin, const double* __restrict__ w,
               const double* __restrict__ bias, double* __restrict__ hout, double* __restrict__ a1out,
               Geometry geo) {
@@ -131,36 +150,60 @@ __global__ void __launch_bounds__(kThreads, 2)
   using TL = Tiles<DIM, BO, T::TC>;
   constexpr int S = T::S, TR = T::TR, Q = TL::Q, QB = TL::QB;
   extern __shared__ __align__(16) double smem[];
-  double* sB = smem;                     // activation chunks [stage][TR][LDC]
-  double* sA = sB + kStages * TR * LDC;  // weight chunks     [stage][CP][LDC]
-  int64_t* rowmap = reinterpret_cast<int64_t*>(sA + kStages * CP * LDC);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int tid = threadIdx.x;
+  double* sB = smem;   // activation chunks [stage][TR][LDC]
+  double* sA = sB + kStages * TR * LDC;                      // weight chunks     [stage][CP][LDC]
+  int64_t* rowmap = reinterpret_cast<int64_t*>(sA + kStages * CP * LDC);  // [2][TR]
+  const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int wc = warp % T::WC, wr = warp / T::WC;
   const int nk = kin / KC;
   const int64_t nint = TL::interior(geo.ni);
   const int64_t ntiles = nint + TL::boundary(geo.nb);
-
-  for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-    __syncthreads();
-    for (int r = threadIdx.x; r < TR; r += kThreads) {
+  const int64_t iters = cta_iterations(ntiles);
+  auto tile_of = [&](int64_t k) { return k * gridDim.x + blockIdx.x; };
+  auto fill_rowmap = [&](int64_t tile, int64_t* rm) {
+    for (int r = tid; r < TR; r += T::THREADS) {
       int tc, s;
       tile_slot<S>(r, tc, s);
-      rowmap[r] = TL::row(geo, nint, tile, tc, s);
+      rm[r] = TL::row(geo, nint, tile, tc, s);
     }
+  };
+  auto load = [&](int kc, int stage, const int64_t* rm) {
+    double* dB = sB + stage * TR * LDC;
+    for (int i = tid; i < TR * (KC / 2); i += T::THREADS) {
+      const int r = i / (KC / 2), p = i % (KC / 2);
+      const int64_t gr = rm[r];
+      cp_async16(dB + r * LDC + 2 * p, hin + (gr >= 0 ? gr : 0) * kin + kc * KC + 2 * p, gr >= 0);
+    }
+    double* dA = sA + stage * CP * LDC;
+    for (int i = tid; i < CP * (KC / 2); i += T::THREADS) {
+      const int r = i / (KC / 2), p = i % (KC / 2);
+      cp_async16(dA + r * LDC + 2 * p, w + int64_t(r) * kin + kc * KC + 2 * p, true);
+    }
+  };
+  auto prologue = [&](const int64_t* rm) {
+#pragma unroll
+    for (int s = 0; s < kStages - 1; ++s) {
+      if (s < nk) load(s, s, rm);
+      cp_async_commit();
+    }
+  };
+  // a thread's channels are fixed for the whole kernel: load their biases once
+  double bias_r[T::MT][2];
+#pragma unroll
+  for (int i = 0; i < T::MT; ++i)
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) bias_r[i][hh] = bias[wc * T::WCH + 16 * i + 8 * hh + g];
+  int buf = 0;
+  if (iters > 0 && tile_of(0) < ntiles) {
+    fill_rowmap(tile_of(0), rowmap);
     __syncthreads();
-    auto load = [&](int kc, int stage) {
-      double* dB = sB + stage * TR * LDC;
-      for (int i = threadIdx.x; i < TR * (KC / 2); i += kThreads) {
-        const int r = i / (KC / 2), p = i % (KC / 2);
-        const int64_t gr = rowmap[r];
-        cp_async16(dB + r * LDC + 2 * p, hin + (gr >= 0 ? gr : 0) * kin + kc * KC + 2 * p, gr >= 0);
-      }
-      double* dA = sA + stage * CP * LDC;
-      for (int i = threadIdx.x; i < CP * (KC / 2); i += kThreads) {
-        const int r = i / (KC / 2), p = i % (KC / 2);
-        cp_async16(dA + r * LDC + 2 * p, w + int64_t(r) * kin + kc * KC + 2 * p, true);
-      }
-    };
+    prologue(rowmap);
+  }
+  for (int64_t k = 0; k < iters; ++k, buf ^= 1) {
+    const int64_t tile = tile_of(k);
+    const bool valid = tile < ntiles;
+    const int64_t* rm = rowmap + buf * TR;
     double acc[T::MT][T::NT][4];
 #pragma unroll
     for (int i = 0; i < T::MT; ++i)
@@ -168,37 +211,43 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int j = 0; j < T::NT; ++j)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0;
+    if (valid) {
+      for (int kc = 0; kc < nk; ++kc) {
+        cp_async_wait<kStages - 2>();
+        __syncthreads();
+        if (kc + kStages - 1 < nk) load(kc + kStages - 1, (kc + kStages - 1) % kStages, rm);
+        cp_async_commit();
+        const double* cB = sB + (kc % kStages) * TR * LDC + wr * (4 * S) * LDC;
+        const double* cA = sA + (kc % kStages) * CP * LDC + wc * T::WCH * LDC;
 #pragma unroll
-    for (int s = 0; s < kStages - 1; ++s) {
-      if (s < nk) load(s, s);
-      cp_async_commit();
-    }
-    for (int kc = 0; kc < nk; ++kc) {
-      cp_async_wait<kStages - 2>();
-      __syncthreads();
-      if (kc + kStages - 1 < nk) load(kc + kStages - 1, (kc + kStages - 1) % kStages);
-      cp_async_commit();
-      const double* cB = sB + (kc % kStages) * TR * LDC + wr * (4 * S) * LDC;
-      const double* cA = sA + (kc % kStages) * CP * LDC + wc * T::WCH * LDC;
+        for (int kk = 0; kk < KC; kk += 8) {
+          double a[T::MT][4];
 #pragma unroll
-      for (int kk = 0; kk < KC; kk += 8) {
-        double a[T::MT][4];
+          for (int i = 0; i < T::MT; ++i) {
+            a[i][0] = cA[(16 * i + g) * LDC + kk + t];
+            a[i][1] = cA[(16 * i + g + 8) * LDC + kk + t];
+            a[i][2] = cA[(16 * i + g) * LDC + kk + t + 4];
+            a[i][3] = cA[(16 * i + g + 8) * LDC + kk + t + 4];
+          }
 #pragma unroll
-        for (int i = 0; i < T::MT; ++i) {
-          a[i][0] = cA[(16 * i + g) * LDC + kk + t];
-          a[i][1] = cA[(16 * i + g + 8) * LDC + kk + t];
-          a[i][2] = cA[(16 * i + g) * LDC + kk + t + 4];
-          a[i][3] = cA[(16 * i + g + 8) * LDC + kk + t + 4];
-        }
+          for (int j = 0; j < T::NT; ++j) {
+            const double b0 = cB[(8 * j + g) * LDC + kk + t];
+            const double b1 = cB[(8 * j + g) * LDC + kk + t + 4];
 #pragma unroll
-        for (int j = 0; j < T::NT; ++j) {
-          const double b0 = cB[(8 * j + g) * LDC + kk + t];
-          const double b1 = cB[(8 * j + g) * LDC + kk + t + 4];
-#pragma unroll
-          for (int i = 0; i < T::MT; ++i) mma_m16n8k8(acc[i][j], a[i], b0, b1);
+            for (int i = 0; i < T::MT; ++i) mma_m16n8k8(acc[i][j], a[i], b0, b1);
+          }
         }
       }
     }
+    // the ring is free: start the next tile's first chunks, then run this tile's epilogue
+    __syncthreads();
+    if (k + 1 < iters && tile_of(k + 1) < ntiles) {
+      int64_t* rn = rowmap + (buf ^ 1) * TR;
+      fill_rowmap(tile_of(k + 1), rn);
+      __syncthreads();
+      prologue(rn);
+    }
+    if (!valid) continue;
     // epilogue: bias on the order-0 coefficient, stable tanh jet, store H and a1
     const int tc = wr * 4 + t;
     const bool interior = tile < nint;
@@ -210,7 +259,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         double z[S];
 #pragma unroll
         for (int s = 0; s < S; ++s) z[s] = acc[i][s >> 1][2 * hh + (s & 1)];
-        const double bch = bias[ch];
+        const double bch = bias_r[i][hh];
         if (interior) {
           const int64_t p = tile * T::TC + tc;
           if (p < geo.ni) {
@@ -224,12 +273,12 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
         } else {
 #pragma unroll
-          for (int k = 0; k < TL::PS; ++k) {
-            const int64_t b = (tile - nint) * (int64_t(T::TC) * TL::PS) + int64_t(tc) * TL::PS + k;
+          for (int kq = 0; kq < TL::PS; ++kq) {
+            const int64_t b = (tile - nint) * (int64_t(T::TC) * TL::PS) + int64_t(tc) * TL::PS + kq;
             if (b < geo.nb) {
               double zz[QB], hv[QB], a1;
 #pragma unroll
-              for (int c = 0; c < QB; ++c) zz[c] = z[k * QB + c];
+              for (int c = 0; c < QB; ++c) zz[c] = z[kq * QB + c];
               zz[0] += bch;
               Jet<DIM, BO ? 1 : 0>::fwd(zz, hv, a1);
               double* dst = hout + (geo.ni * Q + b * QB) * CP + ch;
@@ -246,55 +295,332 @@ __global__ void __launch_bounds__(kThreads, 2)
 }
 
 // ----------------------------------------------------------------------------------
-// backward hidden layer: D_l = jet_vjp(H_l, a1_l, D_{l+1} W_l).  FIRST: contract
+// backward hidden layer: D_l = jet_vjp(H_l, a1_l, D_{l+1} W_l), and the bias gradient of
+// layer l-1 (sum of D_l over order-0 rows) as per-CTA partials [grid][CP].  FIRST: contract
 // D_1 with the coordinate jets (dW_0[c][a] += D[row0][c]*x[a] + D[unit(a)][c],
-// db_0[c] += D[row0][c]) into per-CTA partials instead of storing D_1.
+// db_0[c] += D[row0][c]) into per-CTA partials [grid][CP][DIM+1] instead of storing D_1.
 template <int DIM, int CP, int BO, bool FIRST>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(MmaTile<DIM, CP>::THREADS, 1)
     bwd_layer(const double* __restrict__ dnext, int kout, const double* __restrict__ w,
               const double* __restrict__ hcur, const double* __restrict__ a1cur, double* __restrict__ dcur,
-              const double* __restrict__ x, double* __restrict__ coord_partial, Geometry geo) {
+              const double* __restrict__ x, double* __restrict__ partial, Geometry geo) {
   using T = MmaTile<DIM, CP>;
   using TL = Tiles<DIM, BO, T::TC>;
   constexpr int S = T::S, TR = T::TR, Q = TL::Q, QB = TL::QB, LDA = CP + 4;
+  constexpr int NV = FIRST ? DIM + 1 : 1;  // per-channel partial values
   extern __shared__ __align__(16) double smem[];
-  double* sB = smem;                       // seed chunks   [stage][TR][LDC]
-  double* sA = sB + kStages * TR * LDC;    // weight chunks [stage][KC][CP+4]
-  int64_t* rowmap = reinterpret_cast<int64_t*>(sA + kStages * KC * LDA);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int tid = threadIdx.x;
+  double* sB = smem;   // seed chunks   [stage][TR][LDC]
+  double* sA = sB + kStages * TR * LDC;                      // weight chunks [stage][KC][CP+4]
+  int64_t* rowmap = reinterpret_cast<int64_t*>(sA + kStages * KC * LDA);  // [2][TR]
+  const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int wc = warp % T::WC, wr = warp / T::WC;
   const int nk = kout / KC;
   const int64_t nint = TL::interior(geo.ni);
   const int64_t ntiles = nint + TL::boundary(geo.nb);
-  double cacc[T::MT][2][DIM + 1];
+  const int64_t iters = cta_iterations(ntiles);
+  double cacc[T::MT][2][NV];
 #pragma unroll
   for (int i = 0; i < T::MT; ++i)
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh)
 #pragma unroll
-      for (int a = 0; a <= DIM; ++a) cacc[i][hh][a] = 0.0;
-
-  for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-    __syncthreads();
-    for (int r = threadIdx.x; r < TR; r += kThreads) {
+      for (int a = 0; a < NV; ++a) cacc[i][hh][a] = 0.0;
+  auto tile_of = [&](int64_t k) { return k * gridDim.x + blockIdx.x; };
+  auto fill_rowmap = [&](int64_t tile, int64_t* rm) {
+    for (int r = tid; r < TR; r += T::THREADS) {
       int tc, s;
       tile_slot<S>(r, tc, s);
-      rowmap[r] = TL::row(geo, nint, tile, tc, s);
+      rm[r] = TL::row(geo, nint, tile, tc, s);
+    }
+  };
+  auto load = [&](int kc, int stage, const int64_t* rm) {
+    double* dB = sB + stage * TR * LDC;
+    for (int i = tid; i < TR * (KC / 2); i += T::THREADS) {
+      const int r = i / (KC / 2), p = i % (KC / 2);
+      const int64_t gr = rm[r];
+      cp_async16(dB + r * LDC + 2 * p, dnext + (gr >= 0 ? gr : 0) * kout + kc * KC + 2 * p, gr >= 0);
+    }
+    double* dA = sA + stage * KC * LDA;
+    for (int i = tid; i < KC * (CP / 2); i += T::THREADS) {
+      const int r = i / (CP / 2), p = i % (CP / 2);
+      cp_async16(dA + r * LDA + 2 * p, w + int64_t(kc * KC + r) * CP + 2 * p, true);
+    }
+  };
+  auto prologue = [&](const int64_t* rm) {
+#pragma unroll
+    for (int s = 0; s < kStages - 1; ++s) {
+      if (s < nk) load(s, s, rm);
+      cp_async_commit();
+    }
+  };
+  int buf = 0;
+  if (iters > 0 && tile_of(0) < ntiles) {
+    fill_rowmap(tile_of(0), rowmap);
+    __syncthreads();
+    prologue(rowmap);
+  }
+  for (int64_t k = 0; k < iters; ++k, buf ^= 1) {
+    const int64_t tile = tile_of(k);
+    const bool valid = tile < ntiles;
+    const int64_t* rm = rowmap + buf * TR;
+    double acc[T::MT][T::NT][4];
+#pragma unroll
+    for (int i = 0; i < T::MT; ++i)
+#pragma unroll
+      for (int j = 0; j < T::NT; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0;
+    if (valid && tid == 0) {
+      // the epilogue reads this tile's H rows and a1 rows (each a contiguous range):
+      // start bringing them into L2 while the main loop runs
+      int64_t row0, rows, pt0, pts;
+      if (tile < nint) {
+        pt0 = tile * T::TC;
+        pts = (geo.ni - pt0) < T::TC ? (geo.ni - pt0) : T::TC;
+        row0 = pt0 * Q;
+        rows = pts * Q;
+      } else {
+        const int64_t b0 = (tile - nint) * (int64_t(T::TC) * TL::PS);
+        pts = (geo.nb - b0) < int64_t(T::TC) * TL::PS ? (geo.nb - b0) : int64_t(T::TC) * TL::PS;
+        pt0 = geo.ni + b0;
+        row0 = geo.ni * Q + b0 * QB;
+        rows = pts * QB;
+      }
+      prefetch_l2(hcur + row0 * CP, uint32_t(rows * CP * sizeof(double)));
+      prefetch_l2(a1cur + pt0 * CP, uint32_t(pts * CP * sizeof(double)));
+    }
+    if (valid) {
+      for (int kc = 0; kc < nk; ++kc) {
+        cp_async_wait<kStages - 2>();
+        __syncthreads();
+        if (kc + kStages - 1 < nk) load(kc + kStages - 1, (kc + kStages - 1) % kStages, rm);
+        cp_async_commit();
+        const double* cB = sB + (kc % kStages) * TR * LDC + wr * (4 * S) * LDC;
+        const double* cA = sA + (kc % kStages) * KC * LDA + wc * T::WCH;
+#pragma unroll
+        for (int kk = 0; kk < KC; kk += 8) {
+          double a[T::MT][4];
+#pragma unroll
+          for (int i = 0; i < T::MT; ++i) {
+            a[i][0] = cA[(kk + t) * LDA + 16 * i + g];
+            a[i][1] = cA[(kk + t) * LDA + 16 * i + g + 8];
+            a[i][2] = cA[(kk + t + 4) * LDA + 16 * i + g];
+            a[i][3] = cA[(kk + t + 4) * LDA + 16 * i + g + 8];
+          }
+#pragma unroll
+          for (int j = 0; j < T::NT; ++j) {
+            const double b0 = cB[(8 * j + g) * LDC + kk + t];
+            const double b1 = cB[(8 * j + g) * LDC + kk + t + 4];
+#pragma unroll
+            for (int i = 0; i < T::MT; ++i) mma_m16n8k8(acc[i][j], a[i], b0, b1);
+          }
+        }
+      }
     }
     __syncthreads();
-    auto load = [&](int kc, int stage) {
-      double* dB = sB + stage * TR * LDC;
-      for (int i = threadIdx.x; i < TR * (KC / 2); i += kThreads) {
-        const int r = i / (KC / 2), p = i % (KC / 2);
-        const int64_t gr = rowmap[r];
-        cp_async16(dB + r * LDC + 2 * p, dnext + (gr >= 0 ? gr : 0) * kout + kc * KC + 2 * p, gr >= 0);
+    if (k + 1 < iters && tile_of(k + 1) < ntiles) {
+      int64_t* rn = rowmap + (buf ^ 1) * TR;
+      fill_rowmap(tile_of(k + 1), rn);
+      __syncthreads();
+      prologue(rn);
+    }
+    if (!valid) continue;
+    const int tc = wr * 4 + t;
+    const bool interior = tile < nint;
+#pragma unroll
+    for (int i = 0; i < T::MT; ++i) {
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int ch = wc * T::WCH + 16 * i + 8 * hh + g;
+        double dh[S];
+#pragma unroll
+        for (int s = 0; s < S; ++s) dh[s] = acc[i][s >> 1][2 * hh + (s & 1)];
+        if (interior) {
+          const int64_t p = tile * T::TC + tc;
+          if (p < geo.ni) {
+            double hv[Q], zb[Q];
+            const double* src = hcur + p * Q * CP + ch;
+#pragma unroll
+            for (int s = 0; s < Q; ++s) hv[s] = src[int64_t(s) * CP];
+            Jet<DIM, 3>::vjp(hv, a1cur[p * CP + ch], dh, zb);
+            if constexpr (FIRST) {
+              cacc[i][hh][DIM] += zb[0];
+#pragma unroll
+              for (int a = 0; a < DIM; ++a) cacc[i][hh][a] += zb[0] * x[p * DIM + a] + zb[unit_row<DIM>(a)];
+            } else {
+              double* dst = dcur + p * Q * CP + ch;
+#pragma unroll
+              for (int s = 0; s < Q; ++s) dst[int64_t(s) * CP] = zb[s];
+              cacc[i][hh][0] += zb[0];
+            }
+          }
+        } else {
+#pragma unroll
+          for (int kq = 0; kq < TL::PS; ++kq) {
+            const int64_t b = (tile - nint) * (int64_t(T::TC) * TL::PS) + int64_t(tc) * TL::PS + kq;
+            if (b < geo.nb) {
+              double hv[QB], zb[QB];
+              const double* src = hcur + (geo.ni * Q + b * QB) * CP + ch;
+#pragma unroll
+              for (int c = 0; c < QB; ++c) hv[c] = src[int64_t(c) * CP];
+              Jet<DIM, BO ? 1 : 0>::vjp(hv, a1cur[(geo.ni + b) * CP + ch], dh + kq * QB, zb);
+              if constexpr (FIRST) {
+                cacc[i][hh][DIM] += zb[0];
+#pragma unroll
+                for (int a = 0; a < DIM; ++a) {
+                  double v = zb[0] * x[(geo.ni + b) * DIM + a];
+                  if constexpr (BO) v += zb[unit_row<DIM>(a)];
+                  cacc[i][hh][a] += v;
+                }
+              } else {
+                double* dst = dcur + (geo.ni * Q + b * QB) * CP + ch;
+#pragma unroll
+                for (int c = 0; c < QB; ++c) dst[int64_t(c) * CP] = zb[c];
+                cacc[i][hh][0] += zb[0];
+              }
+            }
+          }
+        }
       }
-      double* dA = sA + stage * KC * LDA;
-      for (int i = threadIdx.x; i < KC * (CP / 2); i += kThreads) {
-        const int r = i / (CP / 2), p = i % (CP / 2);
-        cp_async16(dA + r * LDA + 2 * p, w + int64_t(kc * KC + r) * CP + 2 * p, true);
+    }
+  }
+  cp_async_wait<0>();
+  // fixed-order reduction: the 4 thread columns of a warp, then the warp row groups
+#pragma unroll
+  for (int i = 0; i < T::MT; ++i)
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+      for (int a = 0; a < NV; ++a) {
+        double v = cacc[i][hh][a];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        cacc[i][hh][a] = v;
       }
-    };
+  __syncthreads();
+  double* red = smem;  // [WR][CP][NV]
+  if (t == 0) {
+#pragma unroll
+    for (int i = 0; i < T::MT; ++i)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int ch = wc * T::WCH + 16 * i + 8 * hh + g;
+#pragma unroll
+        for (int a = 0; a < NV; ++a) red[(wr * CP + ch) * NV + a] = cacc[i][hh][a];
+      }
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < CP * NV; idx += T::THREADS) {
+    double s = 0.0;
+    for (int r = 0; r < T::WR; ++r) s += red[r * CP * NV + idx];
+    partial[int64_t(blockIdx.x) * CP * NV + idx] = s;
+  }
+}
+
+// ----------------------------------------------------------------------------------
+// Fused backward of a square 64-wide hidden layer: the dgrad + jet VJP of bwd_layer and
+// the weight gradient dW_l = D_{l+1}^T H_l of the same tile.  Each streamed seed chunk
+// (16 output channels x the tile's rows) is the A operand of both contractions; the
+// tile's H_l rows sit in shared memory (same row permutation) as the wgrad B operand.
+// dW_l accumulates in registers across the CTA's tiles and is written once per CTA, so
+// D_{l+1} and H_l are read from HBM once per layer instead of twice.
+constexpr int kFusedWidth = 64;
+// 16 warps in 2-D (160-row tiles); 8 warps in 3-D, where 16 would need 320-row tiles
+template <int DIM>
+struct FusedTile : MmaTile<DIM, kFusedWidth, DIM == 2 ? 16 : 8> {};
+
+template <int DIM>
+constexpr size_t fused_smem_bytes() {
+  using T = FusedTile<DIM>;
+  constexpr size_t ring = size_t(kStages) * (size_t(T::TR) * LDC + size_t(KC) * (kFusedWidth + 4));
+  constexpr size_t htile = size_t(T::TR) * (kFusedWidth + 4);
+  constexpr size_t a = sizeof(double) * (ring + htile + 2 * T::TR);
+  constexpr size_t red = sizeof(double) * (T::WR * kFusedWidth * (DIM + 1) + 8 * (kFusedWidth / 16) * 4 * 32);
+  return a > red ? a : red;
+}
+
+template <int DIM, int BO, bool FIRST>
+__global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
+    bwd_fused(const double* __restrict__ dnext, const double* __restrict__ w, const double* __restrict__ hcur,
+              const double* __restrict__ a1cur, double* __restrict__ dcur, const double* __restrict__ x,
+              double* __restrict__ partial, double* __restrict__ wpart, Geometry geo) {
+  constexpr int CP = kFusedWidth;
+  using T = FusedTile<DIM>;
+  using TL = Tiles<DIM, BO, T::TC>;
+  constexpr int S = T::S, TR = T::TR, Q = TL::Q, QB = TL::QB, LDA = CP + 4, LDH = CP + 4;
+  constexpr int NK = CP / KC;  // seed chunks per tile
+  constexpr int MK = KC / 16;  // m16 tiles of output channels per chunk
+  constexpr int NM = CP / 16;  // m16 tiles of output channels
+  constexpr int NV = FIRST ? DIM + 1 : 1;
+  // wgrad split: warp -> n8 tile (warp % 8) of dW columns and row share (warp / 8)
+  constexpr int RS = T::NWARPS / 8, RROWS = TR / RS;
+  static_assert(CP / 8 == 8 && T::NWARPS % 8 == 0 && RROWS % 16 == 0, "wgrad warp split");
+  extern __shared__ __align__(16) double smem[];
+  double* sB = smem;                     // seed chunks   [stage][TR][LDC]
+  double* sA = sB + kStages * TR * LDC;  // weight chunks [stage][KC][CP+4]
+  double* sH = sA + kStages * KC * LDA;  // H_l tile      [TR][CP+4]
+  int64_t* rowmap = reinterpret_cast<int64_t*>(sH + TR * LDH);  // [2][TR]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  const int wc = warp % T::WC, wr = warp / T::WC;
+  const int64_t nint = TL::interior(geo.ni);
+  const int64_t ntiles = nint + TL::boundary(geo.nb);
+  double cacc[T::MT][2][NV];
+#pragma unroll
+  for (int i = 0; i < T::MT; ++i)
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+      for (int a = 0; a < NV; ++a) cacc[i][hh][a] = 0.0;
+  const int wn = warp % 8, wrs = warp / 8;
+  double wacc[NM][4];  // dW rows 16m+{g,g+8}, columns 8*wn+{2t,2t+1}, rows of share wrs
+#pragma unroll
+  for (int m = 0; m < NM; ++m)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) wacc[m][e] = 0.0;
+
+  auto fill_rowmap = [&](int64_t tile, int64_t* rm) {
+    for (int r = tid; r < TR; r += T::THREADS) {
+      int tc, s;
+      tile_slot<S>(r, tc, s);
+      rm[r] = TL::row(geo, nint, tile, tc, s);
+    }
+  };
+  auto load = [&](int kc, int stage, const int64_t* rm) {
+    double* dB = sB + stage * TR * LDC;
+    for (int i = tid; i < TR * (KC / 2); i += T::THREADS) {
+      const int r = i / (KC / 2), p = i % (KC / 2);
+      const int64_t gr = rm[r];
+      cp_async16(dB + r * LDC + 2 * p, dnext + (gr >= 0 ? gr : 0) * CP + kc * KC + 2 * p, gr >= 0);
+    }
+    double* dA = sA + stage * KC * LDA;
+    for (int i = tid; i < KC * (CP / 2); i += T::THREADS) {
+      const int r = i / (CP / 2), p = i % (CP / 2);
+      cp_async16(dA + r * LDA + 2 * p, w + int64_t(kc * KC + r) * CP + 2 * p, true);
+    }
+  };
+  auto load_h = [&](const int64_t* rm) {
+    for (int i = tid; i < TR * (CP / 2); i += T::THREADS) {
+      const int r = i / (CP / 2), p = i % (CP / 2);
+      const int64_t gr = rm[r];
+      cp_async16(sH + r * LDH + 2 * p, hcur + (gr >= 0 ? gr : 0) * CP + 2 * p, gr >= 0);
+    }
+  };
+  auto prologue = [&](const int64_t* rm) {  // group 0: H tile + chunk 0; group 1: chunk 1
+    load_h(rm);
+    load(0, 0, rm);
+    cp_async_commit();
+    load(1, 1, rm);
+    cp_async_commit();
+  };
+  int buf = 0;
+  if (int64_t(blockIdx.x) < ntiles) {
+    fill_rowmap(blockIdx.x, rowmap);
+    __syncthreads();
+    prologue(rowmap);
+  }
+  for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, buf ^= 1) {
+    const int64_t* rm = rowmap + buf * TR;
     double acc[T::MT][T::NT][4];
 #pragma unroll
     for (int i = 0; i < T::MT; ++i)
@@ -303,17 +629,15 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0;
 #pragma unroll
-    for (int s = 0; s < kStages - 1; ++s) {
-      if (s < nk) load(s, s);
-      cp_async_commit();
-    }
-    for (int kc = 0; kc < nk; ++kc) {
+    for (int kc = 0; kc < NK; ++kc) {
       cp_async_wait<kStages - 2>();
       __syncthreads();
-      if (kc + kStages - 1 < nk) load(kc + kStages - 1, (kc + kStages - 1) % kStages);
+      if (kc + kStages - 1 < NK) load(kc + kStages - 1, (kc + kStages - 1) % kStages, rm);
       cp_async_commit();
-      const double* cB = sB + (kc % kStages) * TR * LDC + wr * (4 * S) * LDC;
+      const double* cD = sB + (kc % kStages) * TR * LDC;
+      const double* cB = cD + wr * (4 * S) * LDC;
       const double* cA = sA + (kc % kStages) * KC * LDA + wc * T::WCH;
+      // dgrad: dH[ch][rows] += W_l^T[ch][cout chunk] D^T[cout chunk][rows]
 #pragma unroll
       for (int kk = 0; kk < KC; kk += 8) {
         double a[T::MT][4];
@@ -332,6 +656,29 @@ __global__ void __launch_bounds__(kThreads, 2)
           for (int i = 0; i < T::MT; ++i) mma_m16n8k8(acc[i][j], a[i], b0, b1);
         }
       }
+      // wgrad: dW[cout chunk][8*wn..+8] += D^T[cout chunk][rows] H[rows][cin], rows of share wrs
+#pragma unroll 4
+      for (int r = wrs * RROWS; r < (wrs + 1) * RROWS; r += 8) {
+        const double b0 = sH[(r + t) * LDH + 8 * wn + g];
+        const double b1 = sH[(r + t + 4) * LDH + 8 * wn + g];
+#pragma unroll
+        for (int mm = 0; mm < MK; ++mm) {
+          double a[4];
+          a[0] = cD[(r + t) * LDC + 16 * mm + g];
+          a[1] = cD[(r + t) * LDC + 16 * mm + g + 8];
+          a[2] = cD[(r + t + 4) * LDC + 16 * mm + g];
+          a[3] = cD[(r + t + 4) * LDC + 16 * mm + g + 8];
+          mma_m16n8k8(wacc[kc * MK + mm], a, b0, b1);
+        }
+      }
+    }
+    // ring and H tile are free: start the next tile, then run this tile's epilogue
+    __syncthreads();
+    if (tile + gridDim.x < ntiles) {
+      int64_t* rn = rowmap + (buf ^ 1) * TR;
+      fill_rowmap(tile + gridDim.x, rn);
+      __syncthreads();
+      prologue(rn);
     }
     const int tc = wr * 4 + t;
     const bool interior = tile < nint;
@@ -359,18 +706,19 @@ __global__ void __launch_bounds__(kThreads, 2)
               double* dst = dcur + p * Q * CP + ch;
 #pragma unroll
               for (int s = 0; s < Q; ++s) dst[int64_t(s) * CP] = zb[s];
+              cacc[i][hh][0] += zb[0];
             }
           }
         } else {
 #pragma unroll
-          for (int k = 0; k < TL::PS; ++k) {
-            const int64_t b = (tile - nint) * (int64_t(T::TC) * TL::PS) + int64_t(tc) * TL::PS + k;
+          for (int kq = 0; kq < TL::PS; ++kq) {
+            const int64_t b = (tile - nint) * (int64_t(T::TC) * TL::PS) + int64_t(tc) * TL::PS + kq;
             if (b < geo.nb) {
               double hv[QB], zb[QB];
               const double* src = hcur + (geo.ni * Q + b * QB) * CP + ch;
 #pragma unroll
               for (int c = 0; c < QB; ++c) hv[c] = src[int64_t(c) * CP];
-              Jet<DIM, BO ? 1 : 0>::vjp(hv, a1cur[(geo.ni + b) * CP + ch], dh + k * QB, zb);
+              Jet<DIM, BO ? 1 : 0>::vjp(hv, a1cur[(geo.ni + b) * CP + ch], dh + kq * QB, zb);
               if constexpr (FIRST) {
                 cacc[i][hh][DIM] += zb[0];
 #pragma unroll
@@ -383,6 +731,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                 double* dst = dcur + (geo.ni * Q + b * QB) * CP + ch;
 #pragma unroll
                 for (int c = 0; c < QB; ++c) dst[int64_t(c) * CP] = zb[c];
+                cacc[i][hh][0] += zb[0];
               }
             }
           }
@@ -391,48 +740,68 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   }
   cp_async_wait<0>();
-  if constexpr (FIRST) {
-    // fixed-order reduction: the 4 thread columns of a warp, then the warp row groups
+  // weight-gradient partial of this CTA: row shares combined in fixed order through smem
+  __syncthreads();
+  double* wsh = smem + T::WR * CP * NV;  // [8 warps][NM][4][32 lanes]
+  if (RS == 2 && wrs == 1) {
+#pragma unroll
+    for (int m = 0; m < NM; ++m)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) wsh[((wn * NM + m) * 4 + e) * 32 + lane] = wacc[m][e];
+  }
+  __syncthreads();
+  if (wrs == 0) {
+    double* wp = wpart + int64_t(blockIdx.x) * CP * CP;
+#pragma unroll
+    for (int m = 0; m < NM; ++m) {
+      double v[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[e] = wacc[m][e] + (RS == 2 ? wsh[((wn * NM + m) * 4 + e) * 32 + lane] : 0.0);
+      const int o = 16 * m + g, c = 8 * wn + 2 * t;
+      wp[o * CP + c] = v[0];
+      wp[o * CP + c + 1] = v[1];
+      wp[(o + 8) * CP + c] = v[2];
+      wp[(o + 8) * CP + c + 1] = v[3];
+    }
+  }
+  // bias / coordinate partials: fixed-order reduction as in bwd_layer
+#pragma unroll
+  for (int i = 0; i < T::MT; ++i)
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+      for (int a = 0; a < NV; ++a) {
+        double v = cacc[i][hh][a];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        cacc[i][hh][a] = v;
+      }
+  __syncthreads();
+  double* red = smem;  // [WR][CP][NV]
+  if (t == 0) {
 #pragma unroll
     for (int i = 0; i < T::MT; ++i)
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh)
+      for (int hh = 0; hh < 2; ++hh) {
+        const int ch = wc * T::WCH + 16 * i + 8 * hh + g;
 #pragma unroll
-        for (int a = 0; a <= DIM; ++a) {
-          double v = cacc[i][hh][a];
-          v += __shfl_xor_sync(0xffffffffu, v, 1);
-          v += __shfl_xor_sync(0xffffffffu, v, 2);
-          cacc[i][hh][a] = v;
-        }
-    __syncthreads();
-    double* red = smem;  // [WR][CP][DIM+1]
-    if (t == 0) {
-#pragma unroll
-      for (int i = 0; i < T::MT; ++i)
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const int ch = wc * T::WCH + 16 * i + 8 * hh + g;
-#pragma unroll
-          for (int a = 0; a <= DIM; ++a) red[(wr * CP + ch) * (DIM + 1) + a] = cacc[i][hh][a];
-        }
-    }
-    __syncthreads();
-    for (int idx = threadIdx.x; idx < CP * (DIM + 1); idx += kThreads) {
-      double s = 0.0;
-      for (int r = 0; r < T::WR; ++r) s += red[r * CP * (DIM + 1) + idx];
-      coord_partial[int64_t(blockIdx.x) * CP * (DIM + 1) + idx] = s;
-    }
+        for (int a = 0; a < NV; ++a) red[(wr * CP + ch) * NV + a] = cacc[i][hh][a];
+      }
+  }
+  __syncthreads();
+  for (int idx = tid; idx < CP * NV; idx += T::THREADS) {
+    double s = 0.0;
+    for (int r = 0; r < T::WR; ++r) s += red[r * CP * NV + idx];
+    partial[int64_t(blockIdx.x) * CP * NV + idx] = s;
   }
 }
 
 // ----------------------------------------------------------------------------------
-// wgrad: partial[split][o][i] = sum_{rows in split} D[row][o] H[row][i];
-// bias partial[split][o] = sum over order-0 rows of D[row][o] (column block 0 only).
+// wgrad: partial[split][o][i] = sum_{rows in split} D[row][o] H[row][i]
 template <int BM, int BN>
 __global__ void __launch_bounds__(kThreads, 2)
     wgrad_kernel(const double* __restrict__ d, int kout, const double* __restrict__ h, int kin,
-                 Geometry geo, int q, int qb, int64_t rows_per_split, double* __restrict__ wpart,
-                 double* __restrict__ bpart) {
+                 Geometry geo, int64_t rows_per_split, double* __restrict__ wpart) {
   constexpr int MT = BM / 32, NT = BN / 32, LDA = BM + 4, LDB = BN + 4;
   extern __shared__ __align__(16) double smem[];
   double* sA = smem;                     // [stage][KC rows][BM+4]
@@ -445,7 +814,6 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int64_t r0 = int64_t(split) * rows_per_split;
   const int64_t r1 = (r0 + rows_per_split < geo.rows) ? r0 + rows_per_split : geo.rows;
   const int nk = r1 > r0 ? int((r1 - r0 + KC - 1) / KC) : 0;
-  const int64_t full_rows = geo.ni * q;
   auto load = [&](int kc, int stage) {
     double* dA = sA + stage * KC * LDA;
     for (int i = threadIdx.x; i < KC * (BM / 2); i += kThreads) {
@@ -469,7 +837,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int j = 0; j < NT; ++j)
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0;
-  double bacc = 0.0;
 #pragma unroll
   for (int s = 0; s < kStages - 1; ++s) {
     if (s < nk) load(s, s);
@@ -482,15 +849,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     cp_async_commit();
     const double* cA = sA + (kc % kStages) * KC * LDA + wm * (16 * MT);
     const double* cB = sB + (kc % kStages) * KC * LDB + wn * (8 * NT);
-    if (bn == 0 && threadIdx.x < BM) {
-      const double* col = sA + (kc % kStages) * KC * LDA + threadIdx.x;
-      for (int r = 0; r < KC; ++r) {
-        const int64_t gr = r0 + int64_t(kc) * KC + r;
-        if (gr >= r1) break;
-        const bool zero = gr < full_rows ? (gr % q == 0) : ((gr - full_rows) % qb == 0);
-        if (zero) bacc += col[r * LDA];
-      }
-    }
 #pragma unroll
     for (int kk = 0; kk < KC; kk += 8) {
       double a[MT][4];
@@ -523,7 +881,6 @@ __global__ void __launch_bounds__(kThreads, 2)
       out[int64_t(o + 8) * kin + c] = acc[i][j][2];
       out[int64_t(o + 8) * kin + c + 1] = acc[i][j][3];
     }
-  if (bn == 0 && threadIdx.x < BM) bpart[int64_t(split) * kout + bm * BM + threadIdx.x] = bacc;
 }
 
 // ----------------------------------------------------------------------------------
@@ -560,7 +917,7 @@ __global__ void __launch_bounds__(kThreads)
   constexpr int NFT = (HEAD == FLASHNS_B200_HEAD_PSI && BO) ? 3 : NF;  // boundary target fields
   constexpr int TPI = kHeadRows / Q, TPB = kHeadRows / QB;
   constexpr int LD = CP + 2;
-  constexpr int PARTIAL = NF * CP + NF + 1;
+  constexpr int PARTIAL = NF * CP + NF + 1 + CP;  // dW_L | db_L | loss | db_{L-1}
   static_assert(kThreads % CP == 0, "channel ownership must be fixed per thread");
   extern __shared__ __align__(16) double smem[];
   double* sH = smem;                   // [kHeadRows][LD]
@@ -577,10 +934,9 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
   for (int k = 0; k < WPT; ++k) wacc[k] = 0.0;
   double bacc = 0.0, lacc = 0.0;
-  double cacc[DIM + 1];
+  double cacc[DIM + 1];  // FIRST: coordinate contraction; otherwise cacc[0] = bias of layer L-1
 #pragma unroll
   for (int a = 0; a <= DIM; ++a) cacc[a] = 0.0;
-  const int my_c = threadIdx.x % CP;
 
   for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     const bool interior = tile < nint;
@@ -709,6 +1065,7 @@ __global__ void __launch_bounds__(kThreads)
           double* dst = dL + p * Q * CP + c;
 #pragma unroll
           for (int s = 0; s < Q; ++s) dst[int64_t(s) * CP] = zb[s];
+          cacc[0] += zb[0];
         }
       }
     } else {
@@ -738,6 +1095,7 @@ __global__ void __launch_bounds__(kThreads)
           double* dst = dL + (geo.ni * Q + b * QB) * CP + c;
 #pragma unroll
           for (int s = 0; s < QB; ++s) dst[int64_t(s) * CP] = zb[s];
+          cacc[0] += zb[0];
         }
       }
     }
@@ -758,19 +1116,18 @@ __global__ void __launch_bounds__(kThreads)
     for (int i = 0; i < kThreads; ++i) s += sRed[i];
     out[NF * CP + NF] = s;
   }
-  if constexpr (FIRST) {
-    for (int a = 0; a <= DIM; ++a) {
-      __syncthreads();
-      sRed[threadIdx.x] = cacc[a];
-      __syncthreads();
-      if (threadIdx.x < CP) {
-        double s = 0.0;
-        for (int r = threadIdx.x; r < kThreads; r += CP) s += sRed[r];
-        coord_partial[(int64_t(blockIdx.x) * CP + threadIdx.x) * (DIM + 1) + a] = s;
-      }
+  // threads with the same channel (tid % CP) combine in fixed order
+  for (int a = 0; a < (FIRST ? DIM + 1 : 1); ++a) {
+    __syncthreads();
+    sRed[threadIdx.x] = cacc[a];
+    __syncthreads();
+    if (threadIdx.x < CP) {
+      double s = 0.0;
+      for (int r = threadIdx.x; r < kThreads; r += CP) s += sRed[r];
+      if constexpr (FIRST) coord_partial[(int64_t(blockIdx.x) * CP + threadIdx.x) * (DIM + 1) + a] = s;
+      else out[NF * CP + NF + 1 + threadIdx.x] = s;
     }
   }
-  (void)my_c;
 }
 
 template <int DIM, int CP, int NF>
@@ -832,9 +1189,10 @@ struct LayerDesc {
   int coutp, cinp;        // padded widths of the stored buffers
   int64_t w_flat, b_flat; // offsets in the flat parameter vector
   int64_t w_buf, b_buf;   // offsets (doubles) of the padded buffers in the workspace
-  // gradient partials: element (k, o, i) at part[k*ws + o*wo + i]; bias (k, o) at bpart[k*bs + o*bo]
+  // gradient partials: element (k, o, i) at wpart[k*ws + o*wo + i], k < wcount;
+  // bias (k, o) at bpart[k*bs + o*bo], k < bcount
   int64_t wpart, bpart, ws, wo, bs, bo;
-  int count;
+  int wcount, bcount;
 };
 struct LayerTable {
   int n;
@@ -863,33 +1221,55 @@ __global__ void pack_params(const double* __restrict__ flat, double* __restrict_
   }
 }
 
-__global__ void reduce_grads(const double* __restrict__ ws, double* __restrict__ out, const __grid_constant__ LayerTable tab) {
-  const int64_t f = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (f > tab.params) return;
-  if (f == tab.params) {
-    double s = 0.0;
-    for (int k = 0; k < tab.loss_count; ++k) s += ws[tab.loss_part + int64_t(k) * tab.loss_stride];
-    out[f] = s;
-    return;
+// Fixed-order reduction of the per-CTA / per-split partials.  A block covers 32
+// consecutive outputs (coalesced loads along i) and splits the partial index over its 8
+// warps; each thread keeps 4 interleaved accumulators, combined in a fixed order, so the
+// result is bitwise reproducible for a given plan.
+constexpr int kReduceCols = 32, kReduceRows = 8, kReduceAcc = 4;
+
+__device__ __forceinline__ double strided_sum(const double* base, int64_t stride, int count, int start, int step) {
+  double acc[kReduceAcc] = {0.0, 0.0, 0.0, 0.0};
+  int c = start;
+  for (; c + (kReduceAcc - 1) * step < count; c += kReduceAcc * step) {
+#pragma unroll
+    for (int r = 0; r < kReduceAcc; ++r) acc[r] += base[int64_t(c + r * step) * stride];
   }
-  for (int k = 0; k < tab.n; ++k) {
-    const LayerDesc& L = tab.l[k];
-    const int64_t nw = int64_t(L.cout) * L.cin;
-    if (f >= L.w_flat && f < L.w_flat + nw) {
-      const int64_t e = f - L.w_flat;
-      const int o = int(e / L.cin), i = int(e % L.cin);
-      double s = 0.0;
-      for (int c = 0; c < L.count; ++c) s += ws[L.wpart + c * L.ws + o * L.wo + i];
-      out[f] = s;
-      return;
+  for (int r = 0; c < count; c += step, ++r) acc[r] += base[int64_t(c) * stride];
+  return (acc[0] + acc[1]) + (acc[2] + acc[3]);
+}
+
+__global__ void __launch_bounds__(kReduceCols * kReduceRows)
+    reduce_grads(const double* __restrict__ ws, double* __restrict__ out, const __grid_constant__ LayerTable tab) {
+  __shared__ double part[kReduceRows][kReduceCols];
+  const int64_t f = int64_t(blockIdx.x) * kReduceCols + threadIdx.x;
+  const int y = threadIdx.y;
+  double v = 0.0;
+  if (f == tab.params) {
+    v = strided_sum(ws + tab.loss_part, tab.loss_stride, tab.loss_count, y, kReduceRows);
+  } else if (f < tab.params) {
+    for (int k = 0; k < tab.n; ++k) {
+      const LayerDesc& L = tab.l[k];
+      const int64_t nw = int64_t(L.cout) * L.cin;
+      if (f >= L.w_flat && f < L.w_flat + nw) {
+        const int64_t e = f - L.w_flat;
+        const int o = int(e / L.cin), i = int(e % L.cin);
+        v = strided_sum(ws + L.wpart + o * L.wo + i, L.ws, L.wcount, y, kReduceRows);
+        break;
+      }
+      if (f >= L.b_flat && f < L.b_flat + L.cout) {
+        const int o = int(f - L.b_flat);
+        v = strided_sum(ws + L.bpart + o * L.bo, L.bs, L.bcount, y, kReduceRows);
+        break;
+      }
     }
-    if (f >= L.b_flat && f < L.b_flat + L.cout) {
-      const int o = int(f - L.b_flat);
-      double s = 0.0;
-      for (int c = 0; c < L.count; ++c) s += ws[L.bpart + c * L.bs + o * L.bo];
-      out[f] = s;
-      return;
-    }
+  }
+  part[y][threadIdx.x] = v;
+  __syncthreads();
+  if (y == 0 && f <= tab.params) {
+    double s = 0.0;
+#pragma unroll
+    for (int r = 0; r < kReduceRows; ++r) s += part[r][threadIdx.x];
+    out[f] = s;
   }
 }
 
@@ -910,10 +1290,11 @@ struct flashns_b200_plan {
   LayerTable tab;
   // workspace offsets in doubles
   int64_t off_h[kMaxAffine + 1], off_a1[kMaxAffine + 1], off_d[2], off_coord, off_head;
-  int64_t off_wg[kMaxAffine], off_bg[kMaxAffine];
+  int64_t off_wg[kMaxAffine], off_bb[kMaxAffine];
   int64_t workspace_doubles;
   int grid_fwd[kMaxAffine], grid_bwd[kMaxAffine], grid_head, grid_first, grid_coord;
   int wg_splits[kMaxAffine];
+  bool fused[kMaxAffine];  // backward layer l runs bwd_fused (dgrad + VJP + wgrad)
   int64_t wg_rows[kMaxAffine];
   int wg_bm[kMaxAffine], wg_bn[kMaxAffine];
 };
@@ -946,7 +1327,7 @@ struct FwdOps {
   static cudaError_t setup(int& occ) {
     constexpr size_t smem = fwd_smem_bytes<DIM, CP>();
     cudaError_t e = allow_smem(fwd_layer<DIM, CP, BO>, smem);
-    occ = occupancy(fwd_layer<DIM, CP, BO>, smem, kThreads);
+    occ = occupancy(fwd_layer<DIM, CP, BO>, smem, MmaTile<DIM, CP>::THREADS);
     return e;
   }
   static int64_t tiles(const Geometry& g) {
@@ -956,7 +1337,8 @@ struct FwdOps {
   }
   static void launch(int grid, cudaStream_t st, const double* hin, int kin, const double* w, const double* b,
                      double* hout, double* a1, Geometry g) {
-    fwd_layer<DIM, CP, BO><<<grid, kThreads, fwd_smem_bytes<DIM, CP>(), st>>>(hin, kin, w, b, hout, a1, g);
+    fwd_layer<DIM, CP, BO><<<grid, MmaTile<DIM, CP>::THREADS, fwd_smem_bytes<DIM, CP>(), st>>>(hin, kin, w, b, hout,
+                                                                                              a1, g);
   }
 };
 
@@ -965,7 +1347,7 @@ struct BwdOps {
   static cudaError_t setup(int& occ) {
     constexpr size_t smem = bwd_smem_bytes<DIM, CP>();
     cudaError_t e = allow_smem(bwd_layer<DIM, CP, BO, FIRST>, smem);
-    occ = occupancy(bwd_layer<DIM, CP, BO, FIRST>, smem, kThreads);
+    occ = occupancy(bwd_layer<DIM, CP, BO, FIRST>, smem, MmaTile<DIM, CP>::THREADS);
     return e;
   }
   static int64_t tiles(const Geometry& g) {
@@ -975,9 +1357,39 @@ struct BwdOps {
   }
   static void launch(int grid, cudaStream_t st, const double* dn, int kout, const double* w, const double* h,
                      const double* a1, double* dc, const double* x, double* cp, Geometry g) {
-    bwd_layer<DIM, CP, BO, FIRST><<<grid, kThreads, bwd_smem_bytes<DIM, CP>(), st>>>(dn, kout, w, h, a1, dc, x, cp, g);
+    bwd_layer<DIM, CP, BO, FIRST><<<grid, MmaTile<DIM, CP>::THREADS, bwd_smem_bytes<DIM, CP>(), st>>>(
+        dn, kout, w, h, a1, dc, x, cp, g);
   }
 };
+
+template <int DIM, int BO, bool FIRST>
+struct FusedOps {
+  static cudaError_t setup(int& occ) {
+    constexpr size_t smem = fused_smem_bytes<DIM>();
+    cudaError_t e = allow_smem(bwd_fused<DIM, BO, FIRST>, smem);
+    occ = occupancy(bwd_fused<DIM, BO, FIRST>, smem, FusedTile<DIM>::THREADS);
+    return e;
+  }
+  static int64_t tiles(const Geometry& g) {
+    using T = FusedTile<DIM>;
+    using TL = Tiles<DIM, BO, T::TC>;
+    return TL::interior(g.ni) + TL::boundary(g.nb);
+  }
+  static void launch(int grid, cudaStream_t st, const double* dn, const double* w, const double* h, const double* a1,
+                     double* dc, const double* x, double* part, double* wp, Geometry g) {
+    bwd_fused<DIM, BO, FIRST><<<grid, FusedTile<DIM>::THREADS, fused_smem_bytes<DIM>(), st>>>(dn, w, h, a1, dc, x, part,
+                                                                                              wp, g);
+  }
+};
+
+template <bool FIRST, typename F>
+bool with_fused(int dim, int bo, F&& f) {
+  if (dim == 2 && bo == 0) { f(FusedOps<2, 0, FIRST>{}); return true; }
+  if (dim == 2 && bo == 1) { f(FusedOps<2, 1, FIRST>{}); return true; }
+  if (dim == 3 && bo == 0) { f(FusedOps<3, 0, FIRST>{}); return true; }
+  if (dim == 3 && bo == 1) { f(FusedOps<3, 1, FIRST>{}); return true; }
+  return false;
+}
 
 template <int DIM, int CP, int BO, int HEAD, bool FIRST>
 struct HeadOps {
@@ -1044,8 +1456,8 @@ struct WgradOps {
   static size_t smem() { return sizeof(double) * kStages * KC * ((BM + 4) + (BN + 4)); }
   static cudaError_t setup() { return allow_smem(wgrad_kernel<BM, BN>, smem()); }
   static void launch(dim3 grid, cudaStream_t st, const double* d, int kout, const double* h, int kin, Geometry g,
-                     int q, int qb, int64_t rps, double* wp, double* bp) {
-    wgrad_kernel<BM, BN><<<grid, kThreads, smem(), st>>>(d, kout, h, kin, g, q, qb, rps, wp, bp);
+                     int64_t rps, double* wp) {
+    wgrad_kernel<BM, BN><<<grid, kThreads, smem(), st>>>(d, kout, h, kin, g, rps, wp);
   }
 };
 
@@ -1129,6 +1541,7 @@ int flashns_b200_plan_create(int dim, int head, int boundary_order, int n_affine
   }
   for (int l = 1; l < nh; ++l) {  // backward layer l: D_{l+1} -> D_l (width padded[l])
     const int cp = p->padded[l];
+    p->fused[l] = cp == kFusedWidth && p->padded[l + 1] == kFusedWidth;
     auto f = [&](auto ops) {
       int occ = 1;
       cudaError_t e = ops.setup(occ);
@@ -1136,8 +1549,14 @@ int flashns_b200_plan_create(int dim, int head, int boundary_order, int n_affine
       const int64_t t = ops.tiles(p->geo);
       p->grid_bwd[l] = int(std::max<int64_t>(1, std::min<int64_t>(t, int64_t(occ) * p->sms)));
     };
-    if (l == 1) with_bwd<true>(dim, cp, boundary_order, f);
-    else with_bwd<false>(dim, cp, boundary_order, f);
+    if (p->fused[l]) {
+      if (l == 1) with_fused<true>(dim, boundary_order, f);
+      else with_fused<false>(dim, boundary_order, f);
+    } else if (l == 1) {
+      with_bwd<true>(dim, cp, boundary_order, f);
+    } else {
+      with_bwd<false>(dim, cp, boundary_order, f);
+    }
   }
   {
     auto f = [&](auto ops) {
@@ -1188,11 +1607,24 @@ int flashns_b200_plan_create(int dim, int head, int boundary_order, int n_affine
     LayerDesc& L = tab.l[0];
     L.wpart = p->off_coord; L.ws = int64_t(p->padded[1]) * (dim + 1); L.wo = dim + 1;
     L.bpart = p->off_coord + dim; L.bs = L.ws; L.bo = dim + 1;
-    L.count = p->grid_coord;
+    L.wcount = L.bcount = p->grid_coord;
+  }
+  // bias partials of layer l-1 written by backward layer l >= 2: [grid_bwd[l]][CP_l]
+  for (int l = 2; l < nh; ++l) {
+    p->off_bb[l] = take(int64_t(p->grid_bwd[l]) * p->padded[l]);
+    LayerDesc& L = tab.l[l - 1];
+    L.bpart = p->off_bb[l]; L.bs = p->padded[l]; L.bo = 1; L.bcount = p->grid_bwd[l];
   }
   // hidden-layer wgrad partials
   for (int l = 1; l < nh; ++l) {
     const int kout = p->padded[l + 1], kin = p->padded[l];
+    if (p->fused[l]) {  // one [CP][CP] partial per CTA of the fused backward
+      p->off_wg[l] = take(int64_t(p->grid_bwd[l]) * kout * kin);
+      LayerDesc& L = tab.l[l];
+      L.wpart = p->off_wg[l]; L.ws = int64_t(kout) * kin; L.wo = kin;
+      L.wcount = p->grid_bwd[l];
+      continue;
+    }
     const int bm = std::min(kout, 64), bn = std::min(kin, 64);
     const int blocks = (kout / bm) * (kin / bn);
     const int target = 2 * p->sms;
@@ -1202,32 +1634,34 @@ int flashns_b200_plan_create(int dim, int head, int boundary_order, int n_affine
     splits = std::max<int64_t>(1, (p->rows + rps - 1) / rps);
     p->wg_splits[l] = int(splits); p->wg_rows[l] = rps; p->wg_bm[l] = bm; p->wg_bn[l] = bn;
     p->off_wg[l] = take(splits * kout * kin);
-    p->off_bg[l] = take(splits * kout);
     LayerDesc& L = tab.l[l];
     L.wpart = p->off_wg[l]; L.ws = int64_t(kout) * kin; L.wo = kin;
-    L.bpart = p->off_bg[l]; L.bs = kout; L.bo = 1;
-    L.count = int(splits);
+    L.wcount = int(splits);
     with_wgrad(bm, bn, [&](auto ops) {
       cudaError_t e = ops.setup();
       if (e != cudaSuccess) err = e;
     });
   }
-  // head partials: [grid_head][NF*CP + NF + 1]
+  // head partials: [grid_head][NF*CP + NF + 1 + CP]: dW_L, db_L, loss, db_{L-1}
   {
     const int cp = p->padded[nh];
-    const int64_t stride = int64_t(nf) * cp + nf + 1;
+    const int64_t stride = int64_t(nf) * cp + nf + 1 + cp;
     p->off_head = take(int64_t(p->grid_head) * stride);
     LayerDesc& L = tab.l[nh];
     L.wpart = p->off_head; L.ws = stride; L.wo = cp;
     L.bpart = p->off_head + int64_t(nf) * cp; L.bs = stride; L.bo = 1;
-    L.count = p->grid_head;
+    L.wcount = L.bcount = p->grid_head;
+    if (nh >= 2) {
+      LayerDesc& B = tab.l[nh - 1];
+      B.bpart = p->off_head + int64_t(nf) * cp + nf + 1; B.bs = stride; B.bo = 1; B.bcount = p->grid_head;
+    }
     tab.loss_part = p->off_head + int64_t(nf) * cp + nf;
     tab.loss_stride = stride;
     tab.loss_count = p->grid_head;
   }
   if (err != cudaSuccess) { delete p; return int(err); }
   if (p->rows == 0) {  // nothing to evaluate: every partial count is zero, outputs are zeros
-    for (int l = 0; l < n_affine; ++l) tab.l[l].count = 0;
+    for (int l = 0; l < n_affine; ++l) tab.l[l].wcount = tab.l[l].bcount = 0;
     tab.loss_count = 0;
   }
   p->workspace_doubles = off;
@@ -1308,15 +1742,25 @@ static int run_eval(const flashns_b200_plan* p, const double* coordinates, const
       else with_head<false>(p->dim, p->padded[nh], p->bo, p->head, f);
       if ((e = cudaGetLastError()) != cudaSuccess) return int(e);
     }
-    const int q = p->dim == 2 ? 10 : 20, qb = p->bo ? p->dim + 1 : 1;
     for (int l = nh - 1; l >= 1; --l) {
       const LayerDesc& L = tab.l[l];
       const double* dn = ws + p->off_d[(l + 1) % 2];
       auto f = [&](auto ops) {
         ops.launch(p->grid_bwd[l], stream, dn, p->padded[l + 1], ws + L.w_buf, ws + p->off_h[l], ws + p->off_a1[l],
-                   ws + p->off_d[l % 2], coordinates, ws + p->off_coord, g);
+                   ws + p->off_d[l % 2], coordinates, ws + (l == 1 ? p->off_coord : p->off_bb[l]), g);
       };
       mark();
+      if (p->fused[l]) {
+        auto ff = [&](auto ops) {
+          ops.launch(p->grid_bwd[l], stream, dn, ws + L.w_buf, ws + p->off_h[l], ws + p->off_a1[l],
+                     ws + p->off_d[l % 2], coordinates, ws + (l == 1 ? p->off_coord : p->off_bb[l]),
+                     ws + p->off_wg[l], g);
+        };
+        if (l == 1) with_fused<true>(p->dim, p->bo, ff);
+        else with_fused<false>(p->dim, p->bo, ff);
+        if ((e = cudaGetLastError()) != cudaSuccess) return int(e);
+        continue;
+      }
       if (l == 1) with_bwd<true>(p->dim, p->padded[l], p->bo, f);
       else with_bwd<false>(p->dim, p->padded[l], p->bo, f);
       if ((e = cudaGetLastError()) != cudaSuccess) return int(e);
@@ -1324,14 +1768,14 @@ static int run_eval(const flashns_b200_plan* p, const double* coordinates, const
       const dim3 grid(unsigned(p->wg_splits[l]), unsigned((kout / p->wg_bm[l]) * (kin / p->wg_bn[l])));
       mark();
       with_wgrad(p->wg_bm[l], p->wg_bn[l], [&](auto ops) {
-        ops.launch(grid, stream, dn, kout, ws + p->off_h[l], kin, g, q, qb, p->wg_rows[l], ws + p->off_wg[l],
-                   ws + p->off_bg[l]);
+        ops.launch(grid, stream, dn, kout, ws + p->off_h[l], kin, g, p->wg_rows[l], ws + p->off_wg[l]);
       });
       if ((e = cudaGetLastError()) != cudaSuccess) return int(e);
     }
   }
   mark();
-  reduce_grads<<<unsigned((tab.params + 1 + kThreads - 1) / kThreads), kThreads, 0, stream>>>(ws, gradient_and_loss, tab);
+  reduce_grads<<<unsigned((tab.params + 1 + kReduceCols - 1) / kReduceCols), dim3(kReduceCols, kReduceRows), 0, stream>>>(
+      ws, gradient_and_loss, tab);
   e = cudaGetLastError();
   mark();
   if (recorded) *recorded = marks;
@@ -1365,7 +1809,7 @@ int flashns_b200_plan_launch_kinds(const flashns_b200_plan* p, int* kinds, int c
     k.push_back(FLASHNS_B200_KERNEL_HEAD);
     for (int l = nh - 1; l >= 1; --l) {
       k.push_back(FLASHNS_B200_KERNEL_BACKWARD);
-      k.push_back(FLASHNS_B200_KERNEL_WGRAD);
+      if (!p->fused[l]) k.push_back(FLASHNS_B200_KERNEL_WGRAD);
     }
   }
   k.push_back(FLASHNS_B200_KERNEL_REDUCE);
