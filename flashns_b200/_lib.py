@@ -25,6 +25,19 @@ SIGNATURES = {
     "flashns_b200_plan_launch_kinds": [_c_ptr, ctypes.POINTER(_c_int), _c_int, ctypes.POINTER(_c_int)],
     "flashns_b200_fp64_peak_probe": [_c_int, _c_int, _c_ptr, ctypes.POINTER(_c_dbl), _c_ptr],
     "flashns_b200_eval_static": [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr],
+    "flashns_b200_residuals": [_c_int, _c_int, _c_ptr, _c_dbl, _c_ptr, _c_i64, _c_ptr],
+    # reference-ABI hooks (experiments/pinn_v8/native.py:26-51, experiments/cuda_jet_h100/gpu.py)
+    "flashns_v8_activation": [_c_int, _c_int] + [_c_ptr] * 5 + [_c_i64, _c_i64, _c_int, _c_ptr],
+    "flashns_v8_coordinate_affine": [_c_int] + [_c_ptr] * 4 + [_c_i64, _c_i64, _c_int, _c_ptr],
+    "flashns_v8_coordinate_affine_activation": [_c_int] + [_c_ptr] * 5 + [_c_i64, _c_i64, _c_int, _c_ptr],
+    "flashns_v8_tail3": [_c_int, _c_int] + [_c_ptr] * 5 + [_c_i64, _c_i64, _c_int, _c_ptr],
+    "flashns_v8_coordinate_wgrad": [_c_int] + [_c_ptr] * 5 + [_c_i64, _c_i64, _c_int, _c_ptr],
+    "flashns_v8_coordinate_activation_wgrad": [_c_int] + [_c_ptr] * 7 + [_c_i64, _c_i64, _c_int, _c_ptr],
+    "flashns_v8_loss_seed": [_c_ptr] * 8 + [_c_i64] * 3 + [_c_dbl] * 3 + [_c_ptr],
+    "flashns_stable_activation": [_c_int, ctypes.c_bool] + [_c_ptr] * 5 + [_c_size, _c_size, _c_ptr],
+    "flashns_stable_tail3": [_c_int, ctypes.c_bool] + [_c_ptr] * 5 + [_c_size, _c_size, _c_ptr],
+    "flashns_stable_dgrad_vjp": [_c_int, ctypes.c_bool] + [_c_ptr] * 5 + [_c_int] * 3 + [_c_ptr],
+    "flashns_stable_dgrad_shared_bytes": [],
 }
 
 KERNEL_KINDS = {0: "pack", 1: "first", 2: "forward", 3: "head", 4: "backward", 5: "wgrad", 6: "reduce"}

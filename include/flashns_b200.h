@@ -11,6 +11,7 @@
 #ifndef FLASHNS_B200_H
 #define FLASHNS_B200_H
 
+#include <stdbool.h>
 #include <stddef.h>
 #include <stdint.h>
 #include <cuda_runtime.h>
@@ -96,6 +97,65 @@ int flashns_b200_eval_static(const flashns_b200_plan* plan, const double* coordi
  * 8 independent DMMA m16n8k8 per warp from registers; *flops = floating-point operations
  * issued.  Time it with events on `stream` for the FP64 roofline denominator. */
 int flashns_b200_fp64_peak_probe(int blocks, int iters, double* sink, double* flops, cudaStream_t stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Per-stage hooks with the reference's C ABI (same names, argument order and meaning,
+ * caller-provided scratch), so the reference's ctypes bindings can load this library.
+ * Packed layout: rows [full_points x Q ; value_points x 1] x channels, Q = 10 (2-D) / 20 (3-D).
+ */
+
+/* experiments/pinn_v8/native.cu:47-62.  backward=0: input = Z -> output = H, output_auxiliary
+ * = a1 [points, C]; backward=1: input = H, auxiliary = a1, seed = bar_H -> output = bar_Z. */
+int flashns_v8_activation(int dimension, int backward, const double* input, const double* auxiliary,
+                          const double* seed, double* output, double* output_auxiliary, int64_t full_points,
+                          int64_t value_points, int channels, cudaStream_t stream);
+/* experiments/pinn_v8/native.cu:115-121: first affine jet of physical coordinates [points, dim] */
+int flashns_v8_coordinate_affine(int dimension, const double* coordinates, const double* weight, const double* bias,
+                                 double* output, int64_t full_points, int64_t value_points, int channels,
+                                 cudaStream_t stream);
+/* experiments/pinn_v8/native.cu:123-129: the same followed by the stable tanh jet */
+int flashns_v8_coordinate_affine_activation(int dimension, const double* coordinates, const double* weight,
+                                            const double* bias, double* hidden, double* auxiliary,
+                                            int64_t full_points, int64_t value_points, int channels,
+                                            cudaStream_t stream);
+/* experiments/pinn_v8/native.cu:174-200: bar_H = D[rows,3] W[3,C] ((d0 w0 + d1 w1) + d2 w2);
+ * fused=1 applies the jet VJP with hidden/auxiliary */
+int flashns_v8_tail3(int dimension, int fused, const double* d, const double* weight, const double* hidden,
+                     const double* auxiliary, double* output, int64_t full_points, int64_t value_points, int channels,
+                     cudaStream_t stream);
+/* experiments/pinn_v8/native.cu:275-281: dW0[C,dim], db0[C] from bar_Z; partials scratch
+ * [(points+7)/8, C, dim+1]; deterministic (fixed 8-point tiles, fixed-order merge) */
+int flashns_v8_coordinate_wgrad(int dimension, const double* derivative, const double* coordinates, double* partials,
+                                double* weight_gradient, double* bias_gradient, int64_t full_points,
+                                int64_t value_points, int channels, cudaStream_t stream);
+/* experiments/pinn_v8/native.cu:283-290: the first activation's VJP followed by the same */
+int flashns_v8_coordinate_activation_wgrad(int dimension, const double* hidden, const double* auxiliary,
+                                           const double* seed, const double* coordinates, double* partials,
+                                           double* weight_gradient, double* bias_gradient, int64_t full_points,
+                                           int64_t value_points, int channels, cudaStream_t stream);
+/* experiments/pinn_v8/native.cu:325-337: (u, v, p) residual loss + seed; interior jets
+ * [ni,10,3], boundary value rows [nb, stride >= 3]; partial_loss[(ni+nb+127)/128] (summed by
+ * the caller) */
+int flashns_v8_loss_seed(const double* jets, const double* boundary, const double* pde_weights,
+                         const double* boundary_weights, const double* target, double* interior_seed,
+                         double* boundary_seed, double* partial_loss, int64_t ni, int64_t nb, int64_t boundary_stride,
+                         double nu, double gamma, double bc_scale, cudaStream_t stream);
+
+/* Dense [B,Q,C] layout (experiments/cuda_jet_h100/stable_kernels.cu:93-131, stable_dgrad.cu:150-174) */
+int flashns_stable_activation(int dim, bool backward, const double* value, const double* adjoint, const double* aux_in,
+                              double* output, double* aux_out, size_t batch, size_t channels, cudaStream_t stream);
+int flashns_stable_tail3(int dim, bool fused, const double* d, const double* weight, const double* hidden,
+                         const double* aux, double* output, size_t batch, size_t channels, cudaStream_t stream);
+/* out[B,Q,Cin] = D[B,Q,Cout] W[Cout,Cin] (fused: followed by the jet VJP with h[B,Q,Cin], aux[B,Cin]) */
+int flashns_stable_dgrad_vjp(int dim, bool fused, const double* d, const double* w, const double* h, const double* aux,
+                             double* out, int batch, int cout, int cin, cudaStream_t stream);
+/* Residual values at interior points: jets [n, Q, F] coefficient-major -> out [n, R]; head UVP:
+ * the nine residuals of src/flashns/ns_seed.py:26-64 (R = 9); head PSI: (r_u, r_v) (R = 2). */
+int flashns_b200_residuals(int head, int dim, const double* jets, double nu, double* out, int64_t n,
+                           cudaStream_t stream);
+
+/* shared memory the dense dgrad uses per block (0: this implementation stages none) */
+int flashns_stable_dgrad_shared_bytes(void);
 
 #ifdef __cplusplus
 }

@@ -31,7 +31,7 @@ REF = Path(os.environ.get("FLASHNS_REFERENCE", "/root/reference"))
 sys.path.insert(0, str(REF / "src"))
 
 from flashns.jet_packed import PackedLayout, TensorActivation  # noqa: E402
-from flashns.ns_seed import NSLoss, explicit_seed, residuals  # noqa: E402
+from flashns.ns_seed import NSLoss, explicit_seed, residual_terms, residuals  # noqa: E402
 from flashns.pinn_packed import PackedPINN  # noqa: E402
 
 _spec = importlib.util.spec_from_file_location(
@@ -86,6 +86,10 @@ def seed_cases():
                         p + "res": r.numpy()})
             k += 1
     out["seed_count"] = np.array(k)
+    for m, nu in enumerate((0.0, 0.05, 0.07, 0.2)):
+        rows = [(r, c, i, j) for r, terms in enumerate(residual_terms(nu)) for c, i, j in terms]
+        out[f"terms{m}_nu"] = np.array(nu)
+        out[f"terms{m}"] = np.array(rows, dtype=np.float64)
     return out
 
 

@@ -89,3 +89,28 @@ def test_problem_generators_and_shards():
     assert sum(p.interior_count for p in parts) == g.interior_count
     assert sum(len(p.x) for p in parts) == len(g.x)
     assert abs(sum(float(p.pde_weights.sum()) for p in parts) - 1) < 1e-12
+
+
+def test_residual_terms_match_reference_table():
+    """ns_seed.residual_terms (derived from the PDE) equals the reference table
+    (src/flashns/ns_seed.py:26-43, recorded in tests/golden) as polynomials."""
+    from tests.cases import GOLDEN
+    from flashns_b200.ns_seed import residual_terms
+    g = np.load(GOLDEN / "reference_seed.npz")
+
+    def norm(terms):
+        d = {}
+        for c, i, j in terms:
+            i, j = int(i), int(j)
+            k = (min(i, j), max(i, j)) if j >= 0 else (i, -1)
+            d[k] = d.get(k, 0.0) + c
+        return {k: round(v, 12) for k, v in d.items()}
+
+    for m in range(4):
+        nu = float(g[f"terms{m}_nu"])
+        rows = g[f"terms{m}"]
+        ref = [[(c, i, j) for r2, c, i, j in rows if int(r2) == r] for r in range(9)]
+        mine = residual_terms(nu)
+        assert len(mine) == 9
+        for a, b in zip(mine, ref):
+            assert norm(a) == norm(b)
