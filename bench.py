@@ -216,7 +216,7 @@ def main():
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=60), device_id=device)
     c = CONFIGS[args.config]
     widths = c["widths"]
     # weak scaling: the global set is `world` x the config; each rank owns one config-sized shard
@@ -255,11 +255,19 @@ def main():
         return
 
     sampler = ClockSampler(local, f"/tmp/flashns_clocks_{rank}.csv")
-    t_end = time.perf_counter() + 1.0  # settle clocks under load before timing
-    while time.perf_counter() < t_end:
+    # settle clocks under load for about a second; rank 0 decides per batch and every
+    # rank follows, so all ranks issue the same collectives in the same order
+    t_end = time.perf_counter() + 1.0
+    go = torch.ones(1, dtype=torch.int32, device=device)
+    while True:
         for _ in range(20):
             step()
         torch.cuda.synchronize()
+        go.fill_(int(time.perf_counter() < t_end))
+        if world > 1:
+            dist.broadcast(go, 0)
+        if not int(go):
+            break
     for _ in range(max(args.warmup, 3)):
         step()
     barrier()

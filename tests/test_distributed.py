@@ -1,0 +1,104 @@
+"""CPU (gloo, world size 2): the data-parallel reduction gives every rank the
+single-process loss and gradient, and a non-finite value on one rank reaches all."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _oracle_factory(widths, params, poison_rank=None):
+    """Local evaluator on the CPU oracle (test stand-in for the CUDA evaluator)."""
+    from oracle.evaluate import evaluate
+
+    def factory(shard):
+        def run(flat, out=None):
+            n = len(widths) - 1
+            sizes = [i * o for i, o in zip(widths, widths[1:])]
+            f = flat.numpy()
+            ws, off = [], 0
+            for (i, o), sz in zip(zip(widths, widths[1:]), sizes):
+                ws.append(f[off:off + sz].reshape(o, i)); off += sz
+            bs = []
+            for o in widths[1:]:
+                bs.append(f[off:off + o]); off += o
+            loss, grads = evaluate(shard.x.numpy(), shard.interior_count, shard.pde_weights.numpy(),
+                                   shard.boundary_weights.numpy(), shard.target.numpy(), ws, bs, head="psi",
+                                   nu=shard.viscosity, boundary_order=1)
+            res = torch.tensor(np.concatenate([g.reshape(-1) for g in grads] + [[loss]]))
+            if poison_rank is not None and dist.get_rank() == poison_rank:
+                res[3] = float("nan")
+            return res
+        return run
+    return factory
+
+
+def _worker(rank, world, port, widths, params, expected, poison, queue):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from flashns_b200.distributed import DistributedEvaluator
+        from flashns_b200.problems import kovasznay
+        pts = kovasznay(37, 13, seed=4)
+        ev = DistributedEvaluator(pts, widths, local_factory=_oracle_factory(widths, params, poison))
+        out = ev(torch.tensor(params))
+        if poison is None:
+            err = float(np.max(np.abs(out.numpy() - expected) / (2e-12 + 2e-11 * np.abs(expected))))
+            queue.put((rank, "ok", err, DistributedEvaluator.finite(out)))
+        else:
+            queue.put((rank, "poison", 0.0, DistributedEvaluator.finite(out)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("poison", [None, 1])
+def test_two_rank_reduction_matches_single_process(poison):
+    from flashns_b200.evaluator import flat_parameters, xavier_normal
+    from flashns_b200.problems import kovasznay
+    from oracle.evaluate import evaluate
+    widths = [2, 12, 10, 2]
+    ws, bs = xavier_normal(widths, 0)
+    params = flat_parameters(ws, bs).numpy()
+    pts = kovasznay(37, 13, seed=4)
+    loss, grads = evaluate(pts.x.numpy(), pts.interior_count, pts.pde_weights.numpy(), pts.boundary_weights.numpy(),
+                           pts.target.numpy(), [w.numpy() for w in ws], [b.numpy() for b in bs], head="psi",
+                           nu=pts.viscosity, boundary_order=1)
+    expected = np.concatenate([g.reshape(-1) for g in grads] + [[loss]])
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, widths, params, expected, poison, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [queue.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, kind, err, finite in results:
+        if poison is None:
+            assert err <= 1.0 and finite
+        else:
+            assert not finite  # every rank sees the poisoned value
+
+
+def test_shards_partition_points_and_weights():
+    from flashns_b200.problems import kovasznay
+    pts = kovasznay(101, 37, seed=2)
+    for world in (1, 2, 3, 8):
+        shards = [pts.shard(world, r) for r in range(world)]
+        assert sum(s.interior_count for s in shards) == 101
+        assert sum(len(s.x) for s in shards) == 138
+        assert abs(sum(float(s.pde_weights.sum()) for s in shards) - float(pts.pde_weights.sum())) < 1e-14
+        xs = torch.cat([s.x[:s.interior_count] for s in shards])
+        assert torch.equal(xs, pts.x[:101])
