@@ -1876,3 +1876,80 @@ extern "C" int flashns_b200_eval_static(const flashns_b200_plan* p, const double
   return run_eval(p, coordinates, parameters, pde_weights, boundary_weights, target, gradient_and_loss, scratch,
                   size_t(FLASHNS_B200_STATIC_WORKSPACE_BYTES), stream, nullptr, 0, nullptr);
 }
+
+// ======================================================================================
+// Forward-only fields at points (for acceptance grids and validation): a plan created
+// with interior_points = 0 carries every point as a boundary point; the forward kernels
+// run as in an evaluation and the output layer writes per point (u, v, p):
+// psi head with first-order rows: (psi_y, -psi_x, p); value rows: the raw outputs.
+namespace flashns_b200 {
+template <int DIM, int BO, int HEAD>
+__global__ void __launch_bounds__(kThreads)
+    fields_kernel(const double* __restrict__ hL, const double* __restrict__ wL, const double* __restrict__ bL, int cp,
+                  double* __restrict__ out, int64_t points) {
+  constexpr int NF = HeadTraits<HEAD>::NF, QB = BO ? DIM + 1 : 1;
+  constexpr int NFT = (HEAD == FLASHNS_B200_HEAD_PSI && BO) ? 3 : NF;
+  for (int64_t p = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; p < points; p += int64_t(gridDim.x) * blockDim.x) {
+    double y[QB][NF];
+#pragma unroll
+    for (int r = 0; r < QB; ++r) {
+      const double* h = hL + (p * QB + r) * cp;
+#pragma unroll
+      for (int o = 0; o < NF; ++o) {
+        double s = 0.0;
+        for (int c = 0; c < cp; ++c) s += h[c] * wL[o * cp + c];
+        y[r][o] = r == 0 ? s + bL[o] : s;
+      }
+    }
+    double* dst = out + p * NFT;
+    if constexpr (NFT == 3 && HEAD == FLASHNS_B200_HEAD_PSI) {
+      dst[0] = y[unit_row<DIM>(1)][0];   // u = psi_y
+      dst[1] = -y[unit_row<DIM>(0)][0];  // v = -psi_x
+      dst[2] = y[0][1];                  // p
+    } else {
+#pragma unroll
+      for (int o = 0; o < NF; ++o) dst[o] = y[0][o];
+    }
+  }
+}
+}  // namespace flashns_b200
+
+extern "C" int flashns_b200_fields(const flashns_b200_plan* p, const double* coordinates, const double* parameters,
+                                   double* fields, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  if (!p || !parameters || !fields || !workspace || p->ni != 0) return int(cudaErrorInvalidValue);
+  if (workspace_bytes < size_t(p->workspace_doubles) * sizeof(double)) return int(cudaErrorInvalidValue);
+  if ((reinterpret_cast<uintptr_t>(workspace) & 15) != 0) return int(cudaErrorInvalidValue);
+  if (p->points == 0) return int(cudaSuccess);
+  if (!coordinates) return int(cudaErrorInvalidValue);
+  double* ws = static_cast<double*>(workspace);
+  const LayerTable& tab = p->tab;
+  int64_t packed = 0;
+  for (int l = 0; l < p->n_aff; ++l) packed += int64_t(tab.l[l].coutp) * tab.l[l].cinp + tab.l[l].coutp;
+  pack_params<<<unsigned((packed + kThreads - 1) / kThreads), kThreads, 0, stream>>>(parameters, ws, tab);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return int(e);
+  const int nh = p->n_aff - 1;
+  const Geometry g = p->geo;
+  const LayerDesc& L0 = tab.l[0];
+  int r = first_launch(p->dim, p->bo, p->grid_first, stream, coordinates, ws + L0.w_buf, ws + L0.b_buf,
+                       ws + p->off_h[1], ws + p->off_a1[1], p->padded[1], g);
+  if (r) return r;
+  for (int l = 1; l < nh; ++l) {
+    const LayerDesc& L = tab.l[l];
+    with_fwd<FwdOps>(p->dim, p->padded[l + 1], p->bo, [&](auto ops) {
+      ops.launch(p->grid_fwd[l], stream, ws + p->off_h[l], p->padded[l], ws + L.w_buf, ws + L.b_buf,
+                 ws + p->off_h[l + 1], ws + p->off_a1[l + 1], g);
+    });
+    if ((e = cudaGetLastError()) != cudaSuccess) return int(e);
+  }
+  const LayerDesc& LL = tab.l[nh];
+  const unsigned grid = unsigned(std::min<int64_t>((p->points + kThreads - 1) / kThreads, int64_t(p->sms) * 8));
+  const double* h = ws + p->off_h[nh];
+  const int cp = p->padded[nh];
+  if (p->head == FLASHNS_B200_HEAD_UVP) fields_kernel<2, 0, FLASHNS_B200_HEAD_UVP><<<grid, kThreads, 0, stream>>>(h, ws + LL.w_buf, ws + LL.b_buf, cp, fields, p->points);
+  else if (p->dim == 2 && p->bo) fields_kernel<2, 1, FLASHNS_B200_HEAD_PSI><<<grid, kThreads, 0, stream>>>(h, ws + LL.w_buf, ws + LL.b_buf, cp, fields, p->points);
+  else if (p->dim == 2) fields_kernel<2, 0, FLASHNS_B200_HEAD_PSI><<<grid, kThreads, 0, stream>>>(h, ws + LL.w_buf, ws + LL.b_buf, cp, fields, p->points);
+  else if (p->bo) fields_kernel<3, 1, FLASHNS_B200_HEAD_PSI><<<grid, kThreads, 0, stream>>>(h, ws + LL.w_buf, ws + LL.b_buf, cp, fields, p->points);
+  else fields_kernel<3, 0, FLASHNS_B200_HEAD_PSI><<<grid, kThreads, 0, stream>>>(h, ws + LL.w_buf, ws + LL.b_buf, cp, fields, p->points);
+  return int(cudaGetLastError());
+}

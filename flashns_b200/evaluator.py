@@ -163,3 +163,37 @@ def xavier_normal(widths, seed, dtype=torch.float64):
                for i, o in zip(widths, widths[1:])]
     biases = [torch.zeros(o, dtype=dtype) for o in widths[1:]]
     return weights, biases
+
+
+class FieldEvaluator:
+    """Forward-only (u, v, p) -- or the raw outputs with value rows -- at a fixed point set
+    (the acceptance grid of a solve): ``__call__(flat) -> fields [points, F]``."""
+
+    def __init__(self, x, widths, *, head="psi", boundary_order=1, device=None):
+        device = torch.device(device if device is not None else (x.device if x.is_cuda else "cuda"))
+        if device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        if x.ndim != 2 or x.dtype != torch.float64:
+            raise ValueError("FP64 coordinates [points, dim] required")
+        self.widths, self.head, self.device = [int(w) for w in widths], head, device
+        with torch.cuda.device(device):
+            self.plan = Plan(x.shape[1], head, boundary_order, self.widths, 0, len(x), NSLoss())
+            self.x = x.detach().to(device).contiguous()
+            self.workspace = torch.empty(max(1, self.plan.workspace_bytes // 8), dtype=torch.float64, device=device)
+        self.width = target_width(head, boundary_order)
+        self.parameters = self.plan.parameters
+
+    def __call__(self, flat, out=None):
+        if flat.shape != (self.parameters,) or flat.dtype != torch.float64 or flat.device != self.device:
+            raise ValueError(f"flat FP64 parameters [{self.parameters}] on {self.device} required")
+        if out is None:
+            out = torch.empty((len(self.x), self.width), dtype=torch.float64, device=self.device)
+        lib = self.plan._lib
+        with torch.cuda.device(self.device):
+            stream = torch.cuda.current_stream()
+            status = lib.flashns_b200_fields(self.plan.handle, ctypes.c_void_p(self.x.data_ptr()),
+                                             ctypes.c_void_p(flat.contiguous().data_ptr()),
+                                             ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(self.workspace.data_ptr()),
+                                             self.workspace.numel() * 8, ctypes.c_void_p(stream.cuda_stream))
+        _lib.check(status, "flashns_b200_fields")
+        return out

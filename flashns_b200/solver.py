@@ -1,0 +1,160 @@
+"""Kovasznay time-to-accuracy solve.
+
+The reference's complete solve (experiments/pinn_solver/solve.py:77-167) replays a
+CUDA-graph-captured loss + gradient evaluation as the closure of an Adam phase and a
+strong-Wolfe ``torch.optim.LBFGS``.  Here the closure replays one captured
+``flashns_b200_eval`` (plus the gradient all-reduce on several GPUs); acceptance is the
+relative L2 error of (u, v) <= 1e-3 and of p <= 1e-2 against the analytic Kovasznay
+fields on a 201 x 201 grid over the domain, evaluated with ``flashns_b200_fields``.
+
+    python -m flashns_b200.solver                       # one GPU
+    torchrun --nproc-per-node N -m flashns_b200.solver  # N GPUs (sample data parallelism)
+
+The wall time includes setup (point generation, plans, graph capture), every closure
+evaluation of the line searches and the acceptance checks.
+"""
+
+import argparse
+import json
+import math
+import os
+import time
+
+import torch
+import torch.distributed as dist
+
+from flashns_b200.evaluator import FieldEvaluator, PackedEvaluator, flat_parameters, xavier_normal
+from flashns_b200.ns_seed import NSLoss
+from flashns_b200.problems import kovasznay, kovasznay_exact
+
+
+def acceptance_grid(n=201):
+    xs = torch.linspace(-0.5, 1.0, n, dtype=torch.float64)
+    ys = torch.linspace(-0.5, 1.5, n, dtype=torch.float64)
+    gx, gy = torch.meshgrid(xs, ys, indexing="ij")
+    return torch.stack((gx.reshape(-1), gy.reshape(-1)), 1)
+
+
+class Acceptance:
+    """Relative L2 errors of (u, v, p) on the grid against the analytic solution."""
+
+    def __init__(self, widths, re, device, n=201):
+        grid = acceptance_grid(n)
+        u, v, p, _ = kovasznay_exact(grid, re)
+        self.exact = torch.stack((u, v, p), 1).to(device)
+        self.norm = self.exact.square().sum(0).sqrt()
+        self.fields = FieldEvaluator(grid, widths, head="psi", boundary_order=1, device=device)
+
+    def __call__(self, flat):
+        f = self.fields(flat)
+        err = (f - self.exact).square().sum(0).sqrt() / self.norm
+        return [float(e) for e in err.cpu()]
+
+
+def solve(*, interior=16384, boundary=4096, widths=(2, 64, 64, 64, 64, 2), re=20.0, seed=1, init_seed=0,
+          boundary_weight=5.0, tol_uv=1e-3, tol_p=1e-2, max_iterations=50000, check_every=100, history=50,
+          adam_steps=3000, adam_lr=1e-3, grid=201, device=None, log=None, time_limit=None):
+    start = time.perf_counter()
+    world = dist.get_world_size() if dist.is_initialized() else 1
+    rank = dist.get_rank() if dist.is_initialized() else 0
+    device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    widths = list(widths)
+    pts = kovasznay(interior, boundary, re=re, seed=seed, boundary_order=1)
+    loss = NSLoss(viscosity=1.0 / re, boundary_weight=boundary_weight)
+    if world > 1:
+        from flashns_b200.distributed import DistributedEvaluator
+        ev = DistributedEvaluator(pts, widths, head="psi", boundary_order=1, loss=loss, device=device)
+    else:
+        ev = PackedEvaluator(pts.x, pts.interior_count, pts.pde_weights, pts.boundary_weights, pts.target, widths,
+                             head="psi", boundary_order=1, loss=loss, device=device)
+    accept = Acceptance(widths, re, device, grid)
+    ws, bs = xavier_normal(widths, init_seed)
+    flat = torch.nn.Parameter(flat_parameters(ws, bs).to(device))
+    out = torch.empty(ev.parameters + 1, dtype=torch.float64, device=device)
+    # capture one evaluation (the parameter storage stays at the same address)
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            ev(flat.data, out)
+    torch.cuda.current_stream(device).wait_stream(stream)
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        ev(flat.data, out)
+    grad_view, loss_view = out[:ev.parameters], out[ev.parameters]
+    evaluations = [0]
+
+    def closure():
+        graph.replay()
+        evaluations[0] += 1
+        flat.grad = grad_view
+        return loss_view
+
+    if adam_steps:
+        # Adam phase on the same captured closure (experiments/pinn_solver/solve.py:137-149)
+        adam = torch.optim.Adam([flat], lr=adam_lr)
+        for _ in range(adam_steps):
+            closure()
+            adam.step()
+    optimizer = torch.optim.LBFGS([flat], lr=1.0, max_iter=check_every, max_eval=int(check_every * 1.25),
+                                  history_size=history, tolerance_grad=0.0, tolerance_change=0.0,
+                                  line_search_fn="strong_wolfe")
+    setup = time.perf_counter() - start
+    iterations, metrics, accepted = 0, None, False
+    decision = torch.zeros(1, dtype=torch.int32, device=device)
+    while iterations < max_iterations:
+        optimizer.step(closure)
+        iterations = optimizer.state[optimizer._params[0]]["n_iter"]
+        metrics = accept(flat.data)
+        accepted = metrics[0] <= tol_uv and metrics[1] <= tol_uv and metrics[2] <= tol_p
+        decision.fill_(int(accepted or not all(math.isfinite(m) for m in metrics)))
+        if world > 1:
+            dist.broadcast(decision, 0)
+        if log and rank == 0:
+            log(json.dumps({"t": round(time.perf_counter() - start, 3), "iter": iterations, "evals": evaluations[0],
+                            "loss": float(loss_view), "rel_l2_uvp": metrics}))
+        if int(decision):
+            break
+        if time_limit is not None and time.perf_counter() - start > time_limit:
+            break
+    torch.cuda.synchronize(device)
+    wall = time.perf_counter() - start
+    del graph
+    return {"accepted": accepted, "wall_s": wall, "setup_s": setup, "iterations": iterations,
+            "evaluations": evaluations[0], "rel_l2_u": metrics[0], "rel_l2_v": metrics[1], "rel_l2_p": metrics[2],
+            "final_loss": float(loss_view), "n_gpus": world, "interior": interior, "boundary": boundary,
+            "widths": widths, "re": re, "seed": seed, "init_seed": init_seed}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--seed", type=int, default=1)
+    ap.add_argument("--init-seed", type=int, default=0)
+    ap.add_argument("--max-iterations", type=int, default=50000)
+    ap.add_argument("--check-every", type=int, default=100)
+    ap.add_argument("--boundary-weight", type=float, default=5.0)
+    ap.add_argument("--adam-steps", type=int, default=3000)
+    ap.add_argument("--history", type=int, default=50)
+    ap.add_argument("--time-limit", type=float, default=None)
+    ap.add_argument("--quiet", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    result = solve(seed=args.seed, init_seed=args.init_seed, max_iterations=args.max_iterations,
+                   check_every=args.check_every, boundary_weight=args.boundary_weight, adam_steps=args.adam_steps,
+                   history=args.history, time_limit=args.time_limit,
+                   log=None if args.quiet else lambda s: print(s, flush=True))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps(result), flush=True)
+
+
+if __name__ == "__main__":
+    main()

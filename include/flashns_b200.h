@@ -80,6 +80,14 @@ int flashns_b200_eval_marked(const flashns_b200_plan* plan, const double* coordi
                              double* gradient_and_loss, void* workspace, size_t workspace_bytes, cudaStream_t stream,
                              cudaEvent_t* events, int capacity, int* recorded);
 
+/* Forward-only fields at points (acceptance grids, validation).  The plan must have
+ * interior_points = 0 (all points ride the boundary-row path).  fields [points, F]:
+ * psi head with boundary_order 1 -> (u, v, p) = (psi_y, -psi_x, p); value rows -> raw outputs
+ * (F = outputs).  Replaces the reference's forward-only jets(x, W, b) evaluation
+ * (experiments/pinn_solver/problem.py:189-196). */
+int flashns_b200_fields(const flashns_b200_plan* plan, const double* coordinates, const double* parameters,
+                        double* fields, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
 /* No-allocation variant of flashns_b200_eval (no counterpart in the reference).
  * For callers that cannot allocate device memory -- a host runtime without a CUDA
  * allocator that binds this C ABI (Go, Java, JavaScript FFI), or a process that must not

@@ -137,3 +137,32 @@ def test_point_linearity_at_scale(cuda):
                                      head="psi", boundary_order=1, loss=NSLoss(0.05), device=cuda)(params))
     total = (parts[0] + parts[1]).cpu().numpy()
     assert rel_norm(total, full.cpu().numpy()) <= 1e-12
+
+
+@pytest.mark.parametrize("dim,order", [(2, 1), (2, 0), (3, 1)])
+def test_field_evaluator_matches_oracle(cuda, dim, order):
+    from flashns_b200.evaluator import FieldEvaluator
+    from oracle import residuals as RS
+    from oracle.evaluate import evaluate
+    widths = [dim, 64, 64, 2]
+    case = random_case(0, 57, widths, head="psi", boundary_order=order, seed=11)
+    fe = FieldEvaluator(torch.tensor(case["x"]), widths, head="psi", boundary_order=order, device=cuda)
+    got = fe(torch.tensor(flat(case["ws"], case["bs"])).to(cuda)).cpu().numpy()
+    _, _, parts = evaluate(case["x"], 0, case["pw"], case["bw"], case["target"], case["ws"], case["bs"], head="psi",
+                           boundary_order=order, return_parts=True)
+    qb = dim + 1 if order else 1
+    rows = parts["outputs"].reshape(57, qb, 2)
+    expect = RS.boundary_fields(rows, "psi", dim, order)
+    assert close_ratio(got, expect) <= 1.0
+
+
+def test_solver_runs_and_reduces_loss(cuda):
+    """A short solve on a small point set: the machinery (graph-captured closure, L-BFGS,
+    acceptance on a small grid) runs and the loss decreases."""
+    from flashns_b200.solver import solve
+    log = []
+    r = solve(interior=512, boundary=128, widths=(2, 32, 32, 2), max_iterations=40, check_every=20, grid=21,
+              device=cuda, log=log.append)
+    assert r["iterations"] >= 20 and r["evaluations"] >= 20
+    first = __import__("json").loads(log[0])["loss"]
+    assert r["final_loss"] < first
