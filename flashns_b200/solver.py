@@ -24,6 +24,7 @@ import torch
 import torch.distributed as dist
 
 from flashns_b200.evaluator import FieldEvaluator, PackedEvaluator, flat_parameters, xavier_normal
+from flashns_b200.lbfgs import DeviceLBFGS
 from flashns_b200.ns_seed import NSLoss
 from flashns_b200.problems import kovasznay, kovasznay_exact
 
@@ -53,7 +54,7 @@ class Acceptance:
 
 def solve(*, interior=16384, boundary=4096, widths=(2, 64, 64, 64, 64, 2), re=20.0, seed=1, init_seed=0,
           boundary_weight=5.0, tol_uv=1e-3, tol_p=1e-2, max_iterations=50000, check_every=100, history=50,
-          adam_steps=3000, adam_lr=1e-3, grid=201, device=None, log=None, time_limit=None):
+          adam_steps=3000, adam_lr=1e-3, grid=201, device=None, log=None, time_limit=None, optimizer="device"):
     start = time.perf_counter()
     world = dist.get_world_size() if dist.is_initialized() else 1
     rank = dist.get_rank() if dist.is_initialized() else 0
@@ -91,21 +92,29 @@ def solve(*, interior=16384, boundary=4096, widths=(2, 64, 64, 64, 64, 2), re=20
         flat.grad = grad_view
         return loss_view
 
+    setup = time.perf_counter() - start
     if adam_steps:
         # Adam phase on the same captured closure (experiments/pinn_solver/solve.py:137-149)
-        adam = torch.optim.Adam([flat], lr=adam_lr)
+        adam = torch.optim.Adam([flat], lr=adam_lr, fused=True)
         for _ in range(adam_steps):
             closure()
             adam.step()
-    optimizer = torch.optim.LBFGS([flat], lr=1.0, max_iter=check_every, max_eval=int(check_every * 1.25),
+    if optimizer == "device":
+        lbfgs = DeviceLBFGS(flat.data, grad_view, loss_view, graph.replay, history=history)
+    else:
+        lbfgs = torch.optim.LBFGS([flat], lr=1.0, max_iter=check_every, max_eval=int(check_every * 1.25),
                                   history_size=history, tolerance_grad=0.0, tolerance_change=0.0,
                                   line_search_fn="strong_wolfe")
-    setup = time.perf_counter() - start
     iterations, metrics, accepted = 0, None, False
     decision = torch.zeros(1, dtype=torch.int32, device=device)
     while iterations < max_iterations:
-        optimizer.step(closure)
-        iterations = optimizer.state[optimizer._params[0]]["n_iter"]
+        if optimizer == "device":
+            lbfgs.step(check_every)
+            iterations = lbfgs.iterations
+            evaluations[0] = adam_steps + lbfgs.evaluations
+        else:
+            lbfgs.step(closure)
+            iterations = lbfgs.state[lbfgs._params[0]]["n_iter"]
         metrics = accept(flat.data)
         accepted = metrics[0] <= tol_uv and metrics[1] <= tol_uv and metrics[2] <= tol_p
         decision.fill_(int(accepted or not all(math.isfinite(m) for m in metrics)))
@@ -121,7 +130,7 @@ def solve(*, interior=16384, boundary=4096, widths=(2, 64, 64, 64, 64, 2), re=20
     torch.cuda.synchronize(device)
     wall = time.perf_counter() - start
     del graph
-    return {"accepted": accepted, "wall_s": wall, "setup_s": setup, "iterations": iterations,
+    return {"accepted": accepted, "wall_s": wall, "setup_s": setup, "optimizer": optimizer, "iterations": iterations,
             "evaluations": evaluations[0], "rel_l2_u": metrics[0], "rel_l2_v": metrics[1], "rel_l2_p": metrics[2],
             "final_loss": float(loss_view), "n_gpus": world, "interior": interior, "boundary": boundary,
             "widths": widths, "re": re, "seed": seed, "init_seed": init_seed}
@@ -137,6 +146,7 @@ def main():
     ap.add_argument("--adam-steps", type=int, default=3000)
     ap.add_argument("--history", type=int, default=50)
     ap.add_argument("--time-limit", type=float, default=None)
+    ap.add_argument("--optimizer", choices=["device", "torch"], default="device")
     ap.add_argument("--quiet", action="store_true")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -147,7 +157,7 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     result = solve(seed=args.seed, init_seed=args.init_seed, max_iterations=args.max_iterations,
                    check_every=args.check_every, boundary_weight=args.boundary_weight, adam_steps=args.adam_steps,
-                   history=args.history, time_limit=args.time_limit,
+                   history=args.history, time_limit=args.time_limit, optimizer=args.optimizer,
                    log=None if args.quiet else lambda s: print(s, flush=True))
     if world > 1:
         dist.barrier()

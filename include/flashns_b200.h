@@ -162,6 +162,21 @@ int flashns_stable_dgrad_vjp(int dim, bool fused, const double* d, const double*
 int flashns_b200_residuals(int head, int dim, const double* jets, double nu, double* out, int64_t n,
                            cudaStream_t stream);
 
+/* Vector kernels of the device-resident L-BFGS (no reference counterpart: the reference
+ * uses torch.optim.LBFGS, experiments/pinn_solver/solve.py:150-167).
+ *   row_dots:      out[r] = rows[r] . v for r < k (rows [k][stride]); fixed-order reductions
+ *   lbfgs_combine: d = -(gamma g + sum_i cs[i] S[order[i]] + sum_i cy[i] Y[order[i]])
+ *   axpy:          x = x0 + t d
+ *   lbfgs_pair:    s = x - x0, y = g - g0 */
+int flashns_b200_row_dots(const double* rows, int64_t stride, int k, const double* v, double* out, int64_t n,
+                          cudaStream_t stream);
+int flashns_b200_lbfgs_combine(const double* S, const double* Y, int64_t stride, const int* order, int k,
+                               const double* cs, const double* cy, const double* g, double gamma, double* d, int64_t n,
+                               cudaStream_t stream);
+int flashns_b200_axpy(const double* x0, double t, const double* d, double* x, int64_t n, cudaStream_t stream);
+int flashns_b200_lbfgs_pair(const double* x, const double* x0, const double* g, const double* g0, double* s, double* y,
+                            int64_t n, cudaStream_t stream);
+
 /* shared memory the dense dgrad uses per block (0: this implementation stages none) */
 int flashns_stable_dgrad_shared_bytes(void);
 

@@ -161,7 +161,7 @@ def test_solver_runs_and_reduces_loss(cuda):
     acceptance on a small grid) runs and the loss decreases."""
     from flashns_b200.solver import solve
     log = []
-    r = solve(interior=512, boundary=128, widths=(2, 32, 32, 2), max_iterations=40, check_every=20, grid=21,
+    r = solve(interior=512, boundary=128, widths=(2, 32, 32, 2), max_iterations=40, check_every=20, grid=21, adam_steps=50,
               device=cuda, log=log.append)
     assert r["iterations"] >= 20 and r["evaluations"] >= 20
     first = __import__("json").loads(log[0])["loss"]
