@@ -520,9 +520,15 @@ __global__ void __launch_bounds__(MmaTile<DIM, CP>::THREADS, 1)
 
 // ----------------------------------------------------------------------------------
 // Fused backward of a square 64-wide hidden layer: the dgrad + jet VJP of bwd_layer and
-// the weight gradient dW_l = D_{l+1}^T H_l of the same tile.  Each streamed seed chunk
-// (16 output channels x the tile's rows) is the A operand of both contractions; the
-// tile's H_l rows sit in shared memory (same row permutation) as the wgrad B operand.
+// the weight gradient dW_l = D_{l+1}^T H_l of the same tile.  The tile's whole seed
+// D_{l+1} (both 32-channel chunks) and its H_l rows sit in shared memory in the same row
+// permutation; W_l stays resident for the kernel.  Per tile:
+//   dgrad over the two seed chunks (DMMA, accumulators in registers)
+//   wgrad over the tile's rows: seed chunks as A, the H_l tile as B
+//   -> the seed ring is free: the next tile's seed chunks are requested
+//   jet VJP epilogue, reading H_l from the shared tile, storing D_l
+//   -> the H_l tile is free: the next tile's H_l rows are requested
+// so the next tile's seed arrives during this epilogue and its H_l during the next dgrad.
 // dW_l accumulates in registers across the CTA's tiles and is written once per CTA, so
 // D_{l+1} and H_l are read from HBM once per layer instead of twice.
 constexpr int kFusedWidth = 64;
@@ -533,9 +539,10 @@ struct FusedTile : MmaTile<DIM, kFusedWidth, DIM == 2 ? 16 : 8> {};
 template <int DIM>
 constexpr size_t fused_smem_bytes() {
   using T = FusedTile<DIM>;
-  constexpr size_t ring = size_t(kStages) * (size_t(T::TR) * LDC + size_t(KC) * (kFusedWidth + 4));
+  constexpr size_t ring = size_t(kFusedWidth / KC) * size_t(T::TR) * LDC;  // the tile's seed chunks
+  constexpr size_t wres = size_t(kFusedWidth) * (kFusedWidth + 4);           // resident W_l
   constexpr size_t htile = size_t(T::TR) * (kFusedWidth + 4);
-  constexpr size_t a = sizeof(double) * (ring + htile + 2 * T::TR);
+  constexpr size_t a = sizeof(double) * (ring + wres + htile + 2 * T::TR);
   constexpr size_t red = sizeof(double) * (T::WR * kFusedWidth * (DIM + 1) + 8 * (kFusedWidth / 16) * 4 * 32);
   return a > red ? a : red;
 }
@@ -548,7 +555,7 @@ __global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
   constexpr int CP = kFusedWidth;
   using T = FusedTile<DIM>;
   using TL = Tiles<DIM, BO, T::TC>;
-  constexpr int S = T::S, TR = T::TR, Q = TL::Q, QB = TL::QB, LDA = CP + 4, LDH = CP + 4;
+  constexpr int S = T::S, TR = T::TR, Q = TL::Q, QB = TL::QB, LDW = CP + 4, LDH = CP + 4;
   constexpr int NK = CP / KC;  // seed chunks per tile
   constexpr int MK = KC / 16;  // m16 tiles of output channels per chunk
   constexpr int NM = CP / 16;  // m16 tiles of output channels
@@ -556,10 +563,11 @@ __global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
   // wgrad split: warp -> n8 tile (warp % 8) of dW columns and row share (warp / 8)
   constexpr int RS = T::NWARPS / 8, RROWS = TR / RS;
   static_assert(CP / 8 == 8 && T::NWARPS % 8 == 0 && RROWS % 16 == 0, "wgrad warp split");
+  static_assert(NK == 2, "commit-group accounting assumes two seed chunks per tile");
   extern __shared__ __align__(16) double smem[];
-  double* sB = smem;                     // seed chunks   [stage][TR][LDC]
-  double* sA = sB + kStages * TR * LDC;  // weight chunks [stage][KC][CP+4]
-  double* sH = sA + kStages * KC * LDA;  // H_l tile      [TR][CP+4]
+  double* sB = smem;               // seed chunks [NK][TR][LDC]
+  double* sW = sB + NK * TR * LDC;  // W_l         [CP][LDW] (row = output channel)
+  double* sH = sW + CP * LDW;       // H_l tile    [TR][LDH]
   int64_t* rowmap = reinterpret_cast<int64_t*>(sH + TR * LDH);  // [2][TR]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int wc = warp % T::WC, wr = warp / T::WC;
@@ -586,41 +594,46 @@ __global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
       rm[r] = TL::row(geo, nint, tile, tc, s);
     }
   };
-  auto load = [&](int kc, int stage, const int64_t* rm) {
-    double* dB = sB + stage * TR * LDC;
-    for (int i = tid; i < TR * (KC / 2); i += T::THREADS) {
-      const int r = i / (KC / 2), p = i % (KC / 2);
-      const int64_t gr = rm[r];
-      cp_async16(dB + r * LDC + 2 * p, dnext + (gr >= 0 ? gr : 0) * CP + kc * KC + 2 * p, gr >= 0);
-    }
-    double* dA = sA + stage * KC * LDA;
-    for (int i = tid; i < KC * (CP / 2); i += T::THREADS) {
-      const int r = i / (CP / 2), p = i % (CP / 2);
-      cp_async16(dA + r * LDA + 2 * p, w + int64_t(kc * KC + r) * CP + 2 * p, true);
+  auto load_seed = [&](const int64_t* rm) {  // one commit group per chunk
+#pragma unroll
+    for (int kc = 0; kc < NK; ++kc) {
+      double* dB = sB + kc * TR * LDC;
+      for (int i = tid; i < TR * (KC / 2); i += T::THREADS) {
+        const int r = i / (KC / 2), p = i % (KC / 2);
+        const int64_t gr = rm[r];
+        cp_async16(dB + r * LDC + 2 * p, dnext + (gr >= 0 ? gr : 0) * CP + kc * KC + 2 * p, gr >= 0);
+      }
+      cp_async_commit();
     }
   };
-  auto load_h = [&](const int64_t* rm) {
+  auto load_h = [&](const int64_t* rm) {  // one commit group
     for (int i = tid; i < TR * (CP / 2); i += T::THREADS) {
       const int r = i / (CP / 2), p = i % (CP / 2);
       const int64_t gr = rm[r];
       cp_async16(sH + r * LDH + 2 * p, hcur + (gr >= 0 ? gr : 0) * CP + 2 * p, gr >= 0);
     }
-  };
-  auto prologue = [&](const int64_t* rm) {  // group 0: H tile + chunk 0; group 1: chunk 1
-    load_h(rm);
-    load(0, 0, rm);
-    cp_async_commit();
-    load(1, 1, rm);
     cp_async_commit();
   };
+  // commit groups in flight at the top of a tile: [seed 0] [seed 1] [H] (the first tile's
+  // seed 0 group also carries W_l)
+  for (int i = tid; i < CP * (CP / 2); i += T::THREADS) {
+    const int r = i / (CP / 2), p = i % (CP / 2);
+    cp_async16(sW + r * LDW + 2 * p, w + int64_t(r) * CP + 2 * p, true);
+  }
   int buf = 0;
   if (int64_t(blockIdx.x) < ntiles) {
     fill_rowmap(blockIdx.x, rowmap);
     __syncthreads();
-    prologue(rowmap);
+    load_seed(rowmap);
+    load_h(rowmap);
+  } else {
+    cp_async_commit();
   }
   for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, buf ^= 1) {
     const int64_t* rm = rowmap + buf * TR;
+    int64_t* rn = rowmap + (buf ^ 1) * TR;
+    const bool has_next = tile + gridDim.x < ntiles;
+    if (has_next) fill_rowmap(tile + gridDim.x, rn);  // published by the barriers below
     double acc[T::MT][T::NT][4];
 #pragma unroll
     for (int i = 0; i < T::MT; ++i)
@@ -628,25 +641,22 @@ __global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
       for (int j = 0; j < T::NT; ++j)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0;
+    // dgrad: dH[ch][rows] += W_l^T[ch][cout chunk] D^T[cout chunk][rows]
 #pragma unroll
     for (int kc = 0; kc < NK; ++kc) {
-      cp_async_wait<kStages - 2>();
+      if (kc == 0) cp_async_wait<2>(); else cp_async_wait<1>();
       __syncthreads();
-      if (kc + kStages - 1 < NK) load(kc + kStages - 1, (kc + kStages - 1) % kStages, rm);
-      cp_async_commit();
-      const double* cD = sB + (kc % kStages) * TR * LDC;
-      const double* cB = cD + wr * (4 * S) * LDC;
-      const double* cA = sA + (kc % kStages) * KC * LDA + wc * T::WCH;
-      // dgrad: dH[ch][rows] += W_l^T[ch][cout chunk] D^T[cout chunk][rows]
+      const double* cB = sB + kc * TR * LDC + wr * (4 * S) * LDC;
+      const double* cA = sW + kc * KC * LDW + wc * T::WCH;
 #pragma unroll
       for (int kk = 0; kk < KC; kk += 8) {
         double a[T::MT][4];
 #pragma unroll
         for (int i = 0; i < T::MT; ++i) {
-          a[i][0] = cA[(kk + t) * LDA + 16 * i + g];
-          a[i][1] = cA[(kk + t) * LDA + 16 * i + g + 8];
-          a[i][2] = cA[(kk + t + 4) * LDA + 16 * i + g];
-          a[i][3] = cA[(kk + t + 4) * LDA + 16 * i + g + 8];
+          a[i][0] = cA[(kk + t) * LDW + 16 * i + g];
+          a[i][1] = cA[(kk + t) * LDW + 16 * i + g + 8];
+          a[i][2] = cA[(kk + t + 4) * LDW + 16 * i + g];
+          a[i][3] = cA[(kk + t + 4) * LDW + 16 * i + g + 8];
         }
 #pragma unroll
         for (int j = 0; j < T::NT; ++j) {
@@ -656,7 +666,13 @@ __global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
           for (int i = 0; i < T::MT; ++i) mma_m16n8k8(acc[i][j], a[i], b0, b1);
         }
       }
-      // wgrad: dW[cout chunk][8*wn..+8] += D^T[cout chunk][rows] H[rows][cin], rows of share wrs
+    }
+    cp_async_wait<0>();
+    __syncthreads();  // H_l tile visible
+    // wgrad: dW[cout][8*wn..+8] += D^T[cout][rows] H[rows][cin], rows of share wrs
+#pragma unroll
+    for (int kc = 0; kc < NK; ++kc) {
+      const double* cD = sB + kc * TR * LDC;
 #pragma unroll 4
       for (int r = wrs * RROWS; r < (wrs + 1) * RROWS; r += 8) {
         const double b0 = sH[(r + t) * LDH + 8 * wn + g];
@@ -672,15 +688,13 @@ __global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
         }
       }
     }
-    // ring and H tile are free: start the next tile, then run this tile's epilogue
-    __syncthreads();
-    if (tile + gridDim.x < ntiles) {
-      int64_t* rn = rowmap + (buf ^ 1) * TR;
-      fill_rowmap(tile + gridDim.x, rn);
-      __syncthreads();
-      prologue(rn);
-    }
+    __syncthreads();  // seed ring free
+    if (has_next) load_seed(rn);
+    // epilogue: jet VJP of this tile; H_l from the shared tile (row of slot s of thread
+    // column wr*4+t: the inverse of tile_slot)
     const int tc = wr * 4 + t;
+    const double* hrow = sH + (wr * (4 * S) + 2 * t) * LDH;
+    auto hslot = [&](int s, int ch) { return hrow[(8 * (s >> 1) + (s & 1)) * LDH + ch]; };
     const bool interior = tile < nint;
 #pragma unroll
     for (int i = 0; i < T::MT; ++i) {
@@ -694,9 +708,8 @@ __global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
           const int64_t p = tile * T::TC + tc;
           if (p < geo.ni) {
             double hv[Q], zb[Q];
-            const double* src = hcur + p * Q * CP + ch;
 #pragma unroll
-            for (int s = 0; s < Q; ++s) hv[s] = src[int64_t(s) * CP];
+            for (int s = 0; s < Q; ++s) hv[s] = hslot(s, ch);
             Jet<DIM, 3>::vjp(hv, a1cur[p * CP + ch], dh, zb);
             if constexpr (FIRST) {
               cacc[i][hh][DIM] += zb[0];
@@ -715,9 +728,8 @@ __global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
             const int64_t b = (tile - nint) * (int64_t(T::TC) * TL::PS) + int64_t(tc) * TL::PS + kq;
             if (b < geo.nb) {
               double hv[QB], zb[QB];
-              const double* src = hcur + (geo.ni * Q + b * QB) * CP + ch;
 #pragma unroll
-              for (int c = 0; c < QB; ++c) hv[c] = src[int64_t(c) * CP];
+              for (int c = 0; c < QB; ++c) hv[c] = hslot(kq * QB + c, ch);
               Jet<DIM, BO ? 1 : 0>::vjp(hv, a1cur[(geo.ni + b) * CP + ch], dh + kq * QB, zb);
               if constexpr (FIRST) {
                 cacc[i][hh][DIM] += zb[0];
@@ -738,6 +750,8 @@ __global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
         }
       }
     }
+    __syncthreads();  // H_l tile free
+    if (has_next) load_h(rn);
   }
   cp_async_wait<0>();
   // weight-gradient partial of this CTA: row shares combined in fixed order through smem
@@ -1222,20 +1236,25 @@ __global__ void pack_params(const double* __restrict__ flat, double* __restrict_
 }
 
 // Fixed-order reduction of the per-CTA / per-split partials.  A block covers 32
-// consecutive outputs (coalesced loads along i) and splits the partial index over its 8
-// warps; each thread keeps 4 interleaved accumulators, combined in a fixed order, so the
-// result is bitwise reproducible for a given plan.
-constexpr int kReduceCols = 32, kReduceRows = 8, kReduceAcc = 4;
+// consecutive outputs (coalesced loads along i) and splits the partial index over its 16
+// warps.  The partials were written by other SMs and sit in L2 or HBM, so the time is
+// load latency: each thread issues a batch of 8 independent loads before it adds any of
+// them, and combines them in a fixed tree, so the result is bitwise reproducible for a
+// given plan.
+constexpr int kReduceCols = 32, kReduceRows = 16, kReduceBatch = 8;
 
 __device__ __forceinline__ double strided_sum(const double* base, int64_t stride, int count, int start, int step) {
-  double acc[kReduceAcc] = {0.0, 0.0, 0.0, 0.0};
-  int c = start;
-  for (; c + (kReduceAcc - 1) * step < count; c += kReduceAcc * step) {
+  double total = 0.0;
+  for (int c = start; c < count; c += kReduceBatch * step) {
+    double v[kReduceBatch];
 #pragma unroll
-    for (int r = 0; r < kReduceAcc; ++r) acc[r] += base[int64_t(c + r * step) * stride];
+    for (int r = 0; r < kReduceBatch; ++r) {
+      const int cc = c + r * step;
+      v[r] = cc < count ? base[int64_t(cc) * stride] : 0.0;
+    }
+    total += ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
   }
-  for (int r = 0; c < count; c += step, ++r) acc[r] += base[int64_t(c) * stride];
-  return (acc[0] + acc[1]) + (acc[2] + acc[3]);
+  return total;
 }
 
 __global__ void __launch_bounds__(kReduceCols * kReduceRows)
