@@ -83,6 +83,14 @@ struct MmaTile {
   static_assert(CP % WCH == 0 && WC >= 1 && WARPS % WC == 0, "unsupported padded width");
 };
 
+// Forward tiles: the 2-D 64-wide layer runs two 8-warp CTAs per SM (80-row tiles), so one
+// CTA's jet epilogue and stores overlap the other's MMAs; the other widths run one
+// 16-warp (8-warp for 32 channels) CTA per SM.
+template <int DIM, int CP>
+struct FwdTile : MmaTile<DIM, CP, (DIM == 2 && CP == 64) ? 8 : (CP >= 64 ? 16 : 8)> {
+  static constexpr int MINB = (DIM == 2 && CP == 64) ? 2 : 1;  // CTAs per SM
+};
+
 // Interior tiles carry TC points (Q rows each); boundary tiles carry TC*PS points of
 // QB rows (QB = 1 value rows, QB = DIM+1 first-order rows).
 template <int DIM, int BO, int TC>
@@ -112,14 +120,14 @@ __device__ __forceinline__ void tile_slot(int r, int& tc, int& s) {
   s = 2 * j + (rem & 1);
 }
 
-template <int DIM, int CP>
-constexpr size_t fwd_group_doubles() {
-  using T = MmaTile<DIM, CP>;
-  return size_t(kStages) * (T::TR + CP) * LDC + 2 * T::TR;  // ring + rowmap[2][TR] (int64)
-}
-template <int DIM, int CP>
-constexpr size_t fwd_smem_bytes() {
-  return sizeof(double) * fwd_group_doubles<DIM, CP>();
+constexpr size_t kMaxSmem = 227 * 1024;  // dynamic shared memory per CTA on sm_100
+// forward: activation ring [stage][TR][LDC] + weights + rowmap[2][TR] (int64).  RES: W_l
+// resident for the whole kernel ([CP][kin+4]); otherwise one [CP][LDC] chunk per stage.
+template <int DIM, int CP, bool RES>
+constexpr size_t fwd_smem_bytes(int kin) {
+  using T = FwdTile<DIM, CP>;
+  return sizeof(double) * (size_t(kStages) * T::TR * LDC +
+                           (RES ? size_t(CP) * (kin + 4) : size_t(kStages) * CP * LDC) + 2 * size_t(T::TR));
 }
 template <int DIM, int CP>
 constexpr size_t bwd_group_doubles() {
@@ -141,19 +149,20 @@ __device__ __forceinline__ int64_t cta_iterations(int64_t ntiles) {
 
 // ----------------------------------------------------------------------------------
 // forward hidden layer: H_{l+1} = tanh_jet(H_l W_l^T + b_l on order-0 rows)
-template <int DIM, int CP, int BO>
-__global__ void __launch_bounds__(MmaTile<DIM, CP>::THREADS, 1)
+template <int DIM, int CP, int BO, bool RES>
+__global__ void __launch_bounds__(FwdTile<DIM, CP>::THREADS, FwdTile<DIM, CP>::MINB)
     fwd_layer(const double* __restrict__ hin, int kin, const double* __restrict__ w,
               const double* __restrict__ bias, double* __restrict__ hout, double* __restrict__ a1out,
               Geometry geo) {
-  using T = MmaTile<DIM, CP>;
+  using T = FwdTile<DIM, CP>;
   using TL = Tiles<DIM, BO, T::TC>;
   constexpr int S = T::S, TR = T::TR, Q = TL::Q, QB = TL::QB;
   extern __shared__ __align__(16) double smem[];
   const int tid = threadIdx.x;
-  double* sB = smem;   // activation chunks [stage][TR][LDC]
-  double* sA = sB + kStages * TR * LDC;                      // weight chunks     [stage][CP][LDC]
-  int64_t* rowmap = reinterpret_cast<int64_t*>(sA + kStages * CP * LDC);  // [2][TR]
+  double* sB = smem;                     // activation chunks [stage][TR][LDC]
+  double* sA = sB + kStages * TR * LDC;  // weights: resident [CP][kin+4] or chunks [stage][CP][LDC]
+  const int LDA = RES ? kin + 4 : LDC;
+  int64_t* rowmap = reinterpret_cast<int64_t*>(sA + (RES ? CP * LDA : kStages * CP * LDC));  // [2][TR]
   const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int wc = warp % T::WC, wr = warp / T::WC;
   const int nk = kin / KC;
@@ -175,10 +184,12 @@ __global__ void __launch_bounds__(MmaTile<DIM, CP>::THREADS, 1)
       const int64_t gr = rm[r];
       cp_async16(dB + r * LDC + 2 * p, hin + (gr >= 0 ? gr : 0) * kin + kc * KC + 2 * p, gr >= 0);
     }
-    double* dA = sA + stage * CP * LDC;
-    for (int i = tid; i < CP * (KC / 2); i += T::THREADS) {
-      const int r = i / (KC / 2), p = i % (KC / 2);
-      cp_async16(dA + r * LDC + 2 * p, w + int64_t(r) * kin + kc * KC + 2 * p, true);
+    if constexpr (!RES) {
+      double* dA = sA + stage * CP * LDC;
+      for (int i = tid; i < CP * (KC / 2); i += T::THREADS) {
+        const int r = i / (KC / 2), p = i % (KC / 2);
+        cp_async16(dA + r * LDC + 2 * p, w + int64_t(r) * kin + kc * KC + 2 * p, true);
+      }
     }
   };
   auto prologue = [&](const int64_t* rm) {
@@ -194,6 +205,13 @@ __global__ void __launch_bounds__(MmaTile<DIM, CP>::THREADS, 1)
   for (int i = 0; i < T::MT; ++i)
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) bias_r[i][hh] = bias[wc * T::WCH + 16 * i + 8 * hh + g];
+  if constexpr (RES) {  // W_l once per CTA: its own commit group, older than every chunk
+    for (int i = tid; i < CP * (kin / 2); i += T::THREADS) {
+      const int r = i / (kin / 2), p = i % (kin / 2);
+      cp_async16(sA + r * LDA + 2 * p, w + int64_t(r) * kin + 2 * p, true);
+    }
+    cp_async_commit();
+  }
   int buf = 0;
   if (iters > 0 && tile_of(0) < ntiles) {
     fill_rowmap(tile_of(0), rowmap);
@@ -218,16 +236,16 @@ __global__ void __launch_bounds__(MmaTile<DIM, CP>::THREADS, 1)
         if (kc + kStages - 1 < nk) load(kc + kStages - 1, (kc + kStages - 1) % kStages, rm);
         cp_async_commit();
         const double* cB = sB + (kc % kStages) * TR * LDC + wr * (4 * S) * LDC;
-        const double* cA = sA + (kc % kStages) * CP * LDC + wc * T::WCH * LDC;
+        const double* cA = RES ? sA + wc * T::WCH * LDA + kc * KC : sA + (kc % kStages) * CP * LDC + wc * T::WCH * LDC;
 #pragma unroll
         for (int kk = 0; kk < KC; kk += 8) {
           double a[T::MT][4];
 #pragma unroll
           for (int i = 0; i < T::MT; ++i) {
-            a[i][0] = cA[(16 * i + g) * LDC + kk + t];
-            a[i][1] = cA[(16 * i + g + 8) * LDC + kk + t];
-            a[i][2] = cA[(16 * i + g) * LDC + kk + t + 4];
-            a[i][3] = cA[(16 * i + g + 8) * LDC + kk + t + 4];
+            a[i][0] = cA[(16 * i + g) * LDA + kk + t];
+            a[i][1] = cA[(16 * i + g + 8) * LDA + kk + t];
+            a[i][2] = cA[(16 * i + g) * LDA + kk + t + 4];
+            a[i][3] = cA[(16 * i + g + 8) * LDA + kk + t + 4];
           }
 #pragma unroll
           for (int j = 0; j < T::NT; ++j) {
@@ -1343,21 +1361,36 @@ cudaError_t allow_smem(K kernel, size_t smem) {
 // ---- dispatch tables: runtime (dim, width, boundary order, head) -> template instance
 template <int DIM, int CP, int BO>
 struct FwdOps {
-  static cudaError_t setup(int& occ) {
-    constexpr size_t smem = fwd_smem_bytes<DIM, CP>();
-    cudaError_t e = allow_smem(fwd_layer<DIM, CP, BO>, smem);
-    occ = occupancy(fwd_layer<DIM, CP, BO>, smem, MmaTile<DIM, CP>::THREADS);
+  using T = FwdTile<DIM, CP>;
+  static constexpr int kMaxKin = 128;
+  // W_l resident whenever it fits next to the ring (every supported width today)
+  static bool resident(int kin) { return fwd_smem_bytes<DIM, CP, true>(kin) <= kMaxSmem; }
+  static size_t smem(int kin) {
+    return resident(kin) ? fwd_smem_bytes<DIM, CP, true>(kin) : fwd_smem_bytes<DIM, CP, false>(kin);
+  }
+  static cudaError_t setup(int& occ, int kin) {
+    // the attribute is per kernel and shared by all plans: allow the largest input width
+    cudaError_t e = cudaSuccess;
+    if (resident(kin)) {
+      const size_t cap = resident(kMaxKin) ? fwd_smem_bytes<DIM, CP, true>(kMaxKin) : kMaxSmem;
+      e = allow_smem(fwd_layer<DIM, CP, BO, true>, cap);
+      occ = occupancy(fwd_layer<DIM, CP, BO, true>, smem(kin), T::THREADS);
+    } else {
+      e = allow_smem(fwd_layer<DIM, CP, BO, false>, fwd_smem_bytes<DIM, CP, false>(kin));
+      occ = occupancy(fwd_layer<DIM, CP, BO, false>, smem(kin), T::THREADS);
+    }
     return e;
   }
   static int64_t tiles(const Geometry& g) {
-    using T = MmaTile<DIM, CP>;
     using TL = Tiles<DIM, BO, T::TC>;
     return TL::interior(g.ni) + TL::boundary(g.nb);
   }
   static void launch(int grid, cudaStream_t st, const double* hin, int kin, const double* w, const double* b,
                      double* hout, double* a1, Geometry g) {
-    fwd_layer<DIM, CP, BO><<<grid, MmaTile<DIM, CP>::THREADS, fwd_smem_bytes<DIM, CP>(), st>>>(hin, kin, w, b, hout,
-                                                                                              a1, g);
+    if (resident(kin))
+      fwd_layer<DIM, CP, BO, true><<<grid, T::THREADS, smem(kin), st>>>(hin, kin, w, b, hout, a1, g);
+    else
+      fwd_layer<DIM, CP, BO, false><<<grid, T::THREADS, smem(kin), st>>>(hin, kin, w, b, hout, a1, g);
   }
 };
 
@@ -1552,7 +1585,7 @@ int flashns_b200_plan_create(int dim, int head, int boundary_order, int n_affine
     const int cp = p->padded[l + 1];
     with_fwd<FwdOps>(dim, cp, boundary_order, [&](auto ops) {
       int occ = 1;
-      cudaError_t e = ops.setup(occ);
+      cudaError_t e = ops.setup(occ, p->padded[l]);
       if (e != cudaSuccess) err = e;
       const int64_t t = ops.tiles(p->geo);
       p->grid_fwd[l] = int(std::max<int64_t>(1, std::min<int64_t>(t, int64_t(occ) * p->sms)));
