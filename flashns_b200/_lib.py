@@ -46,7 +46,8 @@ SIGNATURES = {
     "flashns_stable_dgrad_shared_bytes": [],
 }
 
-KERNEL_KINDS = {0: "pack", 1: "first", 2: "forward", 3: "head", 4: "backward", 5: "wgrad", 6: "reduce"}
+KERNEL_KINDS = {0: "pack", 1: "first", 2: "forward", 3: "head", 4: "backward", 5: "wgrad", 6: "reduce",
+                7: "forward_head"}
 
 _library = None
 

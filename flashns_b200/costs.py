@@ -43,6 +43,12 @@ def fused_backward(widths, layer):
     return padded_width(widths[layer]) == 64 and padded_width(widths[layer + 1]) == 64
 
 
+def fused_head(widths):
+    """Mirror of the plan: a square 64-wide last hidden layer runs with the output layer."""
+    nh = len(widths) - 2
+    return nh >= 2 and padded_width(widths[nh]) == 64 and padded_width(widths[nh - 1]) == 64
+
+
 def evaluation_costs(widths, ni, nb, *, head, boundary_order):
     """Dict kind -> list of per-launch FLOPs, in launch order, plus totals."""
     dim = widths[0]
@@ -75,6 +81,8 @@ def evaluation_costs(widths, ni, nb, *, head, boundary_order):
             out["wgrad"].append(wgrad)
     if nh == 1:
         out["head"][0] += points * c1 * (2 * dim + 1)
+    if fused_head(widths):
+        out["forward_head"] = [out["forward"].pop() + out["head"].pop()]
     total = sum(sum(v) for v in out.values())
     gemm = 2 * rows * sum(a * b for a, b in zip(widths, widths[1:])) * 3 - 2 * rows * dim * c1
     return {"per_kind": out, "total": total, "gemm": gemm, "rows": rows}

@@ -1168,6 +1168,345 @@ constexpr size_t head_smem_bytes() {
 }
 
 // ----------------------------------------------------------------------------------
+// Last hidden layer fused with the output layer (64-wide layer L-1 -> L, L the last hidden
+// layer): the fwd_layer mainloop gives Z_L in registers; the epilogue forms H_L, stages it
+// in shared memory (natural row order, over the free activation ring), and runs the head
+// on the tile: Y = H_L W^T + b, the residual seeds, the output-layer gradients and the jet
+// VJP into layer L.  Only the seed D_L is stored: H_L and a1_L never reach HBM, and the
+// separate head launch goes away.  The head epilogue is long and latency-bound, so in 2-D
+// two 8-warp CTAs share an SM and one CTA's epilogue runs under the other's MMAs.
+template <int DIM>
+struct HeadTile : MmaTile<DIM, kFusedWidth, 8> {
+  static constexpr int MINB = DIM == 2 ? 2 : 1;  // 80-row tiles in 2-D, 160-row in 3-D
+};
+
+template <int DIM, int NF>
+constexpr size_t fwd_head_smem_bytes() {
+  using T = HeadTile<DIM>;
+  constexpr int CP = kFusedWidth;
+  constexpr size_t ring = size_t(kStages) * T::TR * LDC;
+  constexpr size_t stage = size_t(T::TR) * (CP + 1);  // H_L tile, aliases the ring
+  constexpr size_t main = (ring > stage ? ring : stage) + size_t(CP) * (CP + 4) + 2 * size_t(T::TR);
+  constexpr size_t head = size_t(NF) * CP + 2 * size_t(T::TR) * NF;
+  return sizeof(double) * (main + head);
+}
+
+template <int DIM, int BO, int HEAD>
+__global__ void __launch_bounds__(HeadTile<DIM>::THREADS, HeadTile<DIM>::MINB)
+    fwd_head(const double* __restrict__ hin, const double* __restrict__ w, const double* __restrict__ bias,
+             const double* __restrict__ wL, const double* __restrict__ bL, const double* __restrict__ pde_w,
+             const double* __restrict__ bnd_w, const double* __restrict__ target, double nu, double gamma, double bc,
+             double* __restrict__ dL, double* __restrict__ head_partial, Geometry geo) {
+  constexpr int CP = kFusedWidth, KIN = kFusedWidth;
+  using T = HeadTile<DIM>;
+  using TL = Tiles<DIM, BO, T::TC>;
+  constexpr int S = T::S, TR = T::TR, Q = TL::Q, QB = TL::QB, PS = TL::PS;
+  constexpr int NF = HeadTraits<HEAD>::NF;
+  constexpr int NFT = (HEAD == FLASHNS_B200_HEAD_PSI && BO) ? 3 : NF;  // boundary target fields
+  constexpr int LDA = KIN + 4, LDH = CP + 1;
+  constexpr int PARTIAL = NF * CP + NF + 1 + CP;  // dW_L | db_L | loss | db_{L-1}
+  constexpr int NK = KIN / KC;
+  // output-layer gradient: each (o, c) is owned by RQ threads, one per interleaved row share
+  constexpr int RQ = T::THREADS / (NF * CP) > 0 ? T::THREADS / (NF * CP) : 1;
+  constexpr int WPT = (NF * CP * RQ + T::THREADS - 1) / T::THREADS;
+  static_assert(NK == 2 && kStages == 2, "one chunk of lookahead per tile");
+  constexpr int RING = (kStages * TR * LDC > TR * LDH) ? kStages * TR * LDC : TR * LDH;
+  extern __shared__ __align__(16) double smem[];
+  double* sB = smem;         // activation chunks [stage][TR][LDC] during the mainloop
+  double* sH = smem;         // H_L tile [TR][CP+1], natural row order, during the epilogue
+  double* sA = sB + RING;    // W_{L-1} resident  [CP][KIN+4]
+  int64_t* rowmap = reinterpret_cast<int64_t*>(sA + CP * LDA);  // [2][TR]
+  double* sW = reinterpret_cast<double*>(rowmap + 2 * TR);      // W_L [NF][CP]
+  double* sY = sW + NF * CP;             // Y  [TR][NF]
+  double* sD = sY + TR * NF;             // dY [TR][NF]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  const int wc = warp % T::WC, wr = warp / T::WC;
+  const int64_t nint = TL::interior(geo.ni);
+  const int64_t ntiles = nint + TL::boundary(geo.nb);
+  for (int i = tid; i < NF * CP; i += T::THREADS) sW[i] = wL[i];
+  auto fill_rowmap = [&](int64_t tile, int64_t* rm) {
+    for (int r = tid; r < TR; r += T::THREADS) {
+      int tc, s;
+      tile_slot<S>(r, tc, s);
+      rm[r] = TL::row(geo, nint, tile, tc, s);
+    }
+  };
+  auto load = [&](int kc, int stage, const int64_t* rm) {
+    double* dB = sB + stage * TR * LDC;
+    for (int i = tid; i < TR * (KC / 2); i += T::THREADS) {
+      const int r = i / (KC / 2), p = i % (KC / 2);
+      const int64_t gr = rm[r];
+      cp_async16(dB + r * LDC + 2 * p, hin + (gr >= 0 ? gr : 0) * KIN + kc * KC + 2 * p, gr >= 0);
+    }
+  };
+  double bias_r[2];
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) bias_r[hh] = bias[wc * T::WCH + 8 * hh + g];
+  for (int i = tid; i < CP * (KIN / 2); i += T::THREADS) {  // W_{L-1}: its own (oldest) group
+    const int r = i / (KIN / 2), p = i % (KIN / 2);
+    cp_async16(sA + r * LDA + 2 * p, w + int64_t(r) * KIN + 2 * p, true);
+  }
+  cp_async_commit();
+  double wacc[WPT];
+#pragma unroll
+  for (int k = 0; k < WPT; ++k) wacc[k] = 0.0;
+  double bacc = 0.0, lacc = 0.0, cacc[2] = {0.0, 0.0};
+  int buf = 0;
+  if (int64_t(blockIdx.x) < ntiles) {
+    fill_rowmap(blockIdx.x, rowmap);
+    __syncthreads();
+    load(0, 0, rowmap);
+    cp_async_commit();
+  }
+  for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, buf ^= 1) {
+    const int64_t* rm = rowmap + buf * TR;
+    int64_t* rn = rowmap + (buf ^ 1) * TR;
+    const bool has_next = tile + gridDim.x < ntiles;
+    if (has_next) fill_rowmap(tile + gridDim.x, rn);  // published by the barriers below
+    double acc[T::NT][4];
+#pragma unroll
+    for (int j = 0; j < T::NT; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[j][e] = 0.0;
+#pragma unroll
+    for (int kc = 0; kc < NK; ++kc) {
+      cp_async_wait<0>();
+      __syncthreads();
+      if (kc + 1 < NK) load(kc + 1, (kc + 1) % kStages, rm);
+      cp_async_commit();
+      const double* cB = sB + (kc % kStages) * TR * LDC + wr * (4 * S) * LDC;
+      const double* cA = sA + wc * T::WCH * LDA + kc * KC;
+#pragma unroll
+      for (int kk = 0; kk < KC; kk += 8) {
+        double a[4];
+        a[0] = cA[g * LDA + kk + t];
+        a[1] = cA[(g + 8) * LDA + kk + t];
+        a[2] = cA[g * LDA + kk + t + 4];
+        a[3] = cA[(g + 8) * LDA + kk + t + 4];
+#pragma unroll
+        for (int j = 0; j < T::NT; ++j) {
+          const double b0 = cB[(8 * j + g) * LDC + kk + t];
+          const double b1 = cB[(8 * j + g) * LDC + kk + t + 4];
+          mma_m16n8k8(acc[j], a, b0, b1);
+        }
+      }
+    }
+    __syncthreads();  // ring free: it holds the H_L tile until the end of the epilogue
+    const int tc = wr * 4 + t;
+    const bool interior = tile < nint;
+    const int64_t p0 = interior ? tile * T::TC : (tile - nint) * (int64_t(T::TC) * PS);
+    const int64_t left = interior ? geo.ni - p0 : geo.nb - p0;
+    const int npts = int(left < (interior ? T::TC : T::TC * PS) ? left : (interior ? T::TC : T::TC * PS));
+    const int step = interior ? Q : QB;
+    const int nrows = npts * step;
+    // 1. bias on the order-0 coefficient, stable tanh jet; H_L into the shared tile
+    double a1r[2][PS];
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int ch = wc * T::WCH + 8 * hh + g;
+      double z[S];
+#pragma unroll
+      for (int s = 0; s < S; ++s) z[s] = acc[s >> 1][2 * hh + (s & 1)];
+      if (interior) {
+        if (tc < npts) {
+          double hv[Q];
+          z[0] += bias_r[hh];
+          Jet<DIM, 3>::fwd(z, hv, a1r[hh][0]);
+#pragma unroll
+          for (int s = 0; s < Q; ++s) sH[(tc * Q + s) * LDH + ch] = hv[s];
+        }
+      } else {
+#pragma unroll
+        for (int kq = 0; kq < PS; ++kq) {
+          const int lp = tc * PS + kq;
+          if (lp < npts) {
+            double zz[QB], hv[QB];
+#pragma unroll
+            for (int c = 0; c < QB; ++c) zz[c] = z[kq * QB + c];
+            zz[0] += bias_r[hh];
+            Jet<DIM, BO ? 1 : 0>::fwd(zz, hv, a1r[hh][kq]);
+#pragma unroll
+            for (int c = 0; c < QB; ++c) sH[(lp * QB + c) * LDH + ch] = hv[c];
+          }
+        }
+      }
+    }
+    __syncthreads();
+    // 2. outputs Y[r][o] = H[r].W_L[o] (+ b_L on order-0 rows)
+    for (int i = tid; i < nrows * NF; i += T::THREADS) {
+      const int r = i / NF, o = i % NF;
+      const double* hr = sH + r * LDH;
+      const double* wo = sW + o * CP;
+      double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
+#pragma unroll 4
+      for (int c = 0; c < CP; c += 4) {
+        s0 += hr[c] * wo[c];
+        s1 += hr[c + 1] * wo[c + 1];
+        s2 += hr[c + 2] * wo[c + 2];
+        s3 += hr[c + 3] * wo[c + 3];
+      }
+      double y = (s0 + s1) + (s2 + s3);
+      if (r % step == 0) y += bL[o];
+      sY[r * NF + o] = y;
+    }
+    __syncthreads();
+    // 3. residual seeds, one point per thread
+    if (interior) {
+      if (tid < npts) {
+        double y[Q * NF], dy[Q * NF];
+#pragma unroll
+        for (int k = 0; k < Q * NF; ++k) y[k] = sY[tid * Q * NF + k];
+        lacc += interior_seed<DIM, HEAD>(y, pde_w[p0 + tid], nu, gamma, dy);
+#pragma unroll
+        for (int k = 0; k < Q * NF; ++k) sD[tid * Q * NF + k] = dy[k];
+      }
+    } else {
+      for (int pt = tid; pt < npts; pt += T::THREADS) {
+        const int64_t b = p0 + pt;
+        const double* yr = sY + pt * QB * NF;
+        double* dr = sD + pt * QB * NF;
+#pragma unroll
+        for (int k = 0; k < QB * NF; ++k) dr[k] = 0.0;
+        double f[NFT];
+        if constexpr (BO == 0) {
+#pragma unroll
+          for (int o = 0; o < NF; ++o) f[o] = yr[o];
+        } else {
+          f[0] = yr[unit_row<DIM>(1) * NF + 0];   // u = psi_y
+          f[1] = -yr[unit_row<DIM>(0) * NF + 0];  // v = -psi_x
+          f[2] = yr[1];                           // p
+        }
+        double gsd[NFT];
+#pragma unroll
+        for (int o = 0; o < NFT; ++o) {
+          const double err = f[o] - target[b * NFT + o];
+          const double wgt = bnd_w[b * NFT + o];
+          lacc += bc * wgt * err * err;
+          gsd[o] = 2.0 * bc * wgt * err;
+        }
+        if constexpr (BO == 0) {
+#pragma unroll
+          for (int o = 0; o < NF; ++o) dr[o] = gsd[o];
+        } else {
+          dr[unit_row<DIM>(1) * NF + 0] = gsd[0];
+          dr[unit_row<DIM>(0) * NF + 0] = -gsd[1];
+          dr[1] = gsd[2];
+        }
+      }
+    }
+    __syncthreads();
+    // 4. output-layer gradients: dW_L[o][c] += sum_r dY[r][o] H[r][c]; db_L over order-0 rows
+#pragma unroll
+    for (int k = 0; k < WPT; ++k) {
+      const int idx = tid + k * T::THREADS;
+      if (idx < NF * CP * RQ) {
+        const int rq = idx / (NF * CP), o = (idx % (NF * CP)) / CP, c = idx % CP;
+        double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
+        int r = rq;
+        for (; r + 3 * RQ < nrows; r += 4 * RQ) {
+          s0 += sD[r * NF + o] * sH[r * LDH + c];
+          s1 += sD[(r + RQ) * NF + o] * sH[(r + RQ) * LDH + c];
+          s2 += sD[(r + 2 * RQ) * NF + o] * sH[(r + 2 * RQ) * LDH + c];
+          s3 += sD[(r + 3 * RQ) * NF + o] * sH[(r + 3 * RQ) * LDH + c];
+        }
+        for (; r < nrows; r += RQ) s0 += sD[r * NF + o] * sH[r * LDH + c];
+        wacc[k] += (s0 + s1) + (s2 + s3);
+      }
+    }
+    if (tid < NF)
+      for (int r = 0; r < nrows; r += step) bacc += sD[r * NF + tid];
+    // 5. dgrad through W_L and the jet VJP of layer L on the owned (point, channel) pairs
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int ch = wc * T::WCH + 8 * hh + g;
+      if (interior) {
+        if (tc < npts) {
+          double hv[Q], dh[Q], zb[Q];
+#pragma unroll
+          for (int s = 0; s < Q; ++s) {
+            const int r = tc * Q + s;
+            double v = 0.0;
+#pragma unroll
+            for (int o = 0; o < NF; ++o) v += sD[r * NF + o] * sW[o * CP + ch];
+            dh[s] = v;
+            hv[s] = sH[r * LDH + ch];
+          }
+          Jet<DIM, 3>::vjp(hv, a1r[hh][0], dh, zb);
+          double* dst = dL + (p0 + tc) * Q * CP + ch;
+#pragma unroll
+          for (int s = 0; s < Q; ++s) dst[int64_t(s) * CP] = zb[s];
+          cacc[hh] += zb[0];
+        }
+      } else {
+#pragma unroll
+        for (int kq = 0; kq < PS; ++kq) {
+          const int lp = tc * PS + kq;
+          if (lp < npts) {
+            double hv[QB], dh[QB], zb[QB];
+#pragma unroll
+            for (int c = 0; c < QB; ++c) {
+              const int r = lp * QB + c;
+              double v = 0.0;
+#pragma unroll
+              for (int o = 0; o < NF; ++o) v += sD[r * NF + o] * sW[o * CP + ch];
+              dh[c] = v;
+              hv[c] = sH[r * LDH + ch];
+            }
+            Jet<DIM, BO ? 1 : 0>::vjp(hv, a1r[hh][kq], dh, zb);
+            double* dst = dL + (geo.ni * Q + (p0 + lp) * QB) * CP + ch;
+#pragma unroll
+            for (int c = 0; c < QB; ++c) dst[int64_t(c) * CP] = zb[c];
+            cacc[hh] += zb[0];
+          }
+        }
+      }
+    }
+    __syncthreads();  // staging free: the next tile's first chunk
+    if (has_next) {
+      load(0, 0, rn);
+      cp_async_commit();
+    }
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+  // per-CTA partials, fixed-order reductions
+  double* out = head_partial + int64_t(blockIdx.x) * PARTIAL;
+  if (tid < NF) out[NF * CP + tid] = bacc;
+  double* red = smem;                 // [THREADS] loss partials
+  double* cred = smem + T::THREADS;  // [WR][CP] bias partials of layer L-1
+  double* wred = cred + T::WR * CP;   // [RQ][NF*CP] output-layer gradient shares
+#pragma unroll
+  for (int k = 0; k < WPT; ++k) {
+    const int idx = tid + k * T::THREADS;
+    if (idx < NF * CP * RQ) wred[idx] = wacc[k];
+  }
+  red[tid] = lacc;
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    double v = cacc[hh];
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    if (t == 0) cred[wr * CP + wc * T::WCH + 8 * hh + g] = v;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    double sum = 0.0;
+    for (int i = 0; i < T::THREADS; ++i) sum += red[i];
+    out[NF * CP + NF] = sum;
+  }
+  for (int c = tid; c < CP; c += T::THREADS) {
+    double sum = 0.0;
+    for (int r = 0; r < T::WR; ++r) sum += cred[r * CP + c];
+    out[NF * CP + NF + 1 + c] = sum;
+  }
+  for (int idx = tid; idx < NF * CP; idx += T::THREADS) {
+    double sum = 0.0;
+    for (int r = 0; r < RQ; ++r) sum += wred[r * NF * CP + idx];
+    out[idx] = sum;
+  }
+}
+
+// ----------------------------------------------------------------------------------
 // first layer: coordinates -> affine jet -> stable tanh jet
 template <int DIM, int BO>
 __global__ void __launch_bounds__(kThreads)
@@ -1332,6 +1671,7 @@ struct flashns_b200_plan {
   int grid_fwd[kMaxAffine], grid_bwd[kMaxAffine], grid_head, grid_first, grid_coord;
   int wg_splits[kMaxAffine];
   bool fused[kMaxAffine];  // backward layer l runs bwd_fused (dgrad + VJP + wgrad)
+  bool fused_head;         // the last forward layer and the output layer run as fwd_head
   int64_t wg_rows[kMaxAffine];
   int wg_bm[kMaxAffine], wg_bn[kMaxAffine];
 };
@@ -1464,6 +1804,38 @@ struct HeadOps {
         h, a1, w, b, pw, bw, tg, nu, gm, bc, dl, x, cpart, hpart, g);
   }
 };
+
+template <int DIM, int BO, int HEAD>
+struct FwdHeadOps {
+  static constexpr int NF = HeadTraits<HEAD>::NF;
+  static cudaError_t setup(int& occ) {
+    constexpr size_t smem = fwd_head_smem_bytes<DIM, NF>();
+    static_assert(smem <= kMaxSmem, "fused head tile exceeds shared memory");
+    cudaError_t e = allow_smem(fwd_head<DIM, BO, HEAD>, smem);
+    occ = occupancy(fwd_head<DIM, BO, HEAD>, smem, HeadTile<DIM>::THREADS);
+    return e;
+  }
+  static int64_t tiles(const Geometry& g) {
+    using TL = Tiles<DIM, BO, HeadTile<DIM>::TC>;
+    return TL::interior(g.ni) + TL::boundary(g.nb);
+  }
+  static void launch(int grid, cudaStream_t st, const double* hin, const double* w, const double* b,
+                     const double* wl, const double* bl, const double* pw, const double* bw, const double* tg,
+                     double nu, double gm, double bc, double* dl, double* hpart, Geometry g) {
+    fwd_head<DIM, BO, HEAD><<<grid, HeadTile<DIM>::THREADS, fwd_head_smem_bytes<DIM, NF>(), st>>>(
+        hin, w, b, wl, bl, pw, bw, tg, nu, gm, bc, dl, hpart, g);
+  }
+};
+
+template <typename F>
+bool with_fwd_head(int dim, int bo, int head, F&& f) {
+#define FLASHNS_CASE(D, B, H) \
+  if (dim == D && bo == B && head == H) { f(FwdHeadOps<D, B, H>{}); return true; }
+  FLASHNS_CASE(2, 0, 0) FLASHNS_CASE(2, 0, 1) FLASHNS_CASE(2, 1, 1)
+  FLASHNS_CASE(3, 0, 1) FLASHNS_CASE(3, 1, 1)
+#undef FLASHNS_CASE
+  return false;
+}
 
 // Generic visitor over the runtime parameters.
 template <template <int, int, int> class Ops, typename F>
@@ -1621,6 +1993,9 @@ int flashns_b200_plan_create(int dim, int head, int boundary_order, int n_affine
     const bool ok = nh == 1 ? with_head<true>(dim, p->padded[nh], boundary_order, head, f)
                             : with_head<false>(dim, p->padded[nh], boundary_order, head, f);
     if (!ok) { delete p; return int(cudaErrorInvalidValue); }
+    // square 64-wide last hidden layer: fuse it with the output layer (one launch, no H_L)
+    p->fused_head = nh >= 2 && p->padded[nh] == kFusedWidth && p->padded[nh - 1] == kFusedWidth &&
+                    with_fwd_head(dim, boundary_order, head, f);
   }
   if (err != cudaSuccess) { delete p; return int(err); }
   p->grid_first = int(std::max<int64_t>(1, std::min<int64_t>((p->points * p->padded[1] + kThreads - 1) / kThreads,
@@ -1773,7 +2148,7 @@ static int run_eval(const flashns_b200_plan* p, const double* coordinates, const
     int r = first_launch(p->dim, p->bo, p->grid_first, stream, coordinates, ws + L0.w_buf, ws + L0.b_buf,
                          ws + p->off_h[1], ws + p->off_a1[1], p->padded[1], g);
     if (r) return r;
-    for (int l = 1; l < nh; ++l) {
+    for (int l = 1; l < nh - (p->fused_head ? 1 : 0); ++l) {
       const LayerDesc& L = tab.l[l];
       mark();
       with_fwd<FwdOps>(p->dim, p->padded[l + 1], p->bo, [&](auto ops) {
@@ -1782,7 +2157,17 @@ static int run_eval(const flashns_b200_plan* p, const double* coordinates, const
       });
       if ((e = cudaGetLastError()) != cudaSuccess) return int(e);
     }
-    {
+    if (p->fused_head) {
+      const LayerDesc& L = tab.l[nh - 1];
+      const LayerDesc& H = tab.l[nh];
+      mark();
+      with_fwd_head(p->dim, p->bo, p->head, [&](auto ops) {
+        ops.launch(p->grid_head, stream, ws + p->off_h[nh - 1], ws + L.w_buf, ws + L.b_buf, ws + H.w_buf,
+                   ws + H.b_buf, pde_weights, boundary_weights, target, p->nu, p->gamma, p->bc,
+                   ws + p->off_d[nh % 2], ws + p->off_head, g);
+      });
+      if ((e = cudaGetLastError()) != cudaSuccess) return int(e);
+    } else {
       const LayerDesc& L = tab.l[nh];
       auto f = [&](auto ops) {
         ops.launch(p->grid_head, stream, ws + p->off_h[nh], ws + p->off_a1[nh], ws + L.w_buf, ws + L.b_buf,
@@ -1857,8 +2242,8 @@ int flashns_b200_plan_launch_kinds(const flashns_b200_plan* p, int* kinds, int c
   k.push_back(FLASHNS_B200_KERNEL_PACK);
   if (p->rows > 0) {
     k.push_back(FLASHNS_B200_KERNEL_FIRST);
-    for (int l = 1; l < nh; ++l) k.push_back(FLASHNS_B200_KERNEL_FORWARD);
-    k.push_back(FLASHNS_B200_KERNEL_HEAD);
+    for (int l = 1; l < nh - (p->fused_head ? 1 : 0); ++l) k.push_back(FLASHNS_B200_KERNEL_FORWARD);
+    k.push_back(p->fused_head ? FLASHNS_B200_KERNEL_FORWARD_HEAD : FLASHNS_B200_KERNEL_HEAD);
     for (int l = nh - 1; l >= 1; --l) {
       k.push_back(FLASHNS_B200_KERNEL_BACKWARD);
       if (!p->fused[l]) k.push_back(FLASHNS_B200_KERNEL_WGRAD);

@@ -55,6 +55,7 @@ int flashns_b200_plan_launch_count(const flashns_b200_plan* plan, int* count);
 #define FLASHNS_B200_KERNEL_BACKWARD 4 /* DMMA dgrad + jet-VJP epilogue (+ coordinate contraction) */
 #define FLASHNS_B200_KERNEL_WGRAD 5    /* DMMA weight gradient, split over rows */
 #define FLASHNS_B200_KERNEL_REDUCE 6   /* fixed-order partial reduction -> grad, loss */
+#define FLASHNS_B200_KERNEL_FORWARD_HEAD 7 /* last 64-wide forward layer fused with the output layer */
 int flashns_b200_plan_launch_kinds(const flashns_b200_plan* plan, int* kinds, int capacity, int* count);
 
 /* One complete loss + parameter-gradient evaluation.  Replaces
