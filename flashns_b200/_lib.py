@@ -19,6 +19,8 @@ SIGNATURES = {
     "flashns_b200_plan_workspace_bytes": [_c_ptr, ctypes.POINTER(_c_size)],
     "flashns_b200_plan_parameter_count": [_c_ptr, ctypes.POINTER(_c_i64)],
     "flashns_b200_plan_launch_count": [_c_ptr, ctypes.POINTER(_c_int)],
+    "flashns_b200_device_fault": [ctypes.POINTER(_c_int), _c_int],
+    "flashns_b200_wait_selftest": [ctypes.c_uint, _c_ptr, _c_ptr],
     "flashns_b200_eval": [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_ptr],
     "flashns_b200_eval_marked": [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_ptr,
                                  _c_ptr, _c_int, ctypes.POINTER(_c_int)],

@@ -34,6 +34,20 @@ constexpr int kStages = 2;
 constexpr int KC = 32;       // k-chunk (doubles) per pipeline stage
 constexpr int LDC = KC + 4;  // padded chunk row: conflict-free FP64 fragment loads
 constexpr int kMaxAffine = 16;
+// set by a kernel whose bounded wait on a bulk copy gave up (read by flashns_b200_device_fault)
+__device__ int g_device_fault = 0;
+
+// Self-test of the bounded wait: an mbarrier that nothing arrives at.  The wait gives up
+// after `spins` polls, raises the fault word and the kernel returns normally.
+__global__ void wait_timeout_probe(unsigned spins, int* gave_up) {
+  __shared__ uint64_t bar;
+  mbar_init(&bar, 1);
+  __syncwarp();
+  const bool ok = mbar_wait(&bar, 0, spins);
+  if (!ok) atomicExch(&g_device_fault, 1);
+  *gave_up = ok ? 0 : 1;
+  mbar_inval(&bar);
+}
 
 struct Geometry {
   int64_t ni, nb;  // interior (full-jet) and boundary points
@@ -84,10 +98,10 @@ struct MmaTile {
 };
 
 // Forward tiles: the 2-D 64-wide layer runs two 8-warp CTAs per SM (80-row tiles), so one
-// CTA's jet epilogue and stores overlap the other's MMAs; the other widths run one
-// 16-warp (8-warp for 32 channels) CTA per SM.
+// CTA's jet epilogue and stores overlap the other's MMAs; 128-wide layers run one 16-warp
+// CTA per SM, the rest one 8-warp CTA.  Every shape keeps W_l (up to 128 inputs) resident.
 template <int DIM, int CP>
-struct FwdTile : MmaTile<DIM, CP, (DIM == 2 && CP == 64) ? 8 : (CP >= 64 ? 16 : 8)> {
+struct FwdTile : MmaTile<DIM, CP, CP >= 128 ? 16 : 8> {
   static constexpr int MINB = (DIM == 2 && CP == 64) ? 2 : 1;  // CTAs per SM
 };
 
@@ -121,13 +135,13 @@ __device__ __forceinline__ void tile_slot(int r, int& tc, int& s) {
 }
 
 constexpr size_t kMaxSmem = 227 * 1024;  // dynamic shared memory per CTA on sm_100
-// forward: activation ring [stage][TR][LDC] + weights + rowmap[2][TR] (int64).  RES: W_l
-// resident for the whole kernel ([CP][kin+4]); otherwise one [CP][LDC] chunk per stage.
-template <int DIM, int CP, bool RES>
+constexpr int kMaxWidth = 128;            // widest padded layer
+// forward: activation ring [stage][TR][LDC] + resident W_l [CP][kin+4] + rowmap[2][TR]
+// (int64) + one mbarrier per stage
+template <int DIM, int CP>
 constexpr size_t fwd_smem_bytes(int kin) {
   using T = FwdTile<DIM, CP>;
-  return sizeof(double) * (size_t(kStages) * T::TR * LDC +
-                           (RES ? size_t(CP) * (kin + 4) : size_t(kStages) * CP * LDC) + 2 * size_t(T::TR));
+  return sizeof(double) * (size_t(kStages) * T::TR * LDC + size_t(CP) * (kin + 4) + 2 * size_t(T::TR) + kStages);
 }
 template <int DIM, int CP>
 constexpr size_t bwd_group_doubles() {
@@ -148,8 +162,11 @@ __device__ __forceinline__ int64_t cta_iterations(int64_t ntiles) {
 }
 
 // ----------------------------------------------------------------------------------
-// forward hidden layer: H_{l+1} = tanh_jet(H_l W_l^T + b_l on order-0 rows)
-template <int DIM, int CP, int BO, bool RES>
+// forward hidden layer: H_{l+1} = tanh_jet(H_l W_l^T + b_l on order-0 rows).  W_l stays
+// resident in shared memory; activation rows stream through a two-stage ring of 32-column
+// chunks as bulk copies (TMA engine, one row per copy), each stage completing on its own
+// mbarrier.  The next tile's first chunk is requested before this tile's epilogue.
+template <int DIM, int CP, int BO>
 __global__ void __launch_bounds__(FwdTile<DIM, CP>::THREADS, FwdTile<DIM, CP>::MINB)
     fwd_layer(const double* __restrict__ hin, int kin, const double* __restrict__ w,
               const double* __restrict__ bias, double* __restrict__ hout, double* __restrict__ a1out,
@@ -157,19 +174,19 @@ __global__ void __launch_bounds__(FwdTile<DIM, CP>::THREADS, FwdTile<DIM, CP>::M
   using T = FwdTile<DIM, CP>;
   using TL = Tiles<DIM, BO, T::TC>;
   constexpr int S = T::S, TR = T::TR, Q = TL::Q, QB = TL::QB;
+  constexpr int NIS = TR < T::THREADS ? TR : T::THREADS;  // threads issuing row copies
   extern __shared__ __align__(16) double smem[];
   const int tid = threadIdx.x;
+  const int LDA = kin + 4;
   double* sB = smem;                     // activation chunks [stage][TR][LDC]
-  double* sA = sB + kStages * TR * LDC;  // weights: resident [CP][kin+4] or chunks [stage][CP][LDC]
-  const int LDA = RES ? kin + 4 : LDC;
-  int64_t* rowmap = reinterpret_cast<int64_t*>(sA + (RES ? CP * LDA : kStages * CP * LDC));  // [2][TR]
+  double* sA = sB + kStages * TR * LDC;  // W_l, resident     [CP][kin+4]
+  int64_t* rowmap = reinterpret_cast<int64_t*>(sA + CP * LDA);   // [2][TR]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(rowmap + 2 * TR);  // [kStages] stage full
   const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int wc = warp % T::WC, wr = warp / T::WC;
   const int nk = kin / KC;
   const int64_t nint = TL::interior(geo.ni);
   const int64_t ntiles = nint + TL::boundary(geo.nb);
-  const int64_t iters = cta_iterations(ntiles);
-  auto tile_of = [&](int64_t k) { return k * gridDim.x + blockIdx.x; };
   auto fill_rowmap = [&](int64_t tile, int64_t* rm) {
     for (int r = tid; r < TR; r += T::THREADS) {
       int tc, s;
@@ -177,26 +194,22 @@ __global__ void __launch_bounds__(FwdTile<DIM, CP>::THREADS, FwdTile<DIM, CP>::M
       rm[r] = TL::row(geo, nint, tile, tc, s);
     }
   };
+  // chunk kc of the tile's rows into `stage`: rows past the end of a segment are zero-filled
   auto load = [&](int kc, int stage, const int64_t* rm) {
+    if (tid >= NIS) return;
     double* dB = sB + stage * TR * LDC;
-    for (int i = tid; i < TR * (KC / 2); i += T::THREADS) {
-      const int r = i / (KC / 2), p = i % (KC / 2);
-      const int64_t gr = rm[r];
-      cp_async16(dB + r * LDC + 2 * p, hin + (gr >= 0 ? gr : 0) * kin + kc * KC + 2 * p, gr >= 0);
-    }
-    if constexpr (!RES) {
-      double* dA = sA + stage * CP * LDC;
-      for (int i = tid; i < CP * (KC / 2); i += T::THREADS) {
-        const int r = i / (KC / 2), p = i % (KC / 2);
-        cp_async16(dA + r * LDC + 2 * p, w + int64_t(r) * kin + kc * KC + 2 * p, true);
+    unsigned bytes = 0;
+    for (int r = tid; r < TR; r += T::THREADS) {
+      if (rm[r] >= 0) {
+        bytes += KC * sizeof(double);
+      } else {
+        for (int j = 0; j < KC; ++j) dB[r * LDC + j] = 0.0;
       }
     }
-  };
-  auto prologue = [&](const int64_t* rm) {
-#pragma unroll
-    for (int s = 0; s < kStages - 1; ++s) {
-      if (s < nk) load(s, s, rm);
-      cp_async_commit();
+    mbar_arrive_expect_tx(&bars[stage], bytes);
+    for (int r = tid; r < TR; r += T::THREADS) {
+      const int64_t gr = rm[r];
+      if (gr >= 0) bulk_g2s(dB + r * LDC, hin + gr * kin + kc * KC, KC * sizeof(double), &bars[stage]);
     }
   };
   // a thread's channels are fixed for the whole kernel: load their biases once
@@ -205,23 +218,24 @@ __global__ void __launch_bounds__(FwdTile<DIM, CP>::THREADS, FwdTile<DIM, CP>::M
   for (int i = 0; i < T::MT; ++i)
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) bias_r[i][hh] = bias[wc * T::WCH + 16 * i + 8 * hh + g];
-  if constexpr (RES) {  // W_l once per CTA: its own commit group, older than every chunk
-    for (int i = tid; i < CP * (kin / 2); i += T::THREADS) {
-      const int r = i / (kin / 2), p = i % (kin / 2);
-      cp_async16(sA + r * LDA + 2 * p, w + int64_t(r) * kin + 2 * p, true);
-    }
-    cp_async_commit();
+  for (int i = tid; i < CP * (kin / 2); i += T::THREADS) {  // W_l once per CTA
+    const int r = i / (kin / 2), p = i % (kin / 2);
+    cp_async16(sA + r * LDA + 2 * p, w + int64_t(r) * kin + 2 * p, true);
   }
+  cp_async_commit();
+  if (tid == 0)
+    for (int st = 0; st < kStages; ++st) mbar_init(&bars[st], NIS);
+  if (int64_t(blockIdx.x) < ntiles) fill_rowmap(blockIdx.x, rowmap);
+  cp_async_wait<0>();
+  __syncthreads();  // W_l, barriers and the first rowmap visible
+  if (int64_t(blockIdx.x) < ntiles) load(0, 0, rowmap);
+  unsigned parity = 0;  // bit st: phase parity of the next completion of stage st
   int buf = 0;
-  if (iters > 0 && tile_of(0) < ntiles) {
-    fill_rowmap(tile_of(0), rowmap);
-    __syncthreads();
-    prologue(rowmap);
-  }
-  for (int64_t k = 0; k < iters; ++k, buf ^= 1) {
-    const int64_t tile = tile_of(k);
-    const bool valid = tile < ntiles;
+  for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, buf ^= 1) {
     const int64_t* rm = rowmap + buf * TR;
+    int64_t* rn = rowmap + (buf ^ 1) * TR;
+    const bool has_next = tile + gridDim.x < ntiles;
+    if (has_next) fill_rowmap(tile + gridDim.x, rn);  // published by the barriers below
     double acc[T::MT][T::NT][4];
 #pragma unroll
     for (int i = 0; i < T::MT; ++i)
@@ -229,43 +243,40 @@ __global__ void __launch_bounds__(FwdTile<DIM, CP>::THREADS, FwdTile<DIM, CP>::M
       for (int j = 0; j < T::NT; ++j)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0;
-    if (valid) {
-      for (int kc = 0; kc < nk; ++kc) {
-        cp_async_wait<kStages - 2>();
-        __syncthreads();
-        if (kc + kStages - 1 < nk) load(kc + kStages - 1, (kc + kStages - 1) % kStages, rm);
-        cp_async_commit();
-        const double* cB = sB + (kc % kStages) * TR * LDC + wr * (4 * S) * LDC;
-        const double* cA = RES ? sA + wc * T::WCH * LDA + kc * KC : sA + (kc % kStages) * CP * LDC + wc * T::WCH * LDC;
+    for (int kc = 0; kc < nk; ++kc) {
+      const int stage = kc % kStages;
+      const bool ok = mbar_wait(&bars[stage], (parity >> stage) & 1u);
+      parity ^= 1u << stage;
+      // the barrier also retires the reads of the stage refilled next
+      if (__syncthreads_or(!ok)) {
+        if (tid == 0) atomicExch(&g_device_fault, 1);
+        return;
+      }
+      if (kc + kStages - 1 < nk) load(kc + kStages - 1, (kc + kStages - 1) % kStages, rm);
+      const double* cB = sB + stage * TR * LDC + wr * (4 * S) * LDC;
+      const double* cA = sA + wc * T::WCH * LDA + kc * KC;
 #pragma unroll
-        for (int kk = 0; kk < KC; kk += 8) {
-          double a[T::MT][4];
+      for (int kk = 0; kk < KC; kk += 8) {
+        double a[T::MT][4];
 #pragma unroll
-          for (int i = 0; i < T::MT; ++i) {
-            a[i][0] = cA[(16 * i + g) * LDA + kk + t];
-            a[i][1] = cA[(16 * i + g + 8) * LDA + kk + t];
-            a[i][2] = cA[(16 * i + g) * LDA + kk + t + 4];
-            a[i][3] = cA[(16 * i + g + 8) * LDA + kk + t + 4];
-          }
+        for (int i = 0; i < T::MT; ++i) {
+          a[i][0] = cA[(16 * i + g) * LDA + kk + t];
+          a[i][1] = cA[(16 * i + g + 8) * LDA + kk + t];
+          a[i][2] = cA[(16 * i + g) * LDA + kk + t + 4];
+          a[i][3] = cA[(16 * i + g + 8) * LDA + kk + t + 4];
+        }
 #pragma unroll
-          for (int j = 0; j < T::NT; ++j) {
-            const double b0 = cB[(8 * j + g) * LDC + kk + t];
-            const double b1 = cB[(8 * j + g) * LDC + kk + t + 4];
+        for (int j = 0; j < T::NT; ++j) {
+          const double b0 = cB[(8 * j + g) * LDC + kk + t];
+          const double b1 = cB[(8 * j + g) * LDC + kk + t + 4];
 #pragma unroll
-            for (int i = 0; i < T::MT; ++i) mma_m16n8k8(acc[i][j], a[i], b0, b1);
-          }
+          for (int i = 0; i < T::MT; ++i) mma_m16n8k8(acc[i][j], a[i], b0, b1);
         }
       }
     }
-    // the ring is free: start the next tile's first chunks, then run this tile's epilogue
+    // the ring is free: request the next tile's first chunk, then run this tile's epilogue
     __syncthreads();
-    if (k + 1 < iters && tile_of(k + 1) < ntiles) {
-      int64_t* rn = rowmap + (buf ^ 1) * TR;
-      fill_rowmap(tile_of(k + 1), rn);
-      __syncthreads();
-      prologue(rn);
-    }
-    if (!valid) continue;
+    if (has_next) load(0, 0, rn);
     // epilogue: bias on the order-0 coefficient, stable tanh jet, store H and a1
     const int tc = wr * 4 + t;
     const bool interior = tile < nint;
@@ -309,7 +320,8 @@ __global__ void __launch_bounds__(FwdTile<DIM, CP>::THREADS, FwdTile<DIM, CP>::M
       }
     }
   }
-  cp_async_wait<0>();
+  if (tid == 0 && int64_t(blockIdx.x) < ntiles)  // all waits retired before the last ring barrier
+    for (int st = 0; st < kStages; ++st) mbar_inval(&bars[st]);
 }
 
 // ----------------------------------------------------------------------------------
@@ -1702,23 +1714,11 @@ cudaError_t allow_smem(K kernel, size_t smem) {
 template <int DIM, int CP, int BO>
 struct FwdOps {
   using T = FwdTile<DIM, CP>;
-  static constexpr int kMaxKin = 128;
-  // W_l resident whenever it fits next to the ring (every supported width today)
-  static bool resident(int kin) { return fwd_smem_bytes<DIM, CP, true>(kin) <= kMaxSmem; }
-  static size_t smem(int kin) {
-    return resident(kin) ? fwd_smem_bytes<DIM, CP, true>(kin) : fwd_smem_bytes<DIM, CP, false>(kin);
-  }
+  static_assert(fwd_smem_bytes<DIM, CP>(kMaxWidth) <= kMaxSmem, "resident W_l must fit for every input width");
   static cudaError_t setup(int& occ, int kin) {
     // the attribute is per kernel and shared by all plans: allow the largest input width
-    cudaError_t e = cudaSuccess;
-    if (resident(kin)) {
-      const size_t cap = resident(kMaxKin) ? fwd_smem_bytes<DIM, CP, true>(kMaxKin) : kMaxSmem;
-      e = allow_smem(fwd_layer<DIM, CP, BO, true>, cap);
-      occ = occupancy(fwd_layer<DIM, CP, BO, true>, smem(kin), T::THREADS);
-    } else {
-      e = allow_smem(fwd_layer<DIM, CP, BO, false>, fwd_smem_bytes<DIM, CP, false>(kin));
-      occ = occupancy(fwd_layer<DIM, CP, BO, false>, smem(kin), T::THREADS);
-    }
+    cudaError_t e = allow_smem(fwd_layer<DIM, CP, BO>, fwd_smem_bytes<DIM, CP>(kMaxWidth));
+    occ = occupancy(fwd_layer<DIM, CP, BO>, fwd_smem_bytes<DIM, CP>(kin), T::THREADS);
     return e;
   }
   static int64_t tiles(const Geometry& g) {
@@ -1727,10 +1727,7 @@ struct FwdOps {
   }
   static void launch(int grid, cudaStream_t st, const double* hin, int kin, const double* w, const double* b,
                      double* hout, double* a1, Geometry g) {
-    if (resident(kin))
-      fwd_layer<DIM, CP, BO, true><<<grid, T::THREADS, smem(kin), st>>>(hin, kin, w, b, hout, a1, g);
-    else
-      fwd_layer<DIM, CP, BO, false><<<grid, T::THREADS, smem(kin), st>>>(hin, kin, w, b, hout, a1, g);
+    fwd_layer<DIM, CP, BO><<<grid, T::THREADS, fwd_smem_bytes<DIM, CP>(kin), st>>>(hin, kin, w, b, hout, a1, g);
   }
 };
 
@@ -2111,6 +2108,22 @@ int flashns_b200_plan_parameter_count(const flashns_b200_plan* plan, int64_t* co
   if (!plan || !count) return int(cudaErrorInvalidValue);
   *count = plan->tab.params;
   return int(cudaSuccess);
+}
+
+int flashns_b200_device_fault(int* fault, int clear) {
+  if (!fault) return int(cudaErrorInvalidValue);
+  cudaError_t e = cudaMemcpyFromSymbol(fault, g_device_fault, sizeof(int));
+  if (e == cudaSuccess && clear) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_device_fault, &zero, sizeof(int));
+  }
+  return int(e);
+}
+
+int flashns_b200_wait_selftest(unsigned spins, int* gave_up, cudaStream_t stream) {
+  if (!gave_up || spins == 0 || spins > (1u << 17)) return int(cudaErrorInvalidValue);
+  wait_timeout_probe<<<1, 1, 0, stream>>>(spins, gave_up);
+  return int(cudaGetLastError());
 }
 
 int flashns_b200_plan_launch_count(const flashns_b200_plan* plan, int* count) {

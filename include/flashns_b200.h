@@ -58,6 +58,17 @@ int flashns_b200_plan_launch_count(const flashns_b200_plan* plan, int* count);
 #define FLASHNS_B200_KERNEL_FORWARD_HEAD 7 /* last 64-wide forward layer fused with the output layer */
 int flashns_b200_plan_launch_kinds(const flashns_b200_plan* plan, int* kinds, int capacity, int* count);
 
+/* Device fault word of the current device: nonzero once a kernel gave up a bounded wait on
+ * one of its own asynchronous copies (the kernel then returned without finishing, and the
+ * outputs of that evaluation are invalid).  Synchronous; clear != 0 resets the word.
+ * No reference counterpart (the reference kernels have no in-kernel waits). */
+int flashns_b200_device_fault(int* fault, int clear);
+/* Launches one thread that waits on an mbarrier nothing arrives at, bounded by `spins`
+ * polls (1..131072, each suspending at most 10 us).  It writes 1 to the device int
+ * `gave_up` and raises the fault word when the bound ran out, so callers can check that a
+ * stuck wait ends with an error instead of a hang.  No reference counterpart. */
+int flashns_b200_wait_selftest(unsigned spins, int* gave_up, cudaStream_t stream);
+
 /* One complete loss + parameter-gradient evaluation.  Replaces
  * PackedPINN.__call__(weights, biases) -> (loss, [dW_0..dW_L, db_0..db_L])
  * (src/flashns/pinn_packed.py:93-191) together with the Engine's flattening

@@ -166,3 +166,35 @@ def test_solver_runs_and_reduces_loss(cuda):
     assert r["iterations"] >= 20 and r["evaluations"] >= 20
     first = __import__("json").loads(log[0])["loss"]
     assert r["final_loss"] < first
+
+
+@pytest.mark.gpu
+def test_bounded_wait_reports_instead_of_hanging(cuda):
+    """An mbarrier that nothing arrives at: the kernel's bounded wait gives up, raises the
+    device fault word and returns, and the context stays usable; normal evaluations leave
+    the word clear."""
+    import ctypes
+    from flashns_b200 import _lib
+    lib = _lib.library()
+    fault = ctypes.c_int(-1)
+    _lib.check(lib.flashns_b200_device_fault(ctypes.byref(fault), 1), "device_fault")
+    from flashns_b200.ns_seed import NSLoss
+    widths = [2, 64, 64, 64, 2]
+    case = random_case(64, 16, widths, head="psi", boundary_order=1, seed=3)
+    loss = NSLoss(0.05, 0.0, 2.0)
+    run(case, widths, "psi", 1, loss, cuda)
+    torch.cuda.synchronize()
+    _lib.check(lib.flashns_b200_device_fault(ctypes.byref(fault), 0), "device_fault")
+    assert fault.value == 0
+    gave_up = torch.full((1,), -1, dtype=torch.int32, device=cuda)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    _lib.check(lib.flashns_b200_wait_selftest(200, ctypes.c_void_p(gave_up.data_ptr()), stream), "wait_selftest")
+    torch.cuda.synchronize()
+    assert int(gave_up.item()) == 1
+    _lib.check(lib.flashns_b200_device_fault(ctypes.byref(fault), 1), "device_fault")
+    assert fault.value == 1
+    _lib.check(lib.flashns_b200_device_fault(ctypes.byref(fault), 0), "device_fault")
+    assert fault.value == 0
+    _, out = run(case, widths, "psi", 1, loss, cuda)  # the context still works
+    assert np.isfinite(out).all()
+    np.testing.assert_allclose(out, oracle(case, "psi", 1, loss), rtol=1e-9, atol=1e-12)
