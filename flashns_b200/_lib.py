@@ -29,10 +29,15 @@ SIGNATURES = {
     "flashns_b200_eval_static": [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr],
     "flashns_b200_fields": [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_ptr],
     "flashns_b200_row_dots": [_c_ptr, _c_i64, _c_int, _c_ptr, _c_ptr, _c_i64, _c_ptr],
-    "flashns_b200_lbfgs_combine": [_c_ptr, _c_ptr, _c_i64, _c_ptr, _c_int, _c_ptr, _c_ptr, _c_ptr, _c_dbl, _c_ptr,
-                                   _c_i64, _c_ptr],
     "flashns_b200_axpy": [_c_ptr, _c_dbl, _c_ptr, _c_ptr, _c_i64, _c_ptr],
-    "flashns_b200_lbfgs_pair": [_c_ptr] * 6 + [_c_i64, _c_ptr],
+    "flashns_b200_lbfgs_pair_slot": [_c_ptr] * 6 + [_c_i64, _c_ptr, _c_i64, _c_ptr],
+    "flashns_b200_lbfgs_ring_dots": [_c_ptr, _c_ptr, _c_i64, _c_int, _c_ptr, _c_ptr, _c_int, _c_ptr, _c_i64, _c_ptr],
+    "flashns_b200_lbfgs_commit": [_c_ptr, _c_ptr, _c_ptr, _c_int, _c_ptr, _c_ptr],
+    "flashns_b200_lbfgs_coefficients": [_c_ptr, _c_ptr, _c_ptr, _c_int, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr],
+    "flashns_b200_lbfgs_direction": [_c_ptr, _c_ptr, _c_i64] + [_c_ptr] * 6 + [_c_i64, _c_ptr],
+    "flashns_b200_lbfgs_save": [_c_ptr] * 6 + [_c_i64, _c_ptr],
+    "flashns_b200_lbfgs_step_point": [_c_ptr] * 4 + [_c_i64, _c_ptr],
+    "flashns_b200_adam_step": [_c_ptr] * 4 + [_c_i64, _c_dbl, _c_dbl, _c_dbl, _c_dbl, _c_i64, _c_ptr],
     "flashns_b200_residuals": [_c_int, _c_int, _c_ptr, _c_dbl, _c_ptr, _c_i64, _c_ptr],
     # reference-ABI hooks (experiments/pinn_v8/native.py:26-51, experiments/cuda_jet_h100/gpu.py)
     "flashns_v8_activation": [_c_int, _c_int] + [_c_ptr] * 5 + [_c_i64, _c_i64, _c_int, _c_ptr],

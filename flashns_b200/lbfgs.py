@@ -1,7 +1,10 @@
 """Device-resident L-BFGS with a strong-Wolfe line search.
 
-The vectors (parameters, gradients, the curvature history S, Y) stay on the GPU; each
-iteration moves only O(history) numbers between host and device.
+Everything of the quasi-Newton update lives on the GPU: the parameters, gradients, the
+ring of curvature pairs (S, Y), their products S^T Y and Y^T Y, the pair count and the
+coefficients.  One iteration launches a fixed sequence of small kernels (``csrc/lbfgs.cu``)
+and reads back four scalars (f0, g0.d, f, g.d) once per line-search trial, so the common
+iteration (first trial accepted) costs one evaluation and one host round trip.
 
 * Search direction: the compact representation of the L-BFGS inverse Hessian (Byrd,
   Nocedal and Schnabel, "Representations of quasi-Newton matrices and their use in
@@ -10,23 +13,28 @@ iteration moves only O(history) numbers between host and device.
       H g = gamma g + S cs + Y cy,   u = R^-1 (S^T g),
       cs = R^-T ((D + gamma Y^T Y) u - gamma Y^T g),   cy = -gamma u,
 
-  where R is the upper triangle of S^T Y (oldest to newest) and D its diagonal.  The
-  device computes S^T g and Y^T g (one block per dot product) and the combination; the
-  host solves the two k x k triangular systems.
+  where R is the upper triangle of S^T Y (oldest to newest) and D its diagonal; the two
+  triangular solves run in one CUDA block.  A new pair (s, y) is kept only when
+  s.y > 1e-12 y.y; when the history is full the oldest pair drops out.
 * Step length: strong Wolfe conditions (c1 = 1e-4, c2 = 0.9) by bracketing and zoom with
   cubic interpolation (Nocedal and Wright, Numerical Optimization, 2nd ed., Algorithms
-  3.5 and 3.6, eq. 3.59).  Each trial sets x = x0 + t d on the device, replays the
+  3.5 and 3.6, eq. 3.59).  Each trial sets x = x0 + t d on the device, runs the
   evaluation and reads back (f, g.d).
+* Graph mode (``capture_evaluate`` given): the whole first trial of an iteration (pair
+  update, direction, step, evaluation, read-back) and every further trial are two CUDA
+  graphs; the host writes the step t and the pair flag into pinned memory that the graphs
+  read, so an iteration is one graph launch and one synchronize.
 """
 
 import ctypes
 import math
 
-import numpy as np
 import torch
-from scipy.linalg import solve_triangular
 
 from flashns_b200 import _lib
+
+_GAMMA, _F0, _GD0, _F, _GD, _K, _T = range(7)
+_MAX_HISTORY = 128
 
 
 def _p(t):
@@ -37,106 +45,142 @@ class DeviceLBFGS:
     """Minimize with ``evaluate()`` writing the loss into ``loss_view`` and the gradient
     into ``grad_view`` at the parameters currently in ``x`` (e.g. a CUDA-graph replay)."""
 
-    def __init__(self, x, grad_view, loss_view, evaluate, *, history=50, c1=1e-4, c2=0.9, max_evals_per_search=25):
+    def __init__(self, x, grad_view, loss_view, evaluate, *, history=50, c1=1e-4, c2=0.9, max_evals_per_search=25,
+                 capture_evaluate=None):
+        if not 1 <= history <= _MAX_HISTORY:
+            raise ValueError(f"history must be in 1..{_MAX_HISTORY}")
+        if x.dtype != torch.float64 or not x.is_cuda or not x.is_contiguous():
+            raise ValueError("contiguous CUDA FP64 parameters required")
         self.x, self.g, self.f = x, grad_view, loss_view
         self.evaluate = evaluate
         self.n = x.numel()
         self.m, self.c1, self.c2, self.max_ls = history, c1, c2, max_evals_per_search
+        self.slots = history + 1
         dev = x.device
         z = lambda *shape: torch.zeros(*shape, dtype=torch.float64, device=dev)
         self.x0, self.g0, self.d = z(self.n), z(self.n), z(self.n)
-        self.S, self.Y = z(self.m, self.n), z(self.m, self.n)
-        self.dots = z(2 * self.m + 2)
-        self.coef = z(2 * self.m)
-        self.order_dev = torch.zeros(self.m, dtype=torch.int32, device=dev)
-        self.host = torch.zeros(2 * self.m + 2, dtype=torch.float64).pin_memory()
-        self.order = []  # physical rows, oldest first
-        self.SY = np.zeros((self.m, self.m))  # SY[a, b] = s_a . y_b (a older than or equal to b)
-        self.YY = np.zeros((self.m, self.m))
+        self.S, self.Y = z(self.slots, self.n), z(self.slots, self.n)
+        self.SY, self.YY = z(self.slots, self.slots), z(self.slots, self.slots)
+        self.dots = z(2 * self.slots)
+        self.coef = z(2 * _MAX_HISTORY)
+        self.order = torch.zeros(_MAX_HISTORY, dtype=torch.int32, device=dev)
+        self.state = torch.zeros(4, dtype=torch.int32, device=dev)  # k, spare slot, have_pair, 0
+        self.scal = z(8)                                             # gamma, f0, g0.d, f, g.d, k
+        self.host = torch.zeros(8, dtype=torch.float64).pin_memory()
+        self.t_host = torch.zeros(1, dtype=torch.float64).pin_memory()
+        self.flag_host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self.capture_evaluate = capture_evaluate  # records the evaluation kernels (graph mode)
+        self.graphs = None
         self.evaluations = 0
         self.iterations = 0
         self.lib = _lib.library()
-        self.stream = torch.cuda.current_stream(dev)
         self.fk = None
 
     # ---------------------------------------------------------------- device helpers
     def _s(self):
         return ctypes.c_void_p(torch.cuda.current_stream(self.x.device).cuda_stream)
 
-    def _row_dots(self, rows, k, v, out):
-        _lib.check(self.lib.flashns_b200_row_dots(_p(rows), self.n, k, _p(v), _p(out), self.n, self._s()), "row_dots")
+    def _call(self, name, *args):
+        _lib.check(getattr(self.lib, "flashns_b200_" + name)(*args, self._s()), name)
 
-    def _read(self, count):
-        self.host[:count].copy_(self.dots[:count], non_blocking=True)
+    def _read(self):
+        self.host.copy_(self.scal, non_blocking=True)
         torch.cuda.current_stream(self.x.device).synchronize()
-        return self.host[:count].numpy().copy()
+        return self.host.tolist()
 
-    def _phi(self, t):
-        """Evaluate at x0 + t d; return (f, g.d)."""
-        _lib.check(self.lib.flashns_b200_axpy(_p(self.x0), float(t), _p(self.d), _p(self.x), self.n, self._s()), "axpy")
+    def _eval(self):
         self.evaluate()
         self.evaluations += 1
-        self._row_dots(self.g, 1, self.d, self.dots[1:])
-        self.dots[0].copy_(self.f, non_blocking=True)
-        f, gd = self._read(2)
-        return float(f), float(gd)
+
+    def _trial_kernels(self, evaluate):
+        """x = x0 + t d (t from scal), evaluation, scal[F] = f, scal[GD] = g.d."""
+        self._call("lbfgs_step_point", _p(self.x0), _p(self.scal), _p(self.d), _p(self.x), self.n)
+        evaluate()
+        self.scal[_F:_F + 1].copy_(self.f.reshape(1))
+        self._call("row_dots", _p(self.g), self.n, 1, _p(self.d), _p(self.scal[_GD:]), self.n)
+
+    def _build_graphs(self):
+        dev = self.x.device
+        stream = torch.cuda.Stream(dev)
+        stream.wait_stream(torch.cuda.current_stream(dev))
+        first, trial = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(first, stream=stream):
+            self.state[2:3].copy_(self.flag_host, non_blocking=True)
+            self._direction(set_flag=False)
+            self.scal[_T:_T + 1].copy_(self.t_host, non_blocking=True)
+            self._trial_kernels(self.capture_evaluate)
+            self.host.copy_(self.scal, non_blocking=True)
+        with torch.cuda.graph(trial, stream=stream):
+            self.scal[_T:_T + 1].copy_(self.t_host, non_blocking=True)
+            self._trial_kernels(self.capture_evaluate)
+            self.host.copy_(self.scal, non_blocking=True)
+        torch.cuda.current_stream(dev).wait_stream(stream)
+        self.graphs = (first, trial)
+
+    def _replay(self, graph, t):
+        self.t_host[0] = t
+        graph.replay()
+        self.evaluations += 1
+        torch.cuda.current_stream(self.x.device).synchronize()
+        h = self.host.tolist()
+        return h[_F], h[_GD], h
+
+    def _phi(self, t):
+        """Evaluate at x0 + t d; return (f, g.d, the scalars read back)."""
+        if self.graphs is not None:
+            return self._replay(self.graphs[1], t)
+        self.scal[_T:_T + 1].fill_(float(t))
+        self._trial_kernels(self._eval)
+        h = self._read()
+        return h[_F], h[_GD], h
+
+    def _first_trial(self, t, pair):
+        """Direction (folding in the last pair when `pair`) and the trial at t."""
+        if self.graphs is not None:
+            self.flag_host[0] = int(pair)
+            return self._replay(self.graphs[0], t)
+        if pair:
+            self.state[2:3].fill_(1)
+        self._direction()
+        return self._phi(t)
 
     # ---------------------------------------------------------------- direction
-    def _direction(self):
-        k = len(self.order)
-        if k == 0:
-            self.d.copy_(self.g).neg_()
-            return
-        rows = self.order
-        self._row_dots(self.S, k, self.g, self.dots)   # physical row r -> dots[r]
-        self._row_dots(self.Y, k, self.g, self.dots[self.m:])
-        h = self._read(2 * self.m)
-        p1 = np.array([h[r] for r in rows])
-        p2 = np.array([h[self.m + r] for r in rows])
-        R = np.triu(self.SY[np.ix_(rows, rows)])
-        D = np.diag(np.diag(R))
-        YY = self.YY[np.ix_(rows, rows)]
-        newest = rows[-1]
-        gamma = self.SY[newest, newest] / self.YY[newest, newest]
-        u = _solve_upper(R, p1)
-        cs = _solve_lower(R.T, (D + gamma * YY) @ u - gamma * p2)
-        cy = -gamma * u
-        coef = torch.from_numpy(np.concatenate((cs, cy)))
-        self.coef[:2 * k].copy_(coef.to(self.x.device, non_blocking=False))
-        self.order_dev[:k].copy_(torch.tensor(rows, dtype=torch.int32))
-        _lib.check(self.lib.flashns_b200_lbfgs_combine(_p(self.S), _p(self.Y), self.n, _p(self.order_dev), k,
-                                                       _p(self.coef), _p(self.coef[k:]), _p(self.g), float(gamma),
-                                                       _p(self.d), self.n, self._s()), "lbfgs_combine")
+    def _direction(self, set_flag=True):
+        """Fold the pair of the last accepted step into the history, then d = -H g; saves
+        x0, g0, f0 and g0.d for the line search.  No host round trip."""
+        slots = self.slots
+        self._call("lbfgs_pair_slot", _p(self.x), _p(self.x0), _p(self.g), _p(self.g0), _p(self.S), _p(self.Y),
+                   self.n, _p(self.state), self.n)
+        self._call("lbfgs_ring_dots", _p(self.S), _p(self.Y), self.n, slots, None, _p(self.state), 1, _p(self.dots),
+                   self.n)
+        self._call("lbfgs_commit", _p(self.dots), _p(self.SY), _p(self.YY), slots, _p(self.state))
+        if set_flag:
+            self.state[2:3].zero_()
+        self._call("lbfgs_ring_dots", _p(self.S), _p(self.Y), self.n, slots, _p(self.g), _p(self.state), 0,
+                   _p(self.dots), self.n)
+        self._call("lbfgs_coefficients", _p(self.SY), _p(self.YY), _p(self.dots), slots, _p(self.state),
+                   _p(self.coef), _p(self.order), _p(self.scal))
+        self._call("lbfgs_direction", _p(self.S), _p(self.Y), self.n, _p(self.order), _p(self.state), _p(self.coef),
+                   _p(self.g), _p(self.scal), _p(self.d), self.n)
+        self._call("lbfgs_save", _p(self.x), _p(self.g), _p(self.f), _p(self.x0), _p(self.g0), _p(self.scal), self.n)
+        self._call("row_dots", _p(self.g), self.n, 1, _p(self.d), _p(self.scal[_GD0:]), self.n)
 
-    def _push_pair(self):
-        if len(self.order) == self.m:
-            slot = self.order.pop(0)
-        else:
-            used = set(self.order)
-            slot = next(r for r in range(self.m) if r not in used)
-        _lib.check(self.lib.flashns_b200_lbfgs_pair(_p(self.x), _p(self.x0), _p(self.g), _p(self.g0),
-                                                    _p(self.S[slot]), _p(self.Y[slot]), self.n, self._s()), "pair")
-        rows = self.order + [slot]
-        # s_a . y_new and y_a . y_new for every stored row a (physical indices 0..m-1 as used)
-        self._row_dots(self.S, self.m, self.Y[slot], self.dots)
-        self._row_dots(self.Y, self.m, self.Y[slot], self.dots[self.m:])
-        h = self._read(2 * self.m)
-        sy, yy = h[slot], h[self.m + slot]
-        if not (sy > 1e-12 * max(yy, 1e-300)) or not math.isfinite(sy) or not math.isfinite(yy):
-            return False  # curvature condition fails: the pair is not stored
-        for a in rows:
-            self.SY[a, slot] = h[a]
-            self.YY[a, slot] = self.YY[slot, a] = h[self.m + a]
-        self.order = rows
-        return True
+    def _restart(self):
+        """Drop the history and return to x0 with its gradient and loss."""
+        self.state.zero_()
+        self.x.copy_(self.x0)
+        self.g.copy_(self.g0)
+        self.f.copy_(self.scal[_F0])
 
     # ---------------------------------------------------------------- line search
-    def _line_search(self, f0, gd0, t):
+    def _line_search(self, f0, gd0, t, f, gd):
+        """Strong Wolfe search; the trial at t is already evaluated as (f, gd)."""
         c1, c2 = self.c1, self.c2
         t_prev, f_prev, gd_prev = 0.0, f0, gd0
         best = (f0, 0.0, gd0)
         for i in range(self.max_ls):
-            f, gd = self._phi(t)
+            if i > 0:
+                f, gd, _ = self._phi(t)
             if f < best[0]:
                 best = (f, t, gd)
             if f > f0 + c1 * t * gd0 or (i > 0 and f >= f_prev):
@@ -156,7 +200,7 @@ class DeviceLBFGS:
             a, b = min(lo, hi), max(lo, hi)
             if not (a + 0.1 * (b - a) <= t <= b - 0.1 * (b - a)):
                 t = 0.5 * (a + b)
-            f, gd = self._phi(t)
+            f, gd, _ = self._phi(t)
             if f < best[0]:
                 best = (f, t, gd)
             if f > f0 + c1 * t * gd0 or f >= f_lo:
@@ -182,44 +226,37 @@ class DeviceLBFGS:
     # ---------------------------------------------------------------- driver
     def step(self, iterations):
         """Run up to ``iterations`` iterations; return the current loss."""
+        fresh = False
         if self.fk is None:
-            self.evaluate()
-            self.evaluations += 1
-            self.dots[0].copy_(self.f)
-            self.fk = float(self._read(1)[0])
+            self._eval()
+            self.fk = float(self.f)
+            self.pair = False
+            fresh = True
+            if self.capture_evaluate is not None and self.graphs is None:
+                self._build_graphs()
         for _ in range(iterations):
-            self._direction()
-            self._row_dots(self.g, 1, self.d, self.dots)
-            gd0 = float(self._read(1)[0])
+            t0 = min(1.0, 1.0 / max(float(self.g.abs().sum()), 1e-300)) if fresh else 1.0
+            f, gd, h = self._first_trial(t0, self.pair)
+            gd0 = h[_GD0]
             if not gd0 < 0:  # not a descent direction: restart from steepest descent
-                self.order = []
-                self.d.copy_(self.g).neg_()
-                self._row_dots(self.g, 1, self.d, self.dots)
-                gd0 = float(self._read(1)[0])
+                self._restart()
+                t0 = min(1.0, 1.0 / max(float(self.g.abs().sum()), 1e-300))
+                f, gd, h = self._first_trial(t0, False)
+                gd0 = h[_GD0]
                 if not gd0 < 0:
+                    self._restart()
+                    self.pair = False
                     break
-            t0 = 1.0 if self.order else min(1.0, 1.0 / max(float(self.g.abs().sum()), 1e-300))
-            self.x0.copy_(self.x)
-            self.g0.copy_(self.g)
-            t, f = self._line_search(self.fk, gd0, t0)
-            if t == 0.0:  # no decrease along d: restore x0 (and its gradient) and stop
-                self.x.copy_(self.x0)
-                self.evaluate()
-                self.evaluations += 1
-                self.order = []
+            t, f = self._line_search(h[_F0], gd0, t0, f, gd)
+            if t == 0.0:  # no decrease along d: back to x0 (and its gradient), drop the history
+                self._restart()
+                self.pair = False
                 break
-            self._push_pair()
+            self.pair = True  # the next direction folds in s = x - x0, y = g - g0
             self.fk = f
+            fresh = False
             self.iterations += 1
         return self.fk
-
-
-def _solve_upper(R, b):
-    return solve_triangular(R, b, lower=False, check_finite=False)
-
-
-def _solve_lower(L, b):
-    return solve_triangular(L, b, lower=True, check_finite=False)
 
 
 def _cubic_min(x1, f1, g1, x2, f2, g2):

@@ -138,16 +138,55 @@ def taylor_green(interior, boundary, *, nu=0.01, seed=1, boundary_order=1):
                     f"taylor-green nu={nu:g} {interior}+{boundary}")
 
 
-# BASELINE configurations: (builder, interior, boundary, widths)
+def reference_case(batch, *, seed=7510, scale=0.4):
+    """The reference's own benchmark problem (uvp head, 2-64-64-3, dense Q10 points, no
+    boundary rows, unweighted quadrature): coordinates N(0, scale^2), globally normalized
+    weights 1/batch, nu = 0.07 (docs/cuda-h100-results.md "固定科学目标"; the generator
+    recipe of experiments/cuda_jet_h100/common.py:44-80, restated)."""
+    gen = torch.Generator(device="cpu").manual_seed(seed)
+    x = torch.randn(batch, 2, generator=gen, dtype=torch.float64) * scale
+    pde = torch.full((batch,), 1.0 / max(batch, 1), dtype=torch.float64)
+    empty = torch.zeros(0, 3, dtype=torch.float64)
+    return PointSet(x, batch, pde, empty, empty.clone(), 2, 0.07, f"reference case {batch}")
+
+
+def reference_parameters(widths, seed=7510):
+    """Weights N(0, 0.7^2 / fan_in), biases N(0, 0.1^2) (the reference benchmark's init)."""
+    gen = torch.Generator(device="cpu").manual_seed(seed + 1)
+    ws = [torch.randn(o, i, generator=gen, dtype=torch.float64) * (0.7 / math.sqrt(i))
+          for i, o in zip(widths, widths[1:])]
+    bs = [torch.randn(o, generator=gen, dtype=torch.float64) * 0.1 for o in widths[1:]]
+    return ws, bs
+
+
+# BASELINE configurations: (builder, interior, boundary, widths); ref16k is the reference's
+# own headline workload (its published H100 number: 1.832 ms per evaluation)
 CONFIGS = {
     "cfg0": dict(kind="kovasznay", interior=2048, boundary=512, widths=[2, 64, 64, 64, 64, 2]),
     "cfg1": dict(kind="kovasznay", interior=16384, boundary=4096, widths=[2, 64, 64, 64, 64, 2]),
     "cfg2": dict(kind="kovasznay", interior=65536, boundary=16384, widths=[2] + [128] * 6 + [2]),
     "cfg3": dict(kind="taylor_green", interior=262144, boundary=65536, widths=[3] + [128] * 5 + [2]),
+    "ref16k": dict(kind="reference_case", interior=16384, boundary=0, widths=[2, 64, 64, 3], head="uvp",
+                   boundary_order=0, gamma=0.2, init="reference"),
 }
 
 
-def config_points(name, *, scale=1, seed=1, boundary_order=1):
+def config_options(name):
+    """(head, boundary_order, gradient weight gamma) of a configuration."""
     c = CONFIGS[name]
+    return c.get("head", "psi"), c.get("boundary_order", 1), c.get("gamma", 0.2)
+
+
+def config_parameters(name, seed=0):
+    from flashns_b200.evaluator import xavier_normal
+    c = CONFIGS[name]
+    return reference_parameters(c["widths"]) if c.get("init") == "reference" else xavier_normal(c["widths"], seed)
+
+
+def config_points(name, *, scale=1, seed=1, boundary_order=None):
+    c = CONFIGS[name]
+    if c["kind"] == "reference_case":
+        return reference_case(c["interior"] * scale)
     build = kovasznay if c["kind"] == "kovasznay" else taylor_green
-    return build(c["interior"] * scale, c["boundary"] * scale, seed=seed, boundary_order=boundary_order)
+    order = c.get("boundary_order", 1) if boundary_order is None else boundary_order
+    return build(c["interior"] * scale, c["boundary"] * scale, seed=seed, boundary_order=order)

@@ -15,6 +15,7 @@ evaluation of the line searches and the acceptance checks.
 """
 
 import argparse
+import ctypes
 import json
 import math
 import os
@@ -23,6 +24,7 @@ import time
 import torch
 import torch.distributed as dist
 
+from flashns_b200 import _lib
 from flashns_b200.evaluator import FieldEvaluator, PackedEvaluator, flat_parameters, xavier_normal
 from flashns_b200.lbfgs import DeviceLBFGS
 from flashns_b200.ns_seed import NSLoss
@@ -92,15 +94,27 @@ def solve(*, interior=16384, boundary=4096, widths=(2, 64, 64, 64, 64, 2), re=20
         flat.grad = grad_view
         return loss_view
 
+    torch.cuda.synchronize(device)
     setup = time.perf_counter() - start
+    phases = {"adam_s": 0.0, "lbfgs_s": 0.0, "accept_s": 0.0}
+    t_phase = time.perf_counter()
     if adam_steps:
-        # Adam phase on the same captured closure (experiments/pinn_solver/solve.py:137-149)
-        adam = torch.optim.Adam([flat], lr=adam_lr, fused=True)
-        for _ in range(adam_steps):
-            closure()
-            adam.step()
+        # Adam phase on the same captured closure (experiments/pinn_solver/solve.py:137-149),
+        # one fused update kernel per step
+        m, v = torch.zeros_like(flat.data), torch.zeros_like(flat.data)
+        lib = _lib.library()
+        ptr = lambda t: ctypes.c_void_p(t.data_ptr())
+        launch_stream = ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+        for k in range(1, adam_steps + 1):
+            graph.replay()
+            _lib.check(lib.flashns_b200_adam_step(ptr(flat.data), ptr(grad_view), ptr(m), ptr(v), flat.numel(),
+                                                  adam_lr, 0.9, 0.999, 1e-8, k, launch_stream), "adam_step")
+        evaluations[0] += adam_steps
+        torch.cuda.synchronize(device)
+    phases["adam_s"] = time.perf_counter() - t_phase
     if optimizer == "device":
-        lbfgs = DeviceLBFGS(flat.data, grad_view, loss_view, graph.replay, history=history)
+        lbfgs = DeviceLBFGS(flat.data, grad_view, loss_view, graph.replay, history=history,
+                            capture_evaluate=lambda: ev(flat.data, out))
     else:
         lbfgs = torch.optim.LBFGS([flat], lr=1.0, max_iter=check_every, max_eval=int(check_every * 1.25),
                                   history_size=history, tolerance_grad=0.0, tolerance_change=0.0,
@@ -108,6 +122,7 @@ def solve(*, interior=16384, boundary=4096, widths=(2, 64, 64, 64, 64, 2), re=20
     iterations, metrics, accepted = 0, None, False
     decision = torch.zeros(1, dtype=torch.int32, device=device)
     while iterations < max_iterations:
+        t_phase = time.perf_counter()
         if optimizer == "device":
             lbfgs.step(check_every)
             iterations = lbfgs.iterations
@@ -115,7 +130,10 @@ def solve(*, interior=16384, boundary=4096, widths=(2, 64, 64, 64, 64, 2), re=20
         else:
             lbfgs.step(closure)
             iterations = lbfgs.state[lbfgs._params[0]]["n_iter"]
+        t_accept = time.perf_counter()
+        phases["lbfgs_s"] += t_accept - t_phase
         metrics = accept(flat.data)
+        phases["accept_s"] += time.perf_counter() - t_accept
         accepted = metrics[0] <= tol_uv and metrics[1] <= tol_uv and metrics[2] <= tol_p
         decision.fill_(int(accepted or not all(math.isfinite(m) for m in metrics)))
         if world > 1:
@@ -130,7 +148,8 @@ def solve(*, interior=16384, boundary=4096, widths=(2, 64, 64, 64, 64, 2), re=20
     torch.cuda.synchronize(device)
     wall = time.perf_counter() - start
     del graph
-    return {"accepted": accepted, "wall_s": wall, "setup_s": setup, "optimizer": optimizer, "iterations": iterations,
+    return {"accepted": accepted, "wall_s": wall, "setup_s": setup, **phases, "optimizer": optimizer,
+            "iterations": iterations,
             "evaluations": evaluations[0], "rel_l2_u": metrics[0], "rel_l2_v": metrics[1], "rel_l2_p": metrics[2],
             "final_loss": float(loss_view), "n_gpus": world, "interior": interior, "boundary": boundary,
             "widths": widths, "re": re, "seed": seed, "init_seed": init_seed}

@@ -177,17 +177,49 @@ int flashns_b200_residuals(int head, int dim, const double* jets, double nu, dou
 /* Vector kernels of the device-resident L-BFGS (no reference counterpart: the reference
  * uses torch.optim.LBFGS, experiments/pinn_solver/solve.py:150-167).
  *   row_dots:      out[r] = rows[r] . v for r < k (rows [k][stride]); fixed-order reductions
- *   lbfgs_combine: d = -(gamma g + sum_i cs[i] S[order[i]] + sum_i cy[i] Y[order[i]])
- *   axpy:          x = x0 + t d
- *   lbfgs_pair:    s = x - x0, y = g - g0 */
+ *   axpy:          x = x0 + t d */
 int flashns_b200_row_dots(const double* rows, int64_t stride, int k, const double* v, double* out, int64_t n,
                           cudaStream_t stream);
-int flashns_b200_lbfgs_combine(const double* S, const double* Y, int64_t stride, const int* order, int k,
-                               const double* cs, const double* cy, const double* g, double gamma, double* d, int64_t n,
-                               cudaStream_t stream);
 int flashns_b200_axpy(const double* x0, double t, const double* d, double* x, int64_t n, cudaStream_t stream);
-int flashns_b200_lbfgs_pair(const double* x, const double* x0, const double* g, const double* g0, double* s, double* y,
+
+/* Device-resident L-BFGS state.  The curvature pairs live in a ring of `slots` = history + 1
+ * physical rows (one spare) of S and Y ([slots][stride] each); SY[a][b] = s_a . y_b and
+ * YY[a][b] = y_a . y_b ([slots][slots], physical rows); state = int32 {k stored pairs,
+ * h spare slot, have_pair, 0}; scal = f64 {gamma, f0, g0.d, f, g.d, k, t, 0}; coef = f64[256]
+ * (cs at 0.., cy at 128..); order = int32[128] (physical rows of the stored pairs, oldest
+ * first).  history <= 128.  Every step reads its counts from the device, so one iteration
+ * needs no host round trip before its first line-search trial.  scal[6] holds the trial step.
+ *   lbfgs_pair_slot:    if have_pair: S[h] = x - x0, Y[h] = g - g0
+ *   lbfgs_ring_dots:    out[b] = (b < slots ? S[b] : Y[b - slots]) . v, b < 2 slots;
+ *                       v = `v`, or the spare row Y[h] when from_slot (skipped without a pair)
+ *   lbfgs_commit:       keep the spare pair if s.y > 1e-12 y.y (dots from ring_dots with
+ *                       from_slot): fill its SY column and YY row/column, advance h, k
+ *   lbfgs_coefficients: compact-representation coefficients from dots = [S.g ; Y.g]
+ *                       (Byrd, Nocedal, Schnabel 1994, Thm 2.2), gamma = s.y / y.y newest
+ *   lbfgs_direction:    d = -(gamma g + sum_i cs[i] S[order[i]] + cy[i] Y[order[i]])
+ *   lbfgs_save:         x0 = x, g0 = g, scal[1] = *f
+ *   lbfgs_step_point:   x = x0 + scal[6] d (the trial step read on the device, so a CUDA
+ *                       graph of a line-search trial replays with a new step) */
+int flashns_b200_lbfgs_pair_slot(const double* x, const double* x0, const double* g, const double* g0, double* S,
+                                 double* Y, int64_t stride, const int* state, int64_t n, cudaStream_t stream);
+int flashns_b200_lbfgs_ring_dots(const double* S, const double* Y, int64_t stride, int slots, const double* v,
+                                 const int* state, int from_slot, double* out, int64_t n, cudaStream_t stream);
+int flashns_b200_lbfgs_commit(const double* dots, double* SY, double* YY, int slots, int* state, cudaStream_t stream);
+int flashns_b200_lbfgs_coefficients(const double* SY, const double* YY, const double* dots, int slots,
+                                    const int* state, double* coef, int* order, double* scal, cudaStream_t stream);
+int flashns_b200_lbfgs_direction(const double* S, const double* Y, int64_t stride, const int* order, const int* state,
+                                 const double* coef, const double* g, const double* scal, double* d, int64_t n,
+                                 cudaStream_t stream);
+int flashns_b200_lbfgs_save(const double* x, const double* g, const double* f, double* x0, double* g0, double* scal,
                             int64_t n, cudaStream_t stream);
+int flashns_b200_lbfgs_step_point(const double* x0, const double* scal, const double* d, double* x, int64_t n,
+                                  cudaStream_t stream);
+
+/* One Adam update of the solver's first phase (the reference's captured FP64 Adam,
+ * experiments/pinn_solver/backends.py:216-240): m = b1 m + (1-b1) g, v = b2 v + (1-b2) g^2,
+ * x -= lr (m / (1 - b1^step)) / (sqrt(v / (1 - b2^step)) + eps); step counts from 1. */
+int flashns_b200_adam_step(double* x, const double* g, double* m, double* v, int64_t n, double lr, double beta1,
+                           double beta2, double eps, int64_t step, cudaStream_t stream);
 
 /* shared memory the dense dgrad uses per block (0: this implementation stages none) */
 int flashns_stable_dgrad_shared_bytes(void);
