@@ -1197,7 +1197,7 @@ constexpr size_t fwd_head_smem_bytes() {
   using T = HeadTile<DIM>;
   constexpr int CP = kFusedWidth;
   constexpr size_t ring = size_t(kStages) * T::TR * LDC;
-  constexpr size_t stage = size_t(T::TR) * (CP + 1);  // H_L tile, aliases the ring
+  constexpr size_t stage = size_t(T::TR) * (CP + 4);  // H_L tile, aliases the ring
   constexpr size_t main = (ring > stage ? ring : stage) + size_t(CP) * (CP + 4) + 2 * size_t(T::TR);
   constexpr size_t head = size_t(NF) * CP + 2 * size_t(T::TR) * NF;
   return sizeof(double) * (main + head);
@@ -1215,17 +1215,15 @@ __global__ void __launch_bounds__(HeadTile<DIM>::THREADS, HeadTile<DIM>::MINB)
   constexpr int S = T::S, TR = T::TR, Q = TL::Q, QB = TL::QB, PS = TL::PS;
   constexpr int NF = HeadTraits<HEAD>::NF;
   constexpr int NFT = (HEAD == FLASHNS_B200_HEAD_PSI && BO) ? 3 : NF;  // boundary target fields
-  constexpr int LDA = KIN + 4, LDH = CP + 1;
+  constexpr int LDA = KIN + 4, LDH = CP + 4;  // LDH = 4 mod 16: conflict-free f64 fragments
   constexpr int PARTIAL = NF * CP + NF + 1 + CP;  // dW_L | db_L | loss | db_{L-1}
   constexpr int NK = KIN / KC;
-  // output-layer gradient: each (o, c) is owned by RQ threads, one per interleaved row share
-  constexpr int RQ = T::THREADS / (NF * CP) > 0 ? T::THREADS / (NF * CP) : 1;
-  constexpr int WPT = (NF * CP * RQ + T::THREADS - 1) / T::THREADS;
   static_assert(NK == 2 && kStages == 2, "one chunk of lookahead per tile");
+  static_assert(T::NWARPS == CP / 8 && NF <= 8, "warp w owns output-gradient columns 8w..8w+7");
   constexpr int RING = (kStages * TR * LDC > TR * LDH) ? kStages * TR * LDC : TR * LDH;
   extern __shared__ __align__(16) double smem[];
   double* sB = smem;         // activation chunks [stage][TR][LDC] during the mainloop
-  double* sH = smem;         // H_L tile [TR][CP+1], natural row order, during the epilogue
+  double* sH = smem;         // H_L tile [TR][CP+4], natural row order, during the epilogue
   double* sA = sB + RING;    // W_{L-1} resident  [CP][KIN+4]
   int64_t* rowmap = reinterpret_cast<int64_t*>(sA + CP * LDA);  // [2][TR]
   double* sW = reinterpret_cast<double*>(rowmap + 2 * TR);      // W_L [NF][CP]
@@ -1259,9 +1257,7 @@ __global__ void __launch_bounds__(HeadTile<DIM>::THREADS, HeadTile<DIM>::MINB)
     cp_async16(sA + r * LDA + 2 * p, w + int64_t(r) * KIN + 2 * p, true);
   }
   cp_async_commit();
-  double wacc[WPT];
-#pragma unroll
-  for (int k = 0; k < WPT; ++k) wacc[k] = 0.0;
+  double wacc[4] = {0.0, 0.0, 0.0, 0.0};  // dW_L[g][8 warp + 2t (+1)] (rows g < NF)
   double bacc = 0.0, lacc = 0.0, cacc[2] = {0.0, 0.0};
   int buf = 0;
   if (int64_t(blockIdx.x) < ntiles) {
@@ -1326,6 +1322,9 @@ __global__ void __launch_bounds__(HeadTile<DIM>::THREADS, HeadTile<DIM>::MINB)
           Jet<DIM, 3>::fwd(z, hv, a1r[hh][0]);
 #pragma unroll
           for (int s = 0; s < Q; ++s) sH[(tc * Q + s) * LDH + ch] = hv[s];
+        } else {  // rows of points past the segment stay finite for the row contractions
+#pragma unroll
+          for (int s = 0; s < Q; ++s) sH[(tc * Q + s) * LDH + ch] = 0.0;
         }
       } else {
 #pragma unroll
@@ -1339,30 +1338,33 @@ __global__ void __launch_bounds__(HeadTile<DIM>::THREADS, HeadTile<DIM>::MINB)
             Jet<DIM, BO ? 1 : 0>::fwd(zz, hv, a1r[hh][kq]);
 #pragma unroll
             for (int c = 0; c < QB; ++c) sH[(lp * QB + c) * LDH + ch] = hv[c];
+          } else {
+#pragma unroll
+            for (int c = 0; c < QB; ++c) sH[(lp * QB + c) * LDH + ch] = 0.0;
           }
         }
       }
     }
     __syncthreads();
-    // 2. outputs Y[r][o] = H[r].W_L[o] (+ b_L on order-0 rows)
-    for (int i = tid; i < nrows * NF; i += T::THREADS) {
-      const int r = i / NF, o = i % NF;
-      const double* hr = sH + r * LDH;
-      const double* wo = sW + o * CP;
-      double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
-#pragma unroll 4
-      for (int c = 0; c < CP; c += 4) {
-        s0 += hr[c] * wo[c];
-        s1 += hr[c + 1] * wo[c + 1];
-        s2 += hr[c + 2] * wo[c + 2];
-        s3 += hr[c + 3] * wo[c + 3];
+    // 2. outputs Y^T[o][r] = W_L[o] . H[r] (+ b_L on order-0 rows) as DMMA tiles:
+    //    M = outputs (rows >= NF zero), N = tile rows (n8 tile j per warp), K = channels
+    const int kend = (nrows + 7) & ~7;
+    for (int j = warp; j < kend / 8; j += T::NWARPS) {
+      double c[4] = {0.0, 0.0, 0.0, 0.0};
+#pragma unroll
+      for (int kk = 0; kk < CP; kk += 8) {
+        const double a[4] = {g < NF ? sW[g * CP + kk + t] : 0.0, 0.0, g < NF ? sW[g * CP + kk + t + 4] : 0.0, 0.0};
+        mma_m16n8k8(c, a, sH[(8 * j + g) * LDH + kk + t], sH[(8 * j + g) * LDH + kk + t + 4]);
       }
-      double y = (s0 + s1) + (s2 + s3);
-      if (r % step == 0) y += bL[o];
-      sY[r * NF + o] = y;
+      if (g < NF) {
+        const int r0 = 8 * j + 2 * t;
+        if (r0 < nrows) sY[r0 * NF + g] = c[0] + (r0 % step == 0 ? bL[g] : 0.0);
+        if (r0 + 1 < nrows) sY[(r0 + 1) * NF + g] = c[1] + ((r0 + 1) % step == 0 ? bL[g] : 0.0);
+      }
     }
     __syncthreads();
-    // 3. residual seeds, one point per thread
+    // 3. residual seeds, one point per thread (dY rows up to the next multiple of 8 zeroed)
+    for (int i = tid; i < (kend - nrows) * NF; i += T::THREADS) sD[nrows * NF + i] = 0.0;
     if (interior) {
       if (tid < npts) {
         double y[Q * NF], dy[Q * NF];
@@ -1407,23 +1409,11 @@ __global__ void __launch_bounds__(HeadTile<DIM>::THREADS, HeadTile<DIM>::MINB)
       }
     }
     __syncthreads();
-    // 4. output-layer gradients: dW_L[o][c] += sum_r dY[r][o] H[r][c]; db_L over order-0 rows
-#pragma unroll
-    for (int k = 0; k < WPT; ++k) {
-      const int idx = tid + k * T::THREADS;
-      if (idx < NF * CP * RQ) {
-        const int rq = idx / (NF * CP), o = (idx % (NF * CP)) / CP, c = idx % CP;
-        double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
-        int r = rq;
-        for (; r + 3 * RQ < nrows; r += 4 * RQ) {
-          s0 += sD[r * NF + o] * sH[r * LDH + c];
-          s1 += sD[(r + RQ) * NF + o] * sH[(r + RQ) * LDH + c];
-          s2 += sD[(r + 2 * RQ) * NF + o] * sH[(r + 2 * RQ) * LDH + c];
-          s3 += sD[(r + 3 * RQ) * NF + o] * sH[(r + 3 * RQ) * LDH + c];
-        }
-        for (; r < nrows; r += RQ) s0 += sD[r * NF + o] * sH[r * LDH + c];
-        wacc[k] += (s0 + s1) + (s2 + s3);
-      }
+    // 4. output-layer gradients dW_L[o][c] += sum_r dY[r][o] H[r][c] as DMMA tiles (M =
+    //    outputs, N = channels 8 warp.., K = tile rows); db_L over order-0 rows
+    for (int k0 = 0; k0 < kend; k0 += 8) {
+      const double a[4] = {g < NF ? sD[(k0 + t) * NF + g] : 0.0, 0.0, g < NF ? sD[(k0 + t + 4) * NF + g] : 0.0, 0.0};
+      mma_m16n8k8(wacc, a, sH[(k0 + t) * LDH + 8 * warp + g], sH[(k0 + t + 4) * LDH + 8 * warp + g]);
     }
     if (tid < NF)
       for (int r = 0; r < nrows; r += step) bacc += sD[r * NF + tid];
@@ -1486,11 +1476,9 @@ __global__ void __launch_bounds__(HeadTile<DIM>::THREADS, HeadTile<DIM>::MINB)
   if (tid < NF) out[NF * CP + tid] = bacc;
   double* red = smem;                 // [THREADS] loss partials
   double* cred = smem + T::THREADS;  // [WR][CP] bias partials of layer L-1
-  double* wred = cred + T::WR * CP;   // [RQ][NF*CP] output-layer gradient shares
-#pragma unroll
-  for (int k = 0; k < WPT; ++k) {
-    const int idx = tid + k * T::THREADS;
-    if (idx < NF * CP * RQ) wred[idx] = wacc[k];
+  if (g < NF) {
+    out[g * CP + 8 * warp + 2 * t] = wacc[0];
+    out[g * CP + 8 * warp + 2 * t + 1] = wacc[1];
   }
   red[tid] = lacc;
 #pragma unroll
@@ -1510,11 +1498,6 @@ __global__ void __launch_bounds__(HeadTile<DIM>::THREADS, HeadTile<DIM>::MINB)
     double sum = 0.0;
     for (int r = 0; r < T::WR; ++r) sum += cred[r * CP + c];
     out[NF * CP + NF + 1 + c] = sum;
-  }
-  for (int idx = tid; idx < NF * CP; idx += T::THREADS) {
-    double sum = 0.0;
-    for (int r = 0; r < RQ; ++r) sum += wred[r * NF * CP + idx];
-    out[idx] = sum;
   }
 }
 
