@@ -1667,6 +1667,7 @@ struct flashns_b200_plan {
   int wg_splits[kMaxAffine];
   bool fused[kMaxAffine];  // backward layer l runs bwd_fused (dgrad + VJP + wgrad)
   bool fused_head;         // the last forward layer and the output layer run as fwd_head
+  bool direct;             // flat parameters already have the padded layout: no pack launch
   int64_t wg_rows[kMaxAffine];
   int wg_bm[kMaxAffine], wg_bn[kMaxAffine];
 };
@@ -2002,6 +2003,13 @@ int flashns_b200_plan_create(int dim, int head, int boundary_order, int n_affine
     L.w_buf = take(int64_t(L.coutp) * L.cinp);
     L.b_buf = take(L.coutp);
   }
+  // widths that need no padding: the kernels read W_l and b_l straight from the flat vector
+  // (every block then starts on a 16-byte boundary of a 16-byte aligned parameter vector)
+  p->direct = true;
+  for (int l = 0; l < n_affine; ++l) {
+    const LayerDesc& L = tab.l[l];
+    if (L.coutp != L.cout || L.cinp != L.cin || (L.w_flat & 1) || (L.b_flat & 1) || (L.cinp & 1)) p->direct = false;
+  }
   for (int l = 1; l <= nh; ++l) {
     p->off_h[l] = take(p->rows * p->padded[l]);
     p->off_a1[l] = take(p->points * p->padded[l]);
@@ -2123,6 +2131,7 @@ static int run_eval(const flashns_b200_plan* p, const double* coordinates, const
   if (p->ni && !pde_weights) return int(cudaErrorInvalidValue);
   if (p->nb && (!boundary_weights || !target)) return int(cudaErrorInvalidValue);
   if ((reinterpret_cast<uintptr_t>(workspace) & 15) != 0) return int(cudaErrorInvalidValue);
+  if (p->direct && (reinterpret_cast<uintptr_t>(parameters) & 15) != 0) return int(cudaErrorInvalidValue);
   int marks = 0;
   auto mark = [&]() {
     if (events && marks < capacity) cudaEventRecord(events[marks], stream);
@@ -2130,25 +2139,30 @@ static int run_eval(const flashns_b200_plan* p, const double* coordinates, const
   };
   double* ws = static_cast<double*>(workspace);
   const LayerTable& tab = p->tab;
-  int64_t packed = 0;
-  for (int l = 0; l < p->n_aff; ++l) packed += int64_t(tab.l[l].coutp) * tab.l[l].cinp + tab.l[l].coutp;
-  mark();
-  pack_params<<<unsigned((packed + kThreads - 1) / kThreads), kThreads, 0, stream>>>(parameters, ws, tab);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return int(e);
+  cudaError_t e = cudaSuccess;
+  if (!p->direct) {
+    int64_t packed = 0;
+    for (int l = 0; l < p->n_aff; ++l) packed += int64_t(tab.l[l].coutp) * tab.l[l].cinp + tab.l[l].coutp;
+    mark();
+    pack_params<<<unsigned((packed + kThreads - 1) / kThreads), kThreads, 0, stream>>>(parameters, ws, tab);
+    if ((e = cudaGetLastError()) != cudaSuccess) return int(e);
+  }
+  // padded layer buffers, or the flat vector itself when no layer needs padding
+  auto Wp = [&](const LayerDesc& L) -> const double* { return p->direct ? parameters + L.w_flat : ws + L.w_buf; };
+  auto Bp = [&](const LayerDesc& L) -> const double* { return p->direct ? parameters + L.b_flat : ws + L.b_buf; };
   const int nh = p->n_aff - 1;
   const Geometry g = p->geo;
   if (p->rows > 0) {
     const LayerDesc& L0 = tab.l[0];
     mark();
-    int r = first_launch(p->dim, p->bo, p->grid_first, stream, coordinates, ws + L0.w_buf, ws + L0.b_buf,
+    int r = first_launch(p->dim, p->bo, p->grid_first, stream, coordinates, Wp(L0), Bp(L0),
                          ws + p->off_h[1], ws + p->off_a1[1], p->padded[1], g);
     if (r) return r;
     for (int l = 1; l < nh - (p->fused_head ? 1 : 0); ++l) {
       const LayerDesc& L = tab.l[l];
       mark();
       with_fwd<FwdOps>(p->dim, p->padded[l + 1], p->bo, [&](auto ops) {
-        ops.launch(p->grid_fwd[l], stream, ws + p->off_h[l], p->padded[l], ws + L.w_buf, ws + L.b_buf,
+        ops.launch(p->grid_fwd[l], stream, ws + p->off_h[l], p->padded[l], Wp(L), Bp(L),
                    ws + p->off_h[l + 1], ws + p->off_a1[l + 1], g);
       });
       if ((e = cudaGetLastError()) != cudaSuccess) return int(e);
@@ -2158,15 +2172,15 @@ static int run_eval(const flashns_b200_plan* p, const double* coordinates, const
       const LayerDesc& H = tab.l[nh];
       mark();
       with_fwd_head(p->dim, p->bo, p->head, [&](auto ops) {
-        ops.launch(p->grid_head, stream, ws + p->off_h[nh - 1], ws + L.w_buf, ws + L.b_buf, ws + H.w_buf,
-                   ws + H.b_buf, pde_weights, boundary_weights, target, p->nu, p->gamma, p->bc,
+        ops.launch(p->grid_head, stream, ws + p->off_h[nh - 1], Wp(L), Bp(L), Wp(H),
+                   Bp(H), pde_weights, boundary_weights, target, p->nu, p->gamma, p->bc,
                    ws + p->off_d[nh % 2], ws + p->off_head, g);
       });
       if ((e = cudaGetLastError()) != cudaSuccess) return int(e);
     } else {
       const LayerDesc& L = tab.l[nh];
       auto f = [&](auto ops) {
-        ops.launch(p->grid_head, stream, ws + p->off_h[nh], ws + p->off_a1[nh], ws + L.w_buf, ws + L.b_buf,
+        ops.launch(p->grid_head, stream, ws + p->off_h[nh], ws + p->off_a1[nh], Wp(L), Bp(L),
                    pde_weights, boundary_weights, target, p->nu, p->gamma, p->bc, ws + p->off_d[nh % 2],
                    coordinates, ws + p->off_coord, ws + p->off_head, g);
       };
@@ -2179,13 +2193,13 @@ static int run_eval(const flashns_b200_plan* p, const double* coordinates, const
       const LayerDesc& L = tab.l[l];
       const double* dn = ws + p->off_d[(l + 1) % 2];
       auto f = [&](auto ops) {
-        ops.launch(p->grid_bwd[l], stream, dn, p->padded[l + 1], ws + L.w_buf, ws + p->off_h[l], ws + p->off_a1[l],
+        ops.launch(p->grid_bwd[l], stream, dn, p->padded[l + 1], Wp(L), ws + p->off_h[l], ws + p->off_a1[l],
                    ws + p->off_d[l % 2], coordinates, ws + (l == 1 ? p->off_coord : p->off_bb[l]), g);
       };
       mark();
       if (p->fused[l]) {
         auto ff = [&](auto ops) {
-          ops.launch(p->grid_bwd[l], stream, dn, ws + L.w_buf, ws + p->off_h[l], ws + p->off_a1[l],
+          ops.launch(p->grid_bwd[l], stream, dn, Wp(L), ws + p->off_h[l], ws + p->off_a1[l],
                      ws + p->off_d[l % 2], coordinates, ws + (l == 1 ? p->off_coord : p->off_bb[l]),
                      ws + p->off_wg[l], g);
         };
@@ -2235,7 +2249,7 @@ int flashns_b200_plan_launch_kinds(const flashns_b200_plan* p, int* kinds, int c
   if (!p || !count) return int(cudaErrorInvalidValue);
   std::vector<int> k;
   const int nh = p->n_aff - 1;
-  k.push_back(FLASHNS_B200_KERNEL_PACK);
+  if (!p->direct) k.push_back(FLASHNS_B200_KERNEL_PACK);
   if (p->rows > 0) {
     k.push_back(FLASHNS_B200_KERNEL_FIRST);
     for (int l = 1; l < nh - (p->fused_head ? 1 : 0); ++l) k.push_back(FLASHNS_B200_KERNEL_FORWARD);

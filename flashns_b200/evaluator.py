@@ -121,6 +121,8 @@ class PackedEvaluator:
             raise ValueError(f"flat FP64 parameters [{self.parameters}] on {self.device} required")
         if not flat.is_contiguous():
             raise ValueError("contiguous parameters required")
+        if flat.data_ptr() % 16:
+            flat = flat.clone()  # the C ABI reads parameters from a 16-byte boundary
         if torch.is_grad_enabled() and flat.requires_grad:
             raise NotImplementedError("manual parameter VJP; double backward/HVP unsupported")
         if out is None:

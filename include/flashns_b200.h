@@ -80,6 +80,8 @@ int flashns_b200_wait_selftest(unsigned spins, int* gave_up, cudaStream_t stream
  *                     F = 3 for (uvp head) and (psi head, boundary_order 1): (u, v, p);
  *                     F = 2 for (psi head, boundary_order 0): (psi, p)
  *   gradient_and_loss [P + 1]  gradient in the flat order, then the loss
+ * The workspace, and the parameter vector, start on 16-byte boundaries (when no layer
+ * width needs padding the kernels read W_l and b_l straight from the parameter vector).
  * Deterministic: fixed-order reductions, no floating-point atomics. */
 int flashns_b200_eval(const flashns_b200_plan* plan, const double* coordinates, const double* parameters,
                       const double* pde_weights, const double* boundary_weights, const double* target,

@@ -198,3 +198,22 @@ def test_bounded_wait_reports_instead_of_hanging(cuda):
     _, out = run(case, widths, "psi", 1, loss, cuda)  # the context still works
     assert np.isfinite(out).all()
     np.testing.assert_allclose(out, oracle(case, "psi", 1, loss), rtol=1e-9, atol=1e-12)
+
+
+@pytest.mark.gpu
+def test_unaligned_parameter_view(cuda):
+    """A parameter view off a 16-byte boundary evaluates like the aligned vector (the C ABI
+    reads parameters in place when no width needs padding, so the binding realigns)."""
+    from flashns_b200.ns_seed import NSLoss
+    widths = [2, 64, 64, 2]
+    case = random_case(40, 12, widths, head="psi", boundary_order=1, seed=5)
+    loss = NSLoss(0.05, 0.0, 2.0)
+    ev, ref = run(case, widths, "psi", 1, loss, cuda)
+    p = torch.tensor(flat(case["ws"], case["bs"]), dtype=torch.float64)
+    buf = torch.zeros(p.numel() + 1, dtype=torch.float64, device=cuda)
+    view = buf[1:]
+    view.copy_(p)
+    assert view.data_ptr() % 16 != 0
+    out = ev(view)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), ref)
