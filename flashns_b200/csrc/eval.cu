@@ -143,14 +143,19 @@ constexpr size_t fwd_smem_bytes(int kin) {
   using T = FwdTile<DIM, CP>;
   return sizeof(double) * (size_t(kStages) * T::TR * LDC + size_t(CP) * (kin + 4) + 2 * size_t(T::TR) + kStages);
 }
+// Backward tiles (bwd_layer): the tile's H_l rows stay in shared memory next to the seed and
+// weight ring, so 3-D layers use 8-warp (4-warp for 32 channels) CTAs to fit.
+template <int DIM, int CP>
+struct BwdTile : MmaTile<DIM, CP, DIM == 2 ? (CP >= 64 ? 16 : 8) : (CP >= 64 ? 8 : 4)> {};
+
 template <int DIM, int CP>
 constexpr size_t bwd_group_doubles() {
-  using T = MmaTile<DIM, CP>;
-  return size_t(kStages) * (size_t(T::TR) * LDC + size_t(KC) * (CP + 4)) + 2 * T::TR;
+  using T = BwdTile<DIM, CP>;
+  return size_t(kStages) * (size_t(T::TR) * LDC + size_t(KC) * (CP + 4)) + size_t(T::TR) * (CP + 4) + 2 * T::TR;
 }
 template <int DIM, int CP>
 constexpr size_t bwd_smem_bytes() {
-  using T = MmaTile<DIM, CP>;
+  using T = BwdTile<DIM, CP>;
   constexpr size_t a = sizeof(double) * bwd_group_doubles<DIM, CP>();
   constexpr size_t red = sizeof(double) * T::WR * CP * (DIM + 1);
   return a > red ? a : red;
@@ -329,20 +334,24 @@ __global__ void __launch_bounds__(FwdTile<DIM, CP>::THREADS, FwdTile<DIM, CP>::M
 // layer l-1 (sum of D_l over order-0 rows) as per-CTA partials [grid][CP].  FIRST: contract
 // D_1 with the coordinate jets (dW_0[c][a] += D[row0][c]*x[a] + D[unit(a)][c],
 // db_0[c] += D[row0][c]) into per-CTA partials [grid][CP][DIM+1] instead of storing D_1.
+// The tile's H_l rows are staged in shared memory (same row permutation) during the
+// mainloop and the jet VJP reads them there; the next tile's H_l is requested after the
+// epilogue and lands during the next mainloop.
 template <int DIM, int CP, int BO, bool FIRST>
-__global__ void __launch_bounds__(MmaTile<DIM, CP>::THREADS, 1)
+__global__ void __launch_bounds__(BwdTile<DIM, CP>::THREADS, 1)
     bwd_layer(const double* __restrict__ dnext, int kout, const double* __restrict__ w,
               const double* __restrict__ hcur, const double* __restrict__ a1cur, double* __restrict__ dcur,
               const double* __restrict__ x, double* __restrict__ partial, Geometry geo) {
-  using T = MmaTile<DIM, CP>;
+  using T = BwdTile<DIM, CP>;
   using TL = Tiles<DIM, BO, T::TC>;
-  constexpr int S = T::S, TR = T::TR, Q = TL::Q, QB = TL::QB, LDA = CP + 4;
+  constexpr int S = T::S, TR = T::TR, Q = TL::Q, QB = TL::QB, LDA = CP + 4, LDH = CP + 4;
   constexpr int NV = FIRST ? DIM + 1 : 1;  // per-channel partial values
   extern __shared__ __align__(16) double smem[];
   const int tid = threadIdx.x;
   double* sB = smem;   // seed chunks   [stage][TR][LDC]
   double* sA = sB + kStages * TR * LDC;                      // weight chunks [stage][KC][CP+4]
-  int64_t* rowmap = reinterpret_cast<int64_t*>(sA + kStages * KC * LDA);  // [2][TR]
+  double* sH = sA + kStages * KC * LDA;                      // H_l tile      [TR][CP+4]
+  int64_t* rowmap = reinterpret_cast<int64_t*>(sH + TR * LDH);  // [2][TR]
   const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int wc = warp % T::WC, wr = warp / T::WC;
   const int nk = kout / KC;
@@ -384,11 +393,21 @@ __global__ void __launch_bounds__(MmaTile<DIM, CP>::THREADS, 1)
       cp_async_commit();
     }
   };
+  auto load_h = [&](const int64_t* rm) {  // one commit group, after the tile's first chunk
+    for (int i = tid; i < TR * (CP / 2); i += T::THREADS) {
+      const int r = i / (CP / 2), p = i % (CP / 2);
+      const int64_t gr = rm[r];
+      cp_async16(sH + r * LDH + 2 * p, hcur + (gr >= 0 ? gr : 0) * CP + 2 * p, gr >= 0);
+    }
+    cp_async_commit();
+  };
+  static_assert(kStages == 2, "commit-group accounting: [chunk 0] [H] [chunk 1] ...");
   int buf = 0;
   if (iters > 0 && tile_of(0) < ntiles) {
     fill_rowmap(tile_of(0), rowmap);
     __syncthreads();
     prologue(rowmap);
+    load_h(rowmap);
   }
   for (int64_t k = 0; k < iters; ++k, buf ^= 1) {
     const int64_t tile = tile_of(k);
@@ -402,27 +421,21 @@ __global__ void __launch_bounds__(MmaTile<DIM, CP>::THREADS, 1)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0;
     if (valid && tid == 0) {
-      // the epilogue reads this tile's H rows and a1 rows (each a contiguous range):
-      // start bringing them into L2 while the main loop runs
-      int64_t row0, rows, pt0, pts;
+      // the epilogue reads this tile's a1 rows (a contiguous range): bring them into L2
+      int64_t pt0, pts;
       if (tile < nint) {
         pt0 = tile * T::TC;
         pts = (geo.ni - pt0) < T::TC ? (geo.ni - pt0) : T::TC;
-        row0 = pt0 * Q;
-        rows = pts * Q;
       } else {
         const int64_t b0 = (tile - nint) * (int64_t(T::TC) * TL::PS);
         pts = (geo.nb - b0) < int64_t(T::TC) * TL::PS ? (geo.nb - b0) : int64_t(T::TC) * TL::PS;
         pt0 = geo.ni + b0;
-        row0 = geo.ni * Q + b0 * QB;
-        rows = pts * QB;
       }
-      prefetch_l2(hcur + row0 * CP, uint32_t(rows * CP * sizeof(double)));
       prefetch_l2(a1cur + pt0 * CP, uint32_t(pts * CP * sizeof(double)));
     }
     if (valid) {
       for (int kc = 0; kc < nk; ++kc) {
-        cp_async_wait<kStages - 2>();
+        if (kc == 0) cp_async_wait<1>(); else cp_async_wait<0>();  // chunk 0 may overtake H
         __syncthreads();
         if (kc + kStages - 1 < nk) load(kc + kStages - 1, (kc + kStages - 1) % kStages, rm);
         cp_async_commit();
@@ -448,9 +461,11 @@ __global__ void __launch_bounds__(MmaTile<DIM, CP>::THREADS, 1)
         }
       }
     }
+    cp_async_wait<0>();  // the H_l tile (a single-chunk tile still has it in flight)
     __syncthreads();
-    if (k + 1 < iters && tile_of(k + 1) < ntiles) {
-      int64_t* rn = rowmap + (buf ^ 1) * TR;
+    const bool has_next = k + 1 < iters && tile_of(k + 1) < ntiles;
+    int64_t* rn = rowmap + (buf ^ 1) * TR;
+    if (has_next) {
       fill_rowmap(tile_of(k + 1), rn);
       __syncthreads();
       prologue(rn);
@@ -458,6 +473,9 @@ __global__ void __launch_bounds__(MmaTile<DIM, CP>::THREADS, 1)
     if (!valid) continue;
     const int tc = wr * 4 + t;
     const bool interior = tile < nint;
+    // H_l of slot s of this thread column from the shared tile (inverse of tile_slot)
+    const double* hrow = sH + (wr * (4 * S) + 2 * t) * LDH;
+    auto hslot = [&](int s, int ch) { return hrow[(8 * (s >> 1) + (s & 1)) * LDH + ch]; };
 #pragma unroll
     for (int i = 0; i < T::MT; ++i) {
 #pragma unroll
@@ -470,9 +488,8 @@ __global__ void __launch_bounds__(MmaTile<DIM, CP>::THREADS, 1)
           const int64_t p = tile * T::TC + tc;
           if (p < geo.ni) {
             double hv[Q], zb[Q];
-            const double* src = hcur + p * Q * CP + ch;
 #pragma unroll
-            for (int s = 0; s < Q; ++s) hv[s] = src[int64_t(s) * CP];
+            for (int s = 0; s < Q; ++s) hv[s] = hslot(s, ch);
             Jet<DIM, 3>::vjp(hv, a1cur[p * CP + ch], dh, zb);
             if constexpr (FIRST) {
               cacc[i][hh][DIM] += zb[0];
@@ -491,9 +508,8 @@ __global__ void __launch_bounds__(MmaTile<DIM, CP>::THREADS, 1)
             const int64_t b = (tile - nint) * (int64_t(T::TC) * TL::PS) + int64_t(tc) * TL::PS + kq;
             if (b < geo.nb) {
               double hv[QB], zb[QB];
-              const double* src = hcur + (geo.ni * Q + b * QB) * CP + ch;
 #pragma unroll
-              for (int c = 0; c < QB; ++c) hv[c] = src[int64_t(c) * CP];
+              for (int c = 0; c < QB; ++c) hv[c] = hslot(kq * QB + c, ch);
               Jet<DIM, BO ? 1 : 0>::vjp(hv, a1cur[(geo.ni + b) * CP + ch], dh + kq * QB, zb);
               if constexpr (FIRST) {
                 cacc[i][hh][DIM] += zb[0];
@@ -514,6 +530,8 @@ __global__ void __launch_bounds__(MmaTile<DIM, CP>::THREADS, 1)
         }
       }
     }
+    __syncthreads();  // H_l tile free: the next tile's rows stream in during its mainloop
+    if (has_next) load_h(rn);
   }
   cp_async_wait<0>();
   // fixed-order reduction: the 4 thread columns of a warp, then the warp row groups
@@ -1717,20 +1735,21 @@ struct FwdOps {
 
 template <int DIM, int CP, int BO, bool FIRST>
 struct BwdOps {
+  static_assert(bwd_smem_bytes<DIM, CP>() <= kMaxSmem, "backward tile exceeds shared memory");
   static cudaError_t setup(int& occ) {
     constexpr size_t smem = bwd_smem_bytes<DIM, CP>();
     cudaError_t e = allow_smem(bwd_layer<DIM, CP, BO, FIRST>, smem);
-    occ = occupancy(bwd_layer<DIM, CP, BO, FIRST>, smem, MmaTile<DIM, CP>::THREADS);
+    occ = occupancy(bwd_layer<DIM, CP, BO, FIRST>, smem, BwdTile<DIM, CP>::THREADS);
     return e;
   }
   static int64_t tiles(const Geometry& g) {
-    using T = MmaTile<DIM, CP>;
+    using T = BwdTile<DIM, CP>;
     using TL = Tiles<DIM, BO, T::TC>;
     return TL::interior(g.ni) + TL::boundary(g.nb);
   }
   static void launch(int grid, cudaStream_t st, const double* dn, int kout, const double* w, const double* h,
                      const double* a1, double* dc, const double* x, double* cp, Geometry g) {
-    bwd_layer<DIM, CP, BO, FIRST><<<grid, MmaTile<DIM, CP>::THREADS, bwd_smem_bytes<DIM, CP>(), st>>>(
+    bwd_layer<DIM, CP, BO, FIRST><<<grid, BwdTile<DIM, CP>::THREADS, bwd_smem_bytes<DIM, CP>(), st>>>(
         dn, kout, w, h, a1, dc, x, cp, g);
   }
 };
