@@ -67,6 +67,20 @@ __device__ __forceinline__ void bulk_g2s(void* smem, const void* gmem, unsigned 
       : "memory");
 }
 
+// orders this thread's earlier generic-proxy shared-memory accesses before its later
+// async-proxy (TMA) ones
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
+
+// 2-D tiled TMA load (no multicast): box at coordinates (x = column, y = row) of the tensor
+// map into shared memory, completing its bytes on `bar`.  x * 8 bytes is a multiple of 16.
+__device__ __forceinline__ void tma_load_2d(void* smem, const void* tensor_map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
+          smem_u32(smem)),
+      "l"(tensor_map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // D = A*B + D with FP64 tensor-core MMA (DMMA).  Fragment layout (PTX ISA,
 // m16n8k8 .f64): g = lane/4, t = lane%4;
 //   a0=A[g][t] a1=A[g+8][t] a2=A[g][t+4] a3=A[g+8][t+4]

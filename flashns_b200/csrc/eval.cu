@@ -19,6 +19,8 @@
 #include <algorithm>
 #include <cstdint>
 #include <cstring>
+#include <cuda.h>
+#include <mutex>
 #include <new>
 #include <vector>
 
@@ -180,7 +182,7 @@ __global__ void __launch_bounds__(FwdTile<DIM, CP>::THREADS, FwdTile<DIM, CP>::M
   using TL = Tiles<DIM, BO, T::TC>;
   constexpr int S = T::S, TR = T::TR, Q = TL::Q, QB = TL::QB;
   constexpr int NIS = TR < T::THREADS ? TR : T::THREADS;  // threads issuing row copies
-  extern __shared__ __align__(16) double smem[];
+  extern __shared__ __align__(128) double smem[];
   const int tid = threadIdx.x;
   const int LDA = kin + 4;
   double* sB = smem;                     // activation chunks [stage][TR][LDC]
@@ -346,7 +348,7 @@ __global__ void __launch_bounds__(BwdTile<DIM, CP>::THREADS, 1)
   using TL = Tiles<DIM, BO, T::TC>;
   constexpr int S = T::S, TR = T::TR, Q = TL::Q, QB = TL::QB, LDA = CP + 4, LDH = CP + 4;
   constexpr int NV = FIRST ? DIM + 1 : 1;  // per-channel partial values
-  extern __shared__ __align__(16) double smem[];
+  extern __shared__ __align__(128) double smem[];
   const int tid = threadIdx.x;
   double* sB = smem;   // seed chunks   [stage][TR][LDC]
   double* sA = sB + kStages * TR * LDC;                      // weight chunks [stage][KC][CP+4]
@@ -568,14 +570,15 @@ __global__ void __launch_bounds__(BwdTile<DIM, CP>::THREADS, 1)
 
 // ----------------------------------------------------------------------------------
 // Fused backward of a square 64-wide hidden layer: the dgrad + jet VJP of bwd_layer and
-// the weight gradient dW_l = D_{l+1}^T H_l of the same tile.  The tile's whole seed
-// D_{l+1} (both 32-channel chunks) and its H_l rows sit in shared memory in the same row
-// permutation; W_l stays resident for the kernel.  Per tile:
-//   dgrad over the two seed chunks (DMMA, accumulators in registers)
-//   wgrad over the tile's rows: seed chunks as A, the H_l tile as B
-//   -> the seed ring is free: the next tile's seed chunks are requested
-//   jet VJP epilogue, reading H_l from the shared tile, storing D_l
-//   -> the H_l tile is free: the next tile's H_l rows are requested
+// the weight gradient dW_l = D_{l+1}^T H_l of the same tile.  The tile's seed D_{l+1} and
+// its H_l rows arrive by 2-D TMA loads (two 32-column planes each, rows in global order,
+// thread column tc owning rows tc*S..tc*S+S-1; rows past a segment zero-filled by the
+// tensor map) and W_l stays resident.  Per tile:
+//   dgrad over the two seed planes (DMMA, accumulators in registers)
+//   wgrad over the tile's rows: seed planes as A, the H_l planes as B
+//   -> the seed planes are free: the next tile's seed is requested
+//   jet VJP epilogue, reading H_l from shared memory, storing D_l
+//   -> the H_l planes are free: the next tile's H_l is requested
 // so the next tile's seed arrives during this epilogue and its H_l during the next dgrad.
 // dW_l accumulates in registers across the CTA's tiles and is written once per CTA, so
 // D_{l+1} and H_l are read from HBM once per layer instead of twice.
@@ -584,39 +587,56 @@ constexpr int kFusedWidth = 64;
 template <int DIM>
 struct FusedTile : MmaTile<DIM, kFusedWidth, DIM == 2 ? 16 : 8> {};
 
+// rows per TMA box of a boundary tile: the whole tile when its points fill every slot of a
+// thread column (PS * QB == S); otherwise such tiles stream by cp.async (the value is then
+// only the box shape of an unused tensor map)
+template <int DIM, int BO>
+constexpr int fused_boundary_box_rows() {
+  using TL = Tiles<DIM, BO, FusedTile<DIM>::TC>;
+  return TL::PS * TL::QB == FusedTile<DIM>::S ? FusedTile<DIM>::TR : TL::PS * TL::QB;
+}
+
 template <int DIM>
 constexpr size_t fused_smem_bytes() {
   using T = FusedTile<DIM>;
-  constexpr size_t ring = size_t(kFusedWidth / KC) * size_t(T::TR) * LDC;  // the tile's seed chunks
+  constexpr size_t planes = size_t(kFusedWidth / KC) * size_t(T::TR) * LDC;  // one tensor's tile
   constexpr size_t wres = size_t(kFusedWidth) * (kFusedWidth + 4);           // resident W_l
-  constexpr size_t htile = size_t(T::TR) * (kFusedWidth + 4);
-  constexpr size_t a = sizeof(double) * (ring + wres + htile + 2 * T::TR);
+  constexpr size_t a = sizeof(double) * (2 * planes + wres + 2);              // + 2 mbarriers
   constexpr size_t red = sizeof(double) * (T::WR * kFusedWidth * (DIM + 1) + 8 * (kFusedWidth / 16) * 4 * 32);
   return a > red ? a : red;
 }
 
 template <int DIM, int BO, bool FIRST>
 __global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
-    bwd_fused(const double* __restrict__ dnext, const double* __restrict__ w, const double* __restrict__ hcur,
-              const double* __restrict__ a1cur, double* __restrict__ dcur, const double* __restrict__ x,
-              double* __restrict__ partial, double* __restrict__ wpart, Geometry geo) {
+    bwd_fused(const __grid_constant__ CUtensorMap tm_seed_i, const __grid_constant__ CUtensorMap tm_seed_b,
+              const __grid_constant__ CUtensorMap tm_h_i, const __grid_constant__ CUtensorMap tm_h_b,
+              const double* __restrict__ dnext, const double* __restrict__ hcur, const double* __restrict__ w,
+              const double* __restrict__ a1cur, double* __restrict__ dcur,
+              const double* __restrict__ x, double* __restrict__ partial, double* __restrict__ wpart, Geometry geo) {
   constexpr int CP = kFusedWidth;
   using T = FusedTile<DIM>;
   using TL = Tiles<DIM, BO, T::TC>;
-  constexpr int S = T::S, TR = T::TR, Q = TL::Q, QB = TL::QB, LDW = CP + 4, LDH = CP + 4;
-  constexpr int NK = CP / KC;  // seed chunks per tile
-  constexpr int MK = KC / 16;  // m16 tiles of output channels per chunk
+  constexpr int S = T::S, TR = T::TR, Q = TL::Q, QB = TL::QB, PS = TL::PS, LDW = CP + 4;
+  constexpr int NK = CP / KC;  // 32-column planes per tile
+  constexpr int MK = KC / 16;  // m16 tiles of output channels per plane
   constexpr int NM = CP / 16;  // m16 tiles of output channels
   constexpr int NV = FIRST ? DIM + 1 : 1;
+  constexpr int BB = fused_boundary_box_rows<DIM, BO>();
+  constexpr bool SPLIT = BB != TR;  // boundary tiles: one box per thread column
   // wgrad split: warp -> n8 tile (warp % 8) of dW columns and row share (warp / 8)
   constexpr int RS = T::NWARPS / 8, RROWS = TR / RS;
   static_assert(CP / 8 == 8 && T::NWARPS % 8 == 0 && RROWS % 16 == 0, "wgrad warp split");
-  static_assert(NK == 2, "commit-group accounting assumes two seed chunks per tile");
-  extern __shared__ __align__(16) double smem[];
-  double* sB = smem;               // seed chunks [NK][TR][LDC]
-  double* sW = sB + NK * TR * LDC;  // W_l         [CP][LDW] (row = output channel)
-  double* sH = sW + CP * LDW;       // H_l tile    [TR][LDH]
-  int64_t* rowmap = reinterpret_cast<int64_t*>(sH + TR * LDH);  // [2][TR]
+  static_assert(NK == 2 && KC == 32 && TR <= 256, "TMA boxes: 36 columns, at most 256 rows");
+  static_assert((size_t(TR) * LDC * sizeof(double)) % 128 == 0, "every TMA destination on a 128-byte boundary");
+  extern __shared__ __align__(128) double smem[];
+  double* sB = smem;                // seed planes [NK][TR][LDC]
+  double* sH = sB + NK * TR * LDC;  // H_l planes  [NK][TR][LDC]
+  double* sW = sH + NK * TR * LDC;  // W_l         [CP][LDW] (row = output channel)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sW + CP * LDW);  // [0] seed tile, [1] H_l tile
+  if (smem_u32(smem) & 127) {  // TMA destinations need 128-byte alignment: refuse, never fault
+    if (threadIdx.x == 0) atomicExch(&g_device_fault, 2);
+    return;
+  }
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int wc = warp % T::WC, wr = warp / T::WC;
   const int64_t nint = TL::interior(geo.ni);
@@ -635,53 +655,77 @@ __global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
 #pragma unroll
     for (int e = 0; e < 4; ++e) wacc[m][e] = 0.0;
 
-  auto fill_rowmap = [&](int64_t tile, int64_t* rm) {
-    for (int r = tid; r < TR; r += T::THREADS) {
-      int tc, s;
-      tile_slot<S>(r, tc, s);
-      rm[r] = TL::row(geo, nint, tile, tc, s);
-    }
-  };
-  auto load_seed = [&](const int64_t* rm) {  // one commit group per chunk
-#pragma unroll
-    for (int kc = 0; kc < NK; ++kc) {
-      double* dB = sB + kc * TR * LDC;
-      for (int i = tid; i < TR * (KC / 2); i += T::THREADS) {
-        const int r = i / (KC / 2), p = i % (KC / 2);
-        const int64_t gr = rm[r];
-        cp_async16(dB + r * LDC + 2 * p, dnext + (gr >= 0 ? gr : 0) * CP + kc * KC + 2 * p, gr >= 0);
+  // One tensor's tile (seed or H_l) into its planes.  All threads call it.  Interior tiles
+  // (and boundary tiles whose points fill every slot) are one TMA box per plane, issued by
+  // thread 0 on `bar`; the other boundary tiles (points of fewer rows than a thread column
+  // has slots) stream by cp.async, one commit group, rows past the segment zero-filled.
+  auto tma_tile = [&](int64_t tile) { return !SPLIT || tile < nint; };
+  auto load_tile = [&](int64_t tile, double* dst, const CUtensorMap* mi, const CUtensorMap* mb, uint64_t* bar,
+                       const double* src) {
+    const bool interior = tile < nint;
+    if (SPLIT && !interior) {
+      const int64_t b0 = (tile - nint) * (int64_t(T::TC) * PS);
+      for (int i = tid; i < NK * TR * (KC / 2); i += T::THREADS) {
+        const int kc = i / (TR * (KC / 2)), rem = i % (TR * (KC / 2));
+        const int r = rem / (KC / 2), q = rem % (KC / 2);
+        const int tc = r / S, sl = r % S;
+        const int64_t b = b0 + int64_t(tc) * PS + sl / QB;
+        const bool ok = sl < PS * QB && b < geo.nb;
+        const int64_t gr = ok ? geo.ni * Q + b * QB + sl % QB : 0;
+        cp_async16(dst + kc * TR * LDC + r * LDC + 2 * q, src + gr * CP + kc * KC + 2 * q, ok);
       }
       cp_async_commit();
+      return;
     }
-  };
-  auto load_h = [&](const int64_t* rm) {  // one commit group
-    for (int i = tid; i < TR * (CP / 2); i += T::THREADS) {
-      const int r = i / (CP / 2), p = i % (CP / 2);
-      const int64_t gr = rm[r];
-      cp_async16(sH + r * LDH + 2 * p, hcur + (gr >= 0 ? gr : 0) * CP + 2 * p, gr >= 0);
+    if (tid != 0) return;
+    fence_proxy_async();  // the planes' last readers finished before the barrier that led here
+    if (interior) {
+      mbar_arrive_expect_tx(bar, NK * TR * LDC * sizeof(double));
+#pragma unroll
+      for (int kc = 0; kc < NK; ++kc) tma_load_2d(dst + kc * TR * LDC, mi, kc * KC, int(tile * T::TC * Q), bar);
+      return;
     }
-    cp_async_commit();
+    const int64_t b0 = (tile - nint) * (int64_t(T::TC) * PS);  // first boundary point
+    mbar_arrive_expect_tx(bar, NK * TR * LDC * sizeof(double));
+#pragma unroll
+    for (int kc = 0; kc < NK; ++kc) tma_load_2d(dst + kc * TR * LDC, mb, kc * KC, int(b0 * QB), bar);
   };
-  // commit groups in flight at the top of a tile: [seed 0] [seed 1] [H] (the first tile's
-  // seed 0 group also carries W_l)
-  for (int i = tid; i < CP * (CP / 2); i += T::THREADS) {
+  // bounded wait for a tile that arrived by TMA (phase bit of its barrier) or cp.async
+  auto wait_tile = [&](int64_t tile, uint64_t* bar, unsigned& ph, bool last_group) {
+    bool ok = true;
+    if (tma_tile(tile)) {
+      ok = mbar_wait(bar, ph);
+      ph ^= 1u;
+    } else if (last_group) {
+      cp_async_wait<0>();
+    } else {
+      cp_async_wait<1>();  // the seed group; the H_l group may still be in flight
+    }
+    return ok;
+  };
+  for (int i = tid; i < CP * (CP / 2); i += T::THREADS) {  // W_l, resident
     const int r = i / (CP / 2), p = i % (CP / 2);
     cp_async16(sW + r * LDW + 2 * p, w + int64_t(r) * CP + 2 * p, true);
   }
-  int buf = 0;
-  if (int64_t(blockIdx.x) < ntiles) {
-    fill_rowmap(blockIdx.x, rowmap);
-    __syncthreads();
-    load_seed(rowmap);
-    load_h(rowmap);
-  } else {
-    cp_async_commit();
+  cp_async_commit();
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
   }
-  for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, buf ^= 1) {
-    const int64_t* rm = rowmap + buf * TR;
-    int64_t* rn = rowmap + (buf ^ 1) * TR;
+  cp_async_wait<0>();
+  __syncthreads();  // W_l and the barriers visible
+  if (int64_t(blockIdx.x) < ntiles) {
+    load_tile(blockIdx.x, sB, &tm_seed_i, &tm_seed_b, &bars[0], dnext);
+    load_tile(blockIdx.x, sH, &tm_h_i, &tm_h_b, &bars[1], hcur);
+  }
+  unsigned ph_seed = 0, ph_h = 0;
+  // B fragments of the dgrad: column g of an n8 tile is slot 2j + (g & 1) of thread
+  // column wr*4 + (g >> 1)
+  const int brow = (wr * 4 + (g >> 1)) * S + (g & 1);
+  // wgrad B fragments: H_l columns 8*wn + g live in plane wn / 4
+  const double* hcol = sH + (wn >> 2) * TR * LDC + ((8 * wn) & (KC - 1)) + g;
+  for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     const bool has_next = tile + gridDim.x < ntiles;
-    if (has_next) fill_rowmap(tile + gridDim.x, rn);  // published by the barriers below
     double acc[T::MT][T::NT][4];
 #pragma unroll
     for (int i = 0; i < T::MT; ++i)
@@ -689,12 +733,14 @@ __global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
       for (int j = 0; j < T::NT; ++j)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0;
-    // dgrad: dH[ch][rows] += W_l^T[ch][cout chunk] D^T[cout chunk][rows]
+    if (__syncthreads_or(!wait_tile(tile, &bars[0], ph_seed, false))) {  // seed tile landed (bounded wait)
+      if (tid == 0) atomicExch(&g_device_fault, 1);
+      return;
+    }
+    // dgrad: dH[ch][rows] += W_l^T[ch][cout plane] D^T[cout plane][rows]
 #pragma unroll
     for (int kc = 0; kc < NK; ++kc) {
-      if (kc == 0) cp_async_wait<2>(); else cp_async_wait<1>();
-      __syncthreads();
-      const double* cB = sB + kc * TR * LDC + wr * (4 * S) * LDC;
+      const double* cB = sB + kc * TR * LDC + brow * LDC;
       const double* cA = sW + kc * KC * LDW + wc * T::WCH;
 #pragma unroll
       for (int kk = 0; kk < KC; kk += 8) {
@@ -708,23 +754,25 @@ __global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
         }
 #pragma unroll
         for (int j = 0; j < T::NT; ++j) {
-          const double b0 = cB[(8 * j + g) * LDC + kk + t];
-          const double b1 = cB[(8 * j + g) * LDC + kk + t + 4];
+          const double b0 = cB[2 * j * LDC + kk + t];
+          const double b1 = cB[2 * j * LDC + kk + t + 4];
 #pragma unroll
           for (int i = 0; i < T::MT; ++i) mma_m16n8k8(acc[i][j], a[i], b0, b1);
         }
       }
     }
-    cp_async_wait<0>();
-    __syncthreads();  // H_l tile visible
+    if (__syncthreads_or(!wait_tile(tile, &bars[1], ph_h, true))) {  // H_l tile landed
+      if (tid == 0) atomicExch(&g_device_fault, 1);
+      return;
+    }
     // wgrad: dW[cout][8*wn..+8] += D^T[cout][rows] H[rows][cin], rows of share wrs
 #pragma unroll
     for (int kc = 0; kc < NK; ++kc) {
       const double* cD = sB + kc * TR * LDC;
 #pragma unroll 4
       for (int r = wrs * RROWS; r < (wrs + 1) * RROWS; r += 8) {
-        const double b0 = sH[(r + t) * LDH + 8 * wn + g];
-        const double b1 = sH[(r + t + 4) * LDH + 8 * wn + g];
+        const double b0 = hcol[(r + t) * LDC];
+        const double b1 = hcol[(r + t + 4) * LDC];
 #pragma unroll
         for (int mm = 0; mm < MK; ++mm) {
           double a[4];
@@ -736,13 +784,13 @@ __global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
         }
       }
     }
-    __syncthreads();  // seed ring free
-    if (has_next) load_seed(rn);
-    // epilogue: jet VJP of this tile; H_l from the shared tile (row of slot s of thread
-    // column wr*4+t: the inverse of tile_slot)
+    __syncthreads();  // seed planes free
+    if (has_next) load_tile(tile + gridDim.x, sB, &tm_seed_i, &tm_seed_b, &bars[0], dnext);
+    // epilogue: jet VJP of this tile; H_l from the shared planes (slot s of thread column
+    // wr*4+t is row (wr*4+t)*S + s)
     const int tc = wr * 4 + t;
-    const double* hrow = sH + (wr * (4 * S) + 2 * t) * LDH;
-    auto hslot = [&](int s, int ch) { return hrow[(8 * (s >> 1) + (s & 1)) * LDH + ch]; };
+    const double* hrow = sH + (tc * S) * LDC;
+    auto hslot = [&](int s, int ch) { return hrow[(ch >> 5) * TR * LDC + s * LDC + (ch & (KC - 1))]; };
     const bool interior = tile < nint;
 #pragma unroll
     for (int i = 0; i < T::MT; ++i) {
@@ -798,10 +846,9 @@ __global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
         }
       }
     }
-    __syncthreads();  // H_l tile free
-    if (has_next) load_h(rn);
+    __syncthreads();  // H_l planes free
+    if (has_next) load_tile(tile + gridDim.x, sH, &tm_h_i, &tm_h_b, &bars[1], hcur);
   }
-  cp_async_wait<0>();
   // weight-gradient partial of this CTA: row shares combined in fixed order through smem
   __syncthreads();
   double* wsh = smem + T::WR * CP * NV;  // [8 warps][NM][4][32 lanes]
@@ -856,6 +903,10 @@ __global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
     for (int r = 0; r < T::WR; ++r) s += red[r * CP * NV + idx];
     partial[int64_t(blockIdx.x) * CP * NV + idx] = s;
   }
+  if (tid == 0) {  // every phase completed before the last barrier
+    mbar_inval(&bars[0]);
+    mbar_inval(&bars[1]);
+  }
 }
 
 // ----------------------------------------------------------------------------------
@@ -865,7 +916,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     wgrad_kernel(const double* __restrict__ d, int kout, const double* __restrict__ h, int kin,
                  Geometry geo, int64_t rows_per_split, double* __restrict__ wpart) {
   constexpr int MT = BM / 32, NT = BN / 32, LDA = BM + 4, LDB = BN + 4;
-  extern __shared__ __align__(16) double smem[];
+  extern __shared__ __align__(128) double smem[];
   double* sA = smem;                     // [stage][KC rows][BM+4]
   double* sB = sA + kStages * KC * LDA;  // [stage][KC rows][BN+4]
   const int split = blockIdx.x;
@@ -981,7 +1032,7 @@ __global__ void __launch_bounds__(kThreads)
   constexpr int LD = CP + 2;
   constexpr int PARTIAL = NF * CP + NF + 1 + CP;  // dW_L | db_L | loss | db_{L-1}
   static_assert(kThreads % CP == 0, "channel ownership must be fixed per thread");
-  extern __shared__ __align__(16) double smem[];
+  extern __shared__ __align__(128) double smem[];
   double* sH = smem;                   // [kHeadRows][LD]
   double* sW = sH + kHeadRows * LD;    // [NF][CP]
   double* sY = sW + NF * CP;           // [kHeadRows][NF]
@@ -1239,7 +1290,7 @@ __global__ void __launch_bounds__(HeadTile<DIM>::THREADS, HeadTile<DIM>::MINB)
   static_assert(NK == 2 && kStages == 2, "one chunk of lookahead per tile");
   static_assert(T::NWARPS == CP / 8 && NF <= 8, "warp w owns output-gradient columns 8w..8w+7");
   constexpr int RING = (kStages * TR * LDC > TR * LDH) ? kStages * TR * LDC : TR * LDH;
-  extern __shared__ __align__(16) double smem[];
+  extern __shared__ __align__(128) double smem[];
   double* sB = smem;         // activation chunks [stage][TR][LDC] during the mainloop
   double* sH = smem;         // H_L tile [TR][CP+4], natural row order, during the epilogue
   double* sA = sB + RING;    // W_{L-1} resident  [CP][KIN+4]
@@ -1699,6 +1750,40 @@ int pad_width(int c) {
   return -1;
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda)
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiled tensor_map_encoder() {
+  static EncodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(p);
+  });
+  return fn;
+}
+
+// [rows][cols] row-major FP64 segment read in boxes of box_rows x box_cols; boxes reaching
+// past the segment (rows or columns) read zeros
+cudaError_t row_tensor_map(CUtensorMap* m, const double* base, int64_t rows, int cols, int box_cols, int box_rows) {
+  const EncodeTiled enc = tensor_map_encoder();
+  if (!enc) return cudaErrorNotSupported;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (cols * sizeof(double)) % 16 || (box_cols * sizeof(double)) % 16)
+    return cudaErrorInvalidValue;
+  const cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows > 0 ? rows : 1)};
+  const cuuint64_t strides[1] = {cuuint64_t(cols) * sizeof(double)};
+  const cuuint32_t box[2] = {cuuint32_t(box_cols), cuuint32_t(box_rows)};
+  const cuuint32_t elem[2] = {1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT64, 2, const_cast<double*>(base), dims, strides, box, elem,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 template <typename K>
 int occupancy(K kernel, size_t smem, int threads) {
   int n = 0;
@@ -1767,10 +1852,23 @@ struct FusedOps {
     using TL = Tiles<DIM, BO, T::TC>;
     return TL::interior(g.ni) + TL::boundary(g.nb);
   }
-  static void launch(int grid, cudaStream_t st, const double* dn, const double* w, const double* h, const double* a1,
-                     double* dc, const double* x, double* part, double* wp, Geometry g) {
-    bwd_fused<DIM, BO, FIRST><<<grid, FusedTile<DIM>::THREADS, fused_smem_bytes<DIM>(), st>>>(dn, w, h, a1, dc, x, part,
-                                                                                              wp, g);
+  static cudaError_t launch(int grid, cudaStream_t st, const double* dn, const double* w, const double* h,
+                            const double* a1, double* dc, const double* x, double* part, double* wp, Geometry g) {
+    using T = FusedTile<DIM>;
+    using TL = Tiles<DIM, BO, T::TC>;
+    constexpr int BB = fused_boundary_box_rows<DIM, BO>();
+    const int64_t ri = g.ni * TL::Q, rb = g.nb * TL::QB;  // interior / boundary segment rows
+    if (ri > INT32_MAX - T::TR || rb > INT32_MAX - T::TR) return cudaErrorInvalidValue;  // TMA rows are int32
+    CUtensorMap m[4];
+    cudaError_t e;
+    if ((e = row_tensor_map(&m[0], dn, ri, kFusedWidth, LDC, T::TR)) != cudaSuccess ||
+        (e = row_tensor_map(&m[1], dn + ri * kFusedWidth, rb, kFusedWidth, LDC, BB)) != cudaSuccess ||
+        (e = row_tensor_map(&m[2], h, ri, kFusedWidth, LDC, T::TR)) != cudaSuccess ||
+        (e = row_tensor_map(&m[3], h + ri * kFusedWidth, rb, kFusedWidth, LDC, BB)) != cudaSuccess)
+      return e;
+    bwd_fused<DIM, BO, FIRST><<<grid, T::THREADS, fused_smem_bytes<DIM>(), st>>>(m[0], m[1], m[2], m[3], dn, h, w, a1,
+                                                                                dc, x, part, wp, g);
+    return cudaGetLastError();
   }
 };
 
@@ -2217,13 +2315,15 @@ static int run_eval(const flashns_b200_plan* p, const double* coordinates, const
       };
       mark();
       if (p->fused[l]) {
+        cudaError_t fe = cudaSuccess;
         auto ff = [&](auto ops) {
-          ops.launch(p->grid_bwd[l], stream, dn, Wp(L), ws + p->off_h[l], ws + p->off_a1[l],
-                     ws + p->off_d[l % 2], coordinates, ws + (l == 1 ? p->off_coord : p->off_bb[l]),
-                     ws + p->off_wg[l], g);
+          fe = ops.launch(p->grid_bwd[l], stream, dn, Wp(L), ws + p->off_h[l], ws + p->off_a1[l],
+                          ws + p->off_d[l % 2], coordinates, ws + (l == 1 ? p->off_coord : p->off_bb[l]),
+                          ws + p->off_wg[l], g);
         };
         if (l == 1) with_fused<true>(p->dim, p->bo, ff);
         else with_fused<false>(p->dim, p->bo, ff);
+        if (fe != cudaSuccess) return int(fe);
         if ((e = cudaGetLastError()) != cudaSuccess) return int(e);
         continue;
       }
