@@ -64,15 +64,28 @@ def kovasznay_exact(x, re=20.0):
     return u, v, p, psi
 
 
-def kovasznay(interior, boundary, *, re=20.0, seed=1, boundary_order=1):
+def unit_samples(n, dim, gen, sampling, seed, stream=0):
+    """n points in [0, 1)^dim: uniform from `gen`, or scrambled Sobol (Owen scrambling seeded
+    by `seed` and `stream`, so separate point families get independent sequences)."""
+    if sampling == "uniform":
+        return torch.rand(n, dim, generator=gen, dtype=torch.float64)
+    if sampling == "sobol":
+        if n == 0:
+            return torch.zeros(0, dim, dtype=torch.float64)
+        engine = torch.quasirandom.SobolEngine(dim, scramble=True, seed=seed * 1009 + stream)
+        return engine.draw(n, dtype=torch.float64)
+    raise ValueError("sampling must be 'uniform' or 'sobol'")
+
+
+def kovasznay(interior, boundary, *, re=20.0, seed=1, boundary_order=1, sampling="uniform"):
     gen = torch.Generator(device="cpu").manual_seed(seed)
     lo = torch.tensor([-0.5, -0.5], dtype=torch.float64)
     span = torch.tensor([1.5, 2.0], dtype=torch.float64)
-    xi = lo + span * torch.rand(interior, 2, generator=gen, dtype=torch.float64)
+    xi = lo + span * unit_samples(interior, 2, gen, sampling, seed)
     counts = [boundary // 4 + (1 if k < boundary % 4 else 0) for k in range(4)]
     edges = []
     for k, n in enumerate(counts):
-        s = torch.rand(n, generator=gen, dtype=torch.float64)
+        s = unit_samples(n, 1, gen, sampling, seed, stream=k + 1)[:, 0]
         if k == 0:
             e = torch.stack((-0.5 + 1.5 * s, torch.full_like(s, -0.5)), 1)
         elif k == 1:
@@ -109,16 +122,15 @@ def taylor_green_exact(x, nu=0.01):
     return u, v, p, psi
 
 
-def taylor_green(interior, boundary, *, nu=0.01, seed=1, boundary_order=1):
+def taylor_green(interior, boundary, *, nu=0.01, seed=1, boundary_order=1, sampling="uniform"):
     gen = torch.Generator(device="cpu").manual_seed(seed)
     two_pi = 2 * math.pi
-    xi = torch.rand(interior, 3, generator=gen, dtype=torch.float64) * torch.tensor([two_pi, two_pi, 1.0],
-                                                                                   dtype=torch.float64)
+    xi = unit_samples(interior, 3, gen, sampling, seed) * torch.tensor([two_pi, two_pi, 1.0], dtype=torch.float64)
     n0 = boundary // 2
-    init = torch.rand(n0, 3, generator=gen, dtype=torch.float64) * torch.tensor([two_pi, two_pi, 0.0],
-                                                                               dtype=torch.float64)
-    side = torch.rand(boundary - n0, 3, generator=gen, dtype=torch.float64) * torch.tensor([two_pi, two_pi, 1.0],
-                                                                                          dtype=torch.float64)
+    init = unit_samples(n0, 3, gen, sampling, seed, stream=1) * torch.tensor([two_pi, two_pi, 0.0],
+                                                                             dtype=torch.float64)
+    side = unit_samples(boundary - n0, 3, gen, sampling, seed, stream=2) * torch.tensor([two_pi, two_pi, 1.0],
+                                                                                        dtype=torch.float64)
     face = torch.arange(boundary - n0) % 4
     side[face == 0, 0] = 0.0
     side[face == 1, 0] = two_pi

@@ -20,6 +20,7 @@ import json
 import math
 import os
 import time
+from pathlib import Path
 
 import torch
 import torch.distributed as dist
@@ -54,15 +55,29 @@ class Acceptance:
         return [float(e) for e in err.cpu()]
 
 
+def save_checkpoint(path, flat, meta):
+    """Final parameters and the run description as a torch checkpoint (the record of
+    experiments/pinn_solver/solve.py:255-266); returns the file's sha256."""
+    import hashlib
+    path = Path(path)
+    torch.save({"flat_parameters": flat.detach().cpu(), **meta}, path)
+    return hashlib.sha256(path.read_bytes()).hexdigest()
+
+
+def load_checkpoint(path):
+    return torch.load(Path(path), map_location="cpu", weights_only=True)
+
+
 def solve(*, interior=16384, boundary=4096, widths=(2, 64, 64, 64, 64, 2), re=20.0, seed=1, init_seed=0,
           boundary_weight=5.0, tol_uv=1e-3, tol_p=1e-2, max_iterations=50000, check_every=100, history=50,
-          adam_steps=3000, adam_lr=1e-3, grid=201, device=None, log=None, time_limit=None, optimizer="device"):
+          adam_steps=3000, adam_lr=1e-3, grid=201, device=None, log=None, time_limit=None, optimizer="device",
+          sampling="uniform", initial=None, return_parameters=False):
     start = time.perf_counter()
     world = dist.get_world_size() if dist.is_initialized() else 1
     rank = dist.get_rank() if dist.is_initialized() else 0
     device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
     widths = list(widths)
-    pts = kovasznay(interior, boundary, re=re, seed=seed, boundary_order=1)
+    pts = kovasznay(interior, boundary, re=re, seed=seed, boundary_order=1, sampling=sampling)
     loss = NSLoss(viscosity=1.0 / re, boundary_weight=boundary_weight)
     if world > 1:
         from flashns_b200.distributed import DistributedEvaluator
@@ -72,7 +87,8 @@ def solve(*, interior=16384, boundary=4096, widths=(2, 64, 64, 64, 64, 2), re=20
                              head="psi", boundary_order=1, loss=loss, device=device)
     accept = Acceptance(widths, re, device, grid)
     ws, bs = xavier_normal(widths, init_seed)
-    flat = torch.nn.Parameter(flat_parameters(ws, bs).to(device))
+    start_params = flat_parameters(ws, bs) if initial is None else initial.detach().to(torch.float64).reshape(-1)
+    flat = torch.nn.Parameter(start_params.to(device).contiguous())
     out = torch.empty(ev.parameters + 1, dtype=torch.float64, device=device)
     # capture one evaluation (the parameter storage stays at the same address)
     stream = torch.cuda.Stream(device)
@@ -148,11 +164,12 @@ def solve(*, interior=16384, boundary=4096, widths=(2, 64, 64, 64, 64, 2), re=20
     torch.cuda.synchronize(device)
     wall = time.perf_counter() - start
     del graph
-    return {"accepted": accepted, "wall_s": wall, "setup_s": setup, **phases, "optimizer": optimizer,
-            "iterations": iterations,
-            "evaluations": evaluations[0], "rel_l2_u": metrics[0], "rel_l2_v": metrics[1], "rel_l2_p": metrics[2],
-            "final_loss": float(loss_view), "n_gpus": world, "interior": interior, "boundary": boundary,
-            "widths": widths, "re": re, "seed": seed, "init_seed": init_seed}
+    result = {"accepted": accepted, "wall_s": wall, "setup_s": setup, **phases, "optimizer": optimizer,
+              "iterations": iterations,
+              "evaluations": evaluations[0], "rel_l2_u": metrics[0], "rel_l2_v": metrics[1], "rel_l2_p": metrics[2],
+              "final_loss": float(loss_view), "n_gpus": world, "interior": interior, "boundary": boundary,
+              "widths": widths, "re": re, "seed": seed, "init_seed": init_seed, "sampling": sampling}
+    return (result, flat.detach().cpu()) if return_parameters else result
 
 
 def main():
@@ -166,6 +183,10 @@ def main():
     ap.add_argument("--history", type=int, default=50)
     ap.add_argument("--time-limit", type=float, default=None)
     ap.add_argument("--optimizer", choices=["device", "torch"], default="device")
+    ap.add_argument("--sampling", choices=["uniform", "sobol"], default="uniform")
+    ap.add_argument("--initial", type=Path, default=None, help="start from a checkpoint's flat parameters")
+    ap.add_argument("--output", type=Path, default=None,
+                    help="write OUTPUT.pt (final parameters + run description) and OUTPUT.json (result)")
     ap.add_argument("--quiet", action="store_true")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -174,14 +195,25 @@ def main():
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
-    result = solve(seed=args.seed, init_seed=args.init_seed, max_iterations=args.max_iterations,
-                   check_every=args.check_every, boundary_weight=args.boundary_weight, adam_steps=args.adam_steps,
-                   history=args.history, time_limit=args.time_limit, optimizer=args.optimizer,
-                   log=None if args.quiet else lambda s: print(s, flush=True))
+    initial = load_checkpoint(args.initial)["flat_parameters"] if args.initial else None
+    result, final = solve(seed=args.seed, init_seed=args.init_seed, max_iterations=args.max_iterations,
+                          check_every=args.check_every, boundary_weight=args.boundary_weight,
+                          adam_steps=args.adam_steps, history=args.history, time_limit=args.time_limit,
+                          optimizer=args.optimizer, sampling=args.sampling, initial=initial,
+                          log=None if args.quiet else lambda s: print(s, flush=True), return_parameters=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if int(os.environ.get("RANK", "0")) == 0:
+        if args.output is not None:
+            meta = {"problem": {"name": "kovasznay", "re": result["re"], "interior": result["interior"],
+                                "boundary": result["boundary"], "widths": result["widths"],
+                                "sampling": args.sampling},
+                    "protocol": {k: getattr(args, k) for k in ("adam_steps", "history", "check_every",
+                                                               "boundary_weight", "max_iterations")},
+                    "seed": args.seed, "init_seed": args.init_seed}
+            result["checkpoint_sha256"] = save_checkpoint(args.output.with_suffix(".pt"), final, meta)
+            args.output.with_suffix(".json").write_text(json.dumps(result, indent=1) + "\n")
         print(json.dumps(result), flush=True)
 
 

@@ -114,3 +114,37 @@ def test_residual_terms_match_reference_table():
         assert len(mine) == 9
         for a, b in zip(mine, ref):
             assert norm(a) == norm(b)
+
+
+def test_sobol_sampling_is_seeded_and_in_domain():
+    """Scrambled-Sobol point sets (the reference's data kind): deterministic per seed,
+    inside the domain, boundary points on the edges / faces, weights normalized."""
+    import torch
+    from flashns_b200.problems import kovasznay, taylor_green
+    a = kovasznay(512, 128, seed=3, sampling="sobol")
+    b = kovasznay(512, 128, seed=3, sampling="sobol")
+    c = kovasznay(512, 128, seed=4, sampling="sobol")
+    assert torch.equal(a.x, b.x) and not torch.equal(a.x, c.x)
+    xi = a.x[:512]
+    assert float(xi[:, 0].min()) >= -0.5 and float(xi[:, 0].max()) < 1.0
+    assert float(xi[:, 1].min()) >= -0.5 and float(xi[:, 1].max()) < 1.5
+    xb = a.x[512:]
+    on_edge = (xb[:, 0] == -0.5) | (xb[:, 0] == 1.0) | (xb[:, 1] == -0.5) | (xb[:, 1] == 1.5)
+    assert bool(on_edge.all())
+    assert abs(float(a.pde_weights.sum()) - 1.0) < 1e-12
+    t = taylor_green(256, 64, seed=2, sampling="sobol")
+    assert t.x.shape == (320, 3) and float(t.x[256:288, 2].abs().max()) == 0.0  # initial slab t = 0
+
+
+def test_solver_checkpoint_round_trip(tmp_path):
+    """OUTPUT.pt holds the final flat parameters and the run description; its sha256 is
+    what the solver reports."""
+    import hashlib
+    import torch
+    from flashns_b200.solver import load_checkpoint, save_checkpoint
+    flat = torch.linspace(-1.0, 1.0, 12802, dtype=torch.float64)
+    meta = {"problem": {"name": "kovasznay", "re": 20.0}, "protocol": {"adam_steps": 3000}, "seed": 1}
+    digest = save_checkpoint(tmp_path / "run.pt", flat, meta)
+    assert digest == hashlib.sha256((tmp_path / "run.pt").read_bytes()).hexdigest()
+    back = load_checkpoint(tmp_path / "run.pt")
+    assert torch.equal(back["flat_parameters"], flat) and back["problem"]["re"] == 20.0 and back["seed"] == 1
