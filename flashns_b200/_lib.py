@@ -29,7 +29,6 @@ SIGNATURES = {
     "flashns_b200_eval_static": [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr],
     "flashns_b200_fields": [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_ptr],
     "flashns_b200_row_dots": [_c_ptr, _c_i64, _c_int, _c_ptr, _c_ptr, _c_i64, _c_ptr],
-    "flashns_b200_axpy": [_c_ptr, _c_dbl, _c_ptr, _c_ptr, _c_i64, _c_ptr],
     "flashns_b200_lbfgs_pair_slot": [_c_ptr] * 6 + [_c_i64, _c_ptr, _c_i64, _c_ptr],
     "flashns_b200_lbfgs_ring_dots": [_c_ptr, _c_ptr, _c_i64, _c_int, _c_ptr, _c_ptr, _c_int, _c_ptr, _c_i64, _c_ptr],
     "flashns_b200_lbfgs_commit": [_c_ptr, _c_ptr, _c_ptr, _c_int, _c_ptr, _c_ptr],

@@ -35,13 +35,6 @@ __global__ void __launch_bounds__(kVecThreads)
   if (threadIdx.x == 0) out[blockIdx.x] = red[0];
 }
 
-// x = x0 + t d
-__global__ void __launch_bounds__(kVecThreads)
-    axpy(const double* __restrict__ x0, double t, const double* __restrict__ d, double* __restrict__ x, int64_t n) {
-  for (int64_t j = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; j < n; j += int64_t(gridDim.x) * blockDim.x)
-    x[j] = x0[j] + t * d[j];
-}
-
 // ---- device-resident L-BFGS state: pairs in a ring of `slots` = history + 1 physical rows
 // (one spare).  state = {k stored pairs, h spare slot, have_pair, 0}; the stored pairs are
 // the physical rows (h - k + i) mod slots, i = 0 (oldest) .. k-1 (newest).
@@ -245,13 +238,6 @@ int flashns_b200_row_dots(const double* rows, int64_t stride, int k, const doubl
   if (k == 0) return int(cudaSuccess);
   if (!rows || !v || !out) return int(cudaErrorInvalidValue);
   row_dots<<<unsigned(k), kVecThreads, 0, stream>>>(rows, stride, v, out, n);
-  return int(cudaGetLastError());
-}
-
-int flashns_b200_axpy(const double* x0, double t, const double* d, double* x, int64_t n, cudaStream_t stream) {
-  if (n < 0 || (n && (!x0 || !d || !x))) return int(cudaErrorInvalidValue);
-  if (n == 0) return int(cudaSuccess);
-  axpy<<<vec_grid(n), kVecThreads, 0, stream>>>(x0, t, d, x, n);
   return int(cudaGetLastError());
 }
 

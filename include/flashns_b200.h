@@ -178,11 +178,9 @@ int flashns_b200_residuals(int head, int dim, const double* jets, double nu, dou
 
 /* Vector kernels of the device-resident L-BFGS (no reference counterpart: the reference
  * uses torch.optim.LBFGS, experiments/pinn_solver/solve.py:150-167).
- *   row_dots:      out[r] = rows[r] . v for r < k (rows [k][stride]); fixed-order reductions
- *   axpy:          x = x0 + t d */
+ *   row_dots:      out[r] = rows[r] . v for r < k (rows [k][stride]); fixed-order reductions */
 int flashns_b200_row_dots(const double* rows, int64_t stride, int k, const double* v, double* out, int64_t n,
                           cudaStream_t stream);
-int flashns_b200_axpy(const double* x0, double t, const double* d, double* x, int64_t n, cudaStream_t stream);
 
 /* Device-resident L-BFGS state.  The curvature pairs live in a ring of `slots` = history + 1
  * physical rows (one spare) of S and Y ([slots][stride] each); SY[a][b] = s_a . y_b and
