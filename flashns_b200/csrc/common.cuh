@@ -81,6 +81,12 @@ __device__ __forceinline__ void tma_load_2d(void* smem, const void* tensor_map, 
       : "memory");
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream serialization
+// may start while its predecessor drains; it waits here before touching the predecessor's
+// outputs (a no-op without a programmatic predecessor), then lets its own dependents start.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
 // D = A*B + D with FP64 tensor-core MMA (DMMA).  Fragment layout (PTX ISA,
 // m16n8k8 .f64): g = lane/4, t = lane%4;
 //   a0=A[g][t] a1=A[g+8][t] a2=A[g][t+4] a3=A[g+8][t+4]

@@ -235,6 +235,8 @@ __global__ void __launch_bounds__(FwdTile<DIM, CP>::THREADS, FwdTile<DIM, CP>::M
   if (int64_t(blockIdx.x) < ntiles) fill_rowmap(blockIdx.x, rowmap);
   cp_async_wait<0>();
   __syncthreads();  // W_l, barriers and the first rowmap visible
+  pdl_wait();  // H_l is the predecessor's output
+  pdl_trigger();
   if (int64_t(blockIdx.x) < ntiles) load(0, 0, rowmap);
   unsigned parity = 0;  // bit st: phase parity of the next completion of stage st
   int buf = 0;
@@ -405,6 +407,8 @@ __global__ void __launch_bounds__(BwdTile<DIM, CP>::THREADS, 1)
   };
   static_assert(kStages == 2, "commit-group accounting: [chunk 0] [H] [chunk 1] ...");
   int buf = 0;
+  pdl_wait();  // D_{l+1} is the predecessor's output
+  pdl_trigger();
   if (iters > 0 && tile_of(0) < ntiles) {
     fill_rowmap(tile_of(0), rowmap);
     __syncthreads();
@@ -714,6 +718,8 @@ __global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
   }
   cp_async_wait<0>();
   __syncthreads();  // W_l and the barriers visible
+  pdl_wait();  // D_{l+1} is the predecessor's output
+  pdl_trigger();
   if (int64_t(blockIdx.x) < ntiles) {
     load_tile(blockIdx.x, sB, &tm_seed_i, &tm_seed_b, &bars[0], dnext);
     load_tile(blockIdx.x, sH, &tm_h_i, &tm_h_b, &bars[1], hcur);
@@ -927,6 +933,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int64_t r0 = int64_t(split) * rows_per_split;
   const int64_t r1 = (r0 + rows_per_split < geo.rows) ? r0 + rows_per_split : geo.rows;
   const int nk = r1 > r0 ? int((r1 - r0 + KC - 1) / KC) : 0;
+  pdl_wait();  // D is the predecessor's output
+  pdl_trigger();
   auto load = [&](int kc, int stage) {
     double* dA = sA + stage * KC * LDA;
     for (int i = threadIdx.x; i < KC * (BM / 2); i += kThreads) {
@@ -1039,6 +1047,8 @@ __global__ void __launch_bounds__(kThreads)
   double* sD = sY + kHeadRows * NF;    // [kHeadRows][NF]
   double* sRed = sD + kHeadRows * NF;  // [kThreads] reduction scratch
   for (int i = threadIdx.x; i < NF * CP; i += kThreads) sW[i] = wL[i];
+  pdl_wait();  // H_L is the predecessor's output
+  pdl_trigger();
 
   const int64_t nint = (geo.ni + TPI - 1) / TPI;
   const int64_t ntiles = nint + (geo.nb + TPB - 1) / TPB;
@@ -1329,6 +1339,8 @@ __global__ void __launch_bounds__(HeadTile<DIM>::THREADS, HeadTile<DIM>::MINB)
   double wacc[4] = {0.0, 0.0, 0.0, 0.0};  // dW_L[g][8 warp + 2t (+1)] (rows g < NF)
   double bacc = 0.0, lacc = 0.0, cacc[2] = {0.0, 0.0};
   int buf = 0;
+  pdl_wait();  // H_{L-1} is the predecessor's output
+  pdl_trigger();
   if (int64_t(blockIdx.x) < ntiles) {
     fill_rowmap(blockIdx.x, rowmap);
     __syncthreads();
@@ -1578,6 +1590,8 @@ __global__ void __launch_bounds__(kThreads)
                 double* __restrict__ h1, double* __restrict__ a1, int cp, Geometry geo) {
   constexpr int Q = Basis<DIM>::Q, QB = BO ? DIM + 1 : 1;
   const int64_t total = (geo.ni + geo.nb) * cp;
+  pdl_wait();  // W_0 may be the parameter packing's output
+  pdl_trigger();
   for (int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
        idx += int64_t(gridDim.x) * blockDim.x) {
     const int64_t p = idx / cp;
@@ -1684,6 +1698,8 @@ __global__ void __launch_bounds__(kReduceCols * kReduceRows)
   const int64_t f = int64_t(blockIdx.x) * kReduceCols + threadIdx.x;
   const int y = threadIdx.y;
   double v = 0.0;
+  pdl_wait();  // the partials of every earlier kernel
+  pdl_trigger();
   if (f == tab.params) {
     v = strided_sum(ws + tab.loss_part, tab.loss_stride, tab.loss_count, y, kReduceRows);
   } else if (f < tab.params) {
@@ -1750,6 +1766,27 @@ int pad_width(int c) {
   return -1;
 }
 
+// Launches of one evaluation after its first kernel may overlap the predecessor's tail
+// (programmatic stream serialization); every kernel waits (griddepcontrol.wait) before it
+// touches its predecessor's outputs.  Set by run_eval around its launch sequence.
+thread_local bool t_programmatic = false;
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = t_programmatic ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda)
 using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -1814,7 +1851,8 @@ struct FwdOps {
   }
   static void launch(int grid, cudaStream_t st, const double* hin, int kin, const double* w, const double* b,
                      double* hout, double* a1, Geometry g) {
-    fwd_layer<DIM, CP, BO><<<grid, T::THREADS, fwd_smem_bytes<DIM, CP>(kin), st>>>(hin, kin, w, b, hout, a1, g);
+    launch_kernel(fwd_layer<DIM, CP, BO>, grid, T::THREADS, fwd_smem_bytes<DIM, CP>(kin), st, hin, kin, w, b, hout, a1,
+                  g);
   }
 };
 
@@ -1834,8 +1872,8 @@ struct BwdOps {
   }
   static void launch(int grid, cudaStream_t st, const double* dn, int kout, const double* w, const double* h,
                      const double* a1, double* dc, const double* x, double* cp, Geometry g) {
-    bwd_layer<DIM, CP, BO, FIRST><<<grid, BwdTile<DIM, CP>::THREADS, bwd_smem_bytes<DIM, CP>(), st>>>(
-        dn, kout, w, h, a1, dc, x, cp, g);
+    launch_kernel(bwd_layer<DIM, CP, BO, FIRST>, grid, BwdTile<DIM, CP>::THREADS, bwd_smem_bytes<DIM, CP>(), st, dn,
+                  kout, w, h, a1, dc, x, cp, g);
   }
 };
 
@@ -1866,9 +1904,8 @@ struct FusedOps {
         (e = row_tensor_map(&m[2], h, ri, kFusedWidth, LDC, T::TR)) != cudaSuccess ||
         (e = row_tensor_map(&m[3], h + ri * kFusedWidth, rb, kFusedWidth, LDC, BB)) != cudaSuccess)
       return e;
-    bwd_fused<DIM, BO, FIRST><<<grid, T::THREADS, fused_smem_bytes<DIM>(), st>>>(m[0], m[1], m[2], m[3], dn, h, w, a1,
-                                                                                dc, x, part, wp, g);
-    return cudaGetLastError();
+    return launch_kernel(bwd_fused<DIM, BO, FIRST>, grid, T::THREADS, fused_smem_bytes<DIM>(), st, m[0], m[1], m[2],
+                         m[3], dn, h, w, a1, dc, x, part, wp, g);
   }
 };
 
@@ -1898,8 +1935,8 @@ struct HeadOps {
   static void launch(int grid, cudaStream_t st, const double* h, const double* a1, const double* w, const double* b,
                      const double* pw, const double* bw, const double* tg, double nu, double gm, double bc, double* dl,
                      const double* x, double* cpart, double* hpart, Geometry g) {
-    head_layer<DIM, CP, BO, HEAD, FIRST><<<grid, kThreads, head_smem_bytes<DIM, CP, NF>(), st>>>(
-        h, a1, w, b, pw, bw, tg, nu, gm, bc, dl, x, cpart, hpart, g);
+    launch_kernel(head_layer<DIM, CP, BO, HEAD, FIRST>, grid, kThreads, head_smem_bytes<DIM, CP, NF>(), st, h, a1, w,
+                  b, pw, bw, tg, nu, gm, bc, dl, x, cpart, hpart, g);
   }
 };
 
@@ -1920,8 +1957,8 @@ struct FwdHeadOps {
   static void launch(int grid, cudaStream_t st, const double* hin, const double* w, const double* b,
                      const double* wl, const double* bl, const double* pw, const double* bw, const double* tg,
                      double nu, double gm, double bc, double* dl, double* hpart, Geometry g) {
-    fwd_head<DIM, BO, HEAD><<<grid, HeadTile<DIM>::THREADS, fwd_head_smem_bytes<DIM, NF>(), st>>>(
-        hin, w, b, wl, bl, pw, bw, tg, nu, gm, bc, dl, hpart, g);
+    launch_kernel(fwd_head<DIM, BO, HEAD>, grid, HeadTile<DIM>::THREADS, fwd_head_smem_bytes<DIM, NF>(), st, hin, w, b,
+                  wl, bl, pw, bw, tg, nu, gm, bc, dl, hpart, g);
   }
 };
 
@@ -1979,7 +2016,7 @@ struct WgradOps {
   static cudaError_t setup() { return allow_smem(wgrad_kernel<BM, BN>, smem()); }
   static void launch(dim3 grid, cudaStream_t st, const double* d, int kout, const double* h, int kin, Geometry g,
                      int64_t rps, double* wp) {
-    wgrad_kernel<BM, BN><<<grid, kThreads, smem(), st>>>(d, kout, h, kin, g, rps, wp);
+    launch_kernel(wgrad_kernel<BM, BN>, grid, kThreads, smem(), st, d, kout, h, kin, g, rps, wp);
   }
 };
 
@@ -1994,10 +2031,10 @@ bool with_wgrad(int bm, int bn, F&& f) {
 
 int first_launch(int dim, int bo, int grid, cudaStream_t st, const double* x, const double* w, const double* b,
                  double* h, double* a1, int cp, Geometry g) {
-  if (dim == 2 && bo == 0) first_layer<2, 0><<<grid, kThreads, 0, st>>>(x, w, b, h, a1, cp, g);
-  else if (dim == 2) first_layer<2, 1><<<grid, kThreads, 0, st>>>(x, w, b, h, a1, cp, g);
-  else if (bo == 0) first_layer<3, 0><<<grid, kThreads, 0, st>>>(x, w, b, h, a1, cp, g);
-  else first_layer<3, 1><<<grid, kThreads, 0, st>>>(x, w, b, h, a1, cp, g);
+  if (dim == 2 && bo == 0) launch_kernel(first_layer<2, 0>, grid, kThreads, 0, st, x, w, b, h, a1, cp, g);
+  else if (dim == 2) launch_kernel(first_layer<2, 1>, grid, kThreads, 0, st, x, w, b, h, a1, cp, g);
+  else if (bo == 0) launch_kernel(first_layer<3, 0>, grid, kThreads, 0, st, x, w, b, h, a1, cp, g);
+  else launch_kernel(first_layer<3, 1>, grid, kThreads, 0, st, x, w, b, h, a1, cp, g);
   return int(cudaGetLastError());
 }
 
@@ -2257,12 +2294,20 @@ static int run_eval(const flashns_b200_plan* p, const double* coordinates, const
   double* ws = static_cast<double*>(workspace);
   const LayerTable& tab = p->tab;
   cudaError_t e = cudaSuccess;
+  // the first kernel of the evaluation follows the caller's work normally; the rest may start
+  // under their predecessor's tail (not while per-kernel events are being recorded)
+  struct ProgrammaticScope {
+    ~ProgrammaticScope() { t_programmatic = false; }
+  } programmatic_scope;
+  t_programmatic = false;
+  const bool overlap = events == nullptr;
   if (!p->direct) {
     int64_t packed = 0;
     for (int l = 0; l < p->n_aff; ++l) packed += int64_t(tab.l[l].coutp) * tab.l[l].cinp + tab.l[l].coutp;
     mark();
     pack_params<<<unsigned((packed + kThreads - 1) / kThreads), kThreads, 0, stream>>>(parameters, ws, tab);
     if ((e = cudaGetLastError()) != cudaSuccess) return int(e);
+    t_programmatic = overlap;
   }
   // padded layer buffers, or the flat vector itself when no layer needs padding
   auto Wp = [&](const LayerDesc& L) -> const double* { return p->direct ? parameters + L.w_flat : ws + L.w_buf; };
@@ -2275,6 +2320,7 @@ static int run_eval(const flashns_b200_plan* p, const double* coordinates, const
     int r = first_launch(p->dim, p->bo, p->grid_first, stream, coordinates, Wp(L0), Bp(L0),
                          ws + p->off_h[1], ws + p->off_a1[1], p->padded[1], g);
     if (r) return r;
+    t_programmatic = overlap;
     for (int l = 1; l < nh - (p->fused_head ? 1 : 0); ++l) {
       const LayerDesc& L = tab.l[l];
       mark();
@@ -2340,8 +2386,8 @@ static int run_eval(const flashns_b200_plan* p, const double* coordinates, const
     }
   }
   mark();
-  reduce_grads<<<unsigned((tab.params + 1 + kReduceCols - 1) / kReduceCols), dim3(kReduceCols, kReduceRows), 0, stream>>>(
-      ws, gradient_and_loss, tab);
+  launch_kernel(reduce_grads, dim3(unsigned((tab.params + 1 + kReduceCols - 1) / kReduceCols)),
+                dim3(kReduceCols, kReduceRows), 0, stream, static_cast<const double*>(ws), gradient_and_loss, tab);
   e = cudaGetLastError();
   mark();
   if (recorded) *recorded = marks;
