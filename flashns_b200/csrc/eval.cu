@@ -79,9 +79,9 @@ FLASHNS_JET(3, 3, 20)
 // Tiles of the DMMA kernels.  The GEMM is computed transposed: MMA M = channels,
 // MMA N = packed rows, so a thread's accumulators hold, for two channels per m16 tile,
 // the rows 8j+2t and 8j+2t+1 of every n8 tile j.  Those rows are the S = Q jet
-// coefficients of one point ("thread column"): the forward kernels permute the rows in
-// shared memory (tile_slot), the fused backward and head kernels keep rows in global order
-// and fold the permutation into their fragment addresses.  The tanh-jet epilogue and its
+// coefficients of one point ("thread column"): most kernels permute the rows in shared
+// memory (tile_slot); the fused backward keeps its TMA-loaded rows in global order and folds
+// the permutation into its fragment addresses.  The tanh-jet epilogue and its
 // VJP then run entirely in registers.  One m16 tile of channels per warp keeps 20 (2-D) or
 // 40 (3-D) accumulators per thread; each kernel picks its warp count (FwdTile, BwdTile,
 // FusedTile, HeadTile).
