@@ -38,6 +38,10 @@ SIGNATURES = {
     "flashns_b200_lbfgs_step_point": [_c_ptr] * 4 + [_c_i64, _c_ptr],
     "flashns_b200_adam_step": [_c_ptr] * 4 + [_c_i64, _c_dbl, _c_dbl, _c_dbl, _c_dbl, _c_i64, _c_ptr],
     "flashns_b200_residuals": [_c_int, _c_int, _c_ptr, _c_dbl, _c_ptr, _c_i64, _c_ptr],
+    "flashns_b200_sobol_points": [_c_ptr, _c_ptr, _c_int, _c_i64, _c_i64, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_ptr],
+    "flashns_b200_philox_points": [ctypes.c_uint64, ctypes.c_uint64, _c_int, _c_i64, _c_i64, _c_ptr, _c_ptr, _c_ptr,
+                                   _c_i64, _c_ptr],
+    "flashns_b200_pack_coordinates": [_c_ptr, _c_i64, _c_i64, _c_int, _c_ptr, _c_ptr],
     # reference-ABI hooks (experiments/pinn_v8/native.py:26-51, experiments/cuda_jet_h100/gpu.py)
     "flashns_v8_activation": [_c_int, _c_int] + [_c_ptr] * 5 + [_c_i64, _c_i64, _c_int, _c_ptr],
     "flashns_v8_coordinate_affine": [_c_int] + [_c_ptr] * 4 + [_c_i64, _c_i64, _c_int, _c_ptr],

@@ -49,6 +49,18 @@ class PackedLayout:
         """Input jets of the coordinates (order-0 value, unit first-order coefficients)."""
         if x.shape != (self.points, self.dimension) or x.dtype != torch.float64:
             raise ValueError("FP64 coordinates must match the layout")
+        if x.is_cuda:  # one kernel (flashns_b200_pack_coordinates), same values
+            import ctypes
+
+            from flashns_b200 import _lib
+            x = x.contiguous()
+            result = torch.empty((self.rows, self.dimension), dtype=torch.float64, device=x.device)
+            with torch.cuda.device(x.device):
+                stream = ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
+                _lib.check(_lib.library().flashns_b200_pack_coordinates(
+                    ctypes.c_void_p(x.data_ptr()), self.full_points, self.value_points, self.dimension,
+                    ctypes.c_void_p(result.data_ptr()), stream), "flashns_b200_pack_coordinates")
+            return result
         result = x.new_zeros((self.rows, self.dimension))
         result[self.zero_rows(x.device)] = x
         order = JetSpec(self.dimension).coefficient_order

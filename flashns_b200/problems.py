@@ -64,51 +64,122 @@ def kovasznay_exact(x, re=20.0):
     return u, v, p, psi
 
 
+SAMPLINGS = ("uniform", "sobol", "philox")
+
+
+def sobol_engine(dim, seed, stream=0):
+    """The scrambled Sobol engine of one point family: seeded by `seed` and `stream`, so
+    separate families get independent sequences."""
+    return torch.quasirandom.SobolEngine(dim, scramble=True, seed=seed * 1009 + stream)
+
+
+def philox_key(seed, stream=0):
+    """(key0, key1) of a family's Philox4x64-10 stream."""
+    if not 0 <= seed < 2 ** 64 or not 0 <= stream < 2 ** 64:
+        raise ValueError("philox sampling needs 0 <= seed, stream < 2^64")
+    return seed, stream
+
+
 def unit_samples(n, dim, gen, sampling, seed, stream=0):
-    """n points in [0, 1)^dim: uniform from `gen`, or scrambled Sobol (Owen scrambling seeded
-    by `seed` and `stream`, so separate point families get independent sequences)."""
+    """n points in [0, 1)^dim on the host.
+
+    * ``uniform``: torch's CPU generator `gen` (host only);
+    * ``sobol``: scrambled Sobol from ``sobol_engine(dim, seed, stream)``;
+    * ``philox``: Philox4x64-10 keyed by ``philox_key(seed, stream)``, the stream of
+      ``numpy.random.Generator(numpy.random.Philox(key=key0 + 2^64 key1)).random()``.
+
+    The device kernels draw the Sobol and Philox families bit for bit alike
+    (``sample_points``)."""
+    if sampling not in SAMPLINGS:
+        raise ValueError(f"sampling must be one of {SAMPLINGS}")
+    if n == 0:
+        return torch.zeros(0, dim, dtype=torch.float64)
     if sampling == "uniform":
         return torch.rand(n, dim, generator=gen, dtype=torch.float64)
     if sampling == "sobol":
-        if n == 0:
-            return torch.zeros(0, dim, dtype=torch.float64)
-        engine = torch.quasirandom.SobolEngine(dim, scramble=True, seed=seed * 1009 + stream)
-        return engine.draw(n, dtype=torch.float64)
-    raise ValueError("sampling must be 'uniform' or 'sobol'")
+        return sobol_engine(dim, seed, stream).draw(n, dtype=torch.float64)
+    import numpy as np
+    k0, k1 = philox_key(seed, stream)
+    rng = np.random.Generator(np.random.Philox(key=k0 + (k1 << 64)))
+    return torch.from_numpy(rng.random((n, dim)))
 
 
-def kovasznay(interior, boundary, *, re=20.0, seed=1, boundary_order=1, sampling="uniform"):
+def sample_points(n, dim, gen, sampling, seed, stream=0, *, lo=None, span=None, device=None):
+    """[n, dim] points ``lo + span * u`` (u from ``unit_samples``; the product and the sum
+    rounded separately; lo / span None drop them) on `device`.
+
+    On a CUDA device the Sobol and Philox families are drawn there by
+    ``flashns_b200_sobol_points`` / ``flashns_b200_philox_points``, bit-identical to the
+    host; uniform points come from torch's CPU generator and are copied."""
+    device = torch.device(device or "cpu")
+    lo_t = None if lo is None else torch.tensor(lo, dtype=torch.float64)
+    span_t = None if span is None else torch.tensor(span, dtype=torch.float64)
+    for t in (lo_t, span_t):
+        if t is not None and t.shape != (dim,):
+            raise ValueError("lo and span need one value per coordinate")
+    if device.type == "cuda" and sampling in ("sobol", "philox"):
+        return _device_points(n, dim, sampling, seed, stream, lo_t, span_t, device)
+    u = unit_samples(n, dim, gen, sampling, seed, stream)
+    if span_t is not None:
+        u = span_t * u
+    if lo_t is not None:
+        u = lo_t + u
+    return u.to(device)
+
+
+def _device_points(n, dim, sampling, seed, stream, lo, span, device):
+    import ctypes
+
+    from flashns_b200 import _lib
+    out = torch.empty(n, dim, dtype=torch.float64, device=device)
+    if n == 0:
+        return out
+    dbl = lambda t: None if t is None else (ctypes.c_double * dim)(*t.tolist())
+    lib = _lib.library()
+    with torch.cuda.device(device):
+        s = ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+        if sampling == "sobol":
+            engine = sobol_engine(dim, seed, stream)
+            dirs = engine.sobolstate.contiguous()
+            shift = engine.shift.contiguous()
+            status = lib.flashns_b200_sobol_points(ctypes.c_void_p(dirs.data_ptr()), ctypes.c_void_p(shift.data_ptr()),
+                                                   dim, 0, n, dbl(lo), dbl(span), ctypes.c_void_p(out.data_ptr()), dim,
+                                                   s)
+        else:
+            k0, k1 = philox_key(seed, stream)
+            status = lib.flashns_b200_philox_points(k0, k1, dim, 0, n, dbl(lo), dbl(span),
+                                                    ctypes.c_void_p(out.data_ptr()), dim, s)
+    _lib.check(status, f"flashns_b200_{sampling}_points")
+    return out
+
+
+def kovasznay(interior, boundary, *, re=20.0, seed=1, boundary_order=1, sampling="uniform", device=None):
+    """Kovasznay point set on `device` (default: the host).  With ``sobol`` or ``philox``
+    sampling on a CUDA device the points are drawn there (``sample_points``)."""
     gen = torch.Generator(device="cpu").manual_seed(seed)
-    lo = torch.tensor([-0.5, -0.5], dtype=torch.float64)
-    span = torch.tensor([1.5, 2.0], dtype=torch.float64)
-    xi = lo + span * unit_samples(interior, 2, gen, sampling, seed)
+    device = torch.device(device or "cpu")
+    f64 = dict(dtype=torch.float64, device=device)
+    xi = sample_points(interior, 2, gen, sampling, seed, lo=[-0.5, -0.5], span=[1.5, 2.0], device=device)
     counts = [boundary // 4 + (1 if k < boundary % 4 else 0) for k in range(4)]
     edges = []
     for k, n in enumerate(counts):
-        s = unit_samples(n, 1, gen, sampling, seed, stream=k + 1)[:, 0]
-        if k == 0:
-            e = torch.stack((-0.5 + 1.5 * s, torch.full_like(s, -0.5)), 1)
-        elif k == 1:
-            e = torch.stack((-0.5 + 1.5 * s, torch.full_like(s, 1.5)), 1)
-        elif k == 2:
-            e = torch.stack((torch.full_like(s, -0.5), -0.5 + 2.0 * s), 1)
-        else:
-            e = torch.stack((torch.full_like(s, 1.0), -0.5 + 2.0 * s), 1)
-        edges.append(e)
+        lo, span = (-0.5, 1.5) if k < 2 else (-0.5, 2.0)
+        s = sample_points(n, 1, gen, sampling, seed, stream=k + 1, lo=[lo], span=[span], device=device)
+        fixed = torch.full_like(s, (-0.5, 1.5, -0.5, 1.0)[k])
+        edges.append(torch.cat((s, fixed) if k < 2 else (fixed, s), 1))
     xb = torch.cat(edges)
     u, v, p, psi = kovasznay_exact(xb, re)
-    outflow = torch.zeros(boundary, dtype=torch.bool)
+    outflow = torch.zeros(boundary, dtype=torch.bool, device=device)
     outflow[boundary - counts[3]:] = True
     wv = 1.0 / max(boundary, 1)
-    wp = torch.zeros(boundary, dtype=torch.float64)
-    wp[outflow] = 1.0 / max(counts[3], 1)
+    wp = torch.zeros(boundary, **f64).masked_fill_(outflow, 1.0 / max(counts[3], 1))
     if boundary_order == 1:
         target = torch.stack((u, v, p), 1)
         weights = torch.stack((torch.full_like(u, wv), torch.full_like(u, wv), wp), 1)
     else:
         target = torch.stack((psi, p), 1)
         weights = torch.stack((torch.full_like(u, wv), wp), 1)
-    pde = torch.full((interior,), 1.0 / max(interior, 1), dtype=torch.float64)
+    pde = torch.full((interior,), 1.0 / max(interior, 1), **f64)
     return PointSet(torch.cat((xi, xb)), interior, pde, weights, target, 2, 1.0 / re,
                     f"kovasznay Re={re:g} {interior}+{boundary}")
 
@@ -122,30 +193,29 @@ def taylor_green_exact(x, nu=0.01):
     return u, v, p, psi
 
 
-def taylor_green(interior, boundary, *, nu=0.01, seed=1, boundary_order=1, sampling="uniform"):
+def taylor_green(interior, boundary, *, nu=0.01, seed=1, boundary_order=1, sampling="uniform", device=None):
+    """Taylor-Green point set on `device` (default: the host), drawn there with ``sobol``
+    or ``philox`` sampling on a CUDA device."""
     gen = torch.Generator(device="cpu").manual_seed(seed)
+    device = torch.device(device or "cpu")
     two_pi = 2 * math.pi
-    xi = unit_samples(interior, 3, gen, sampling, seed) * torch.tensor([two_pi, two_pi, 1.0], dtype=torch.float64)
+    xi = sample_points(interior, 3, gen, sampling, seed, span=[two_pi, two_pi, 1.0], device=device)
     n0 = boundary // 2
-    init = unit_samples(n0, 3, gen, sampling, seed, stream=1) * torch.tensor([two_pi, two_pi, 0.0],
-                                                                             dtype=torch.float64)
-    side = unit_samples(boundary - n0, 3, gen, sampling, seed, stream=2) * torch.tensor([two_pi, two_pi, 1.0],
-                                                                                        dtype=torch.float64)
-    face = torch.arange(boundary - n0) % 4
-    side[face == 0, 0] = 0.0
-    side[face == 1, 0] = two_pi
-    side[face == 2, 1] = 0.0
-    side[face == 3, 1] = two_pi
+    init = sample_points(n0, 3, gen, sampling, seed, stream=1, span=[two_pi, two_pi, 0.0], device=device)
+    side = sample_points(boundary - n0, 3, gen, sampling, seed, stream=2, span=[two_pi, two_pi, 1.0], device=device)
+    face = torch.arange(boundary - n0, device=device) % 4
+    for k, (axis, value) in enumerate(((0, 0.0), (0, two_pi), (1, 0.0), (1, two_pi))):
+        side[:, axis] = torch.where(face == k, value, side[:, axis])
     xb = torch.cat((init, side))
     u, v, p, psi = taylor_green_exact(xb, nu)
     w = 1.0 / max(boundary, 1)
     if boundary_order == 1:
         target = torch.stack((u, v, p), 1)
-        weights = torch.full((boundary, 3), w, dtype=torch.float64)
+        weights = torch.full((boundary, 3), w, dtype=torch.float64, device=device)
     else:
         target = torch.stack((psi, p), 1)
-        weights = torch.full((boundary, 2), w, dtype=torch.float64)
-    pde = torch.full((interior,), 1.0 / max(interior, 1), dtype=torch.float64)
+        weights = torch.full((boundary, 2), w, dtype=torch.float64, device=device)
+    pde = torch.full((interior,), 1.0 / max(interior, 1), dtype=torch.float64, device=device)
     return PointSet(torch.cat((xi, xb)), interior, pde, weights, target, 3, nu,
                     f"taylor-green nu={nu:g} {interior}+{boundary}")
 

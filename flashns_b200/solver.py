@@ -29,7 +29,7 @@ from flashns_b200 import _lib
 from flashns_b200.evaluator import FieldEvaluator, PackedEvaluator, flat_parameters, xavier_normal
 from flashns_b200.lbfgs import DeviceLBFGS
 from flashns_b200.ns_seed import NSLoss
-from flashns_b200.problems import kovasznay, kovasznay_exact
+from flashns_b200.problems import SAMPLINGS, kovasznay, kovasznay_exact
 
 
 def acceptance_grid(n=201):
@@ -77,7 +77,7 @@ def solve(*, interior=16384, boundary=4096, widths=(2, 64, 64, 64, 64, 2), re=20
     rank = dist.get_rank() if dist.is_initialized() else 0
     device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
     widths = list(widths)
-    pts = kovasznay(interior, boundary, re=re, seed=seed, boundary_order=1, sampling=sampling)
+    pts = kovasznay(interior, boundary, re=re, seed=seed, boundary_order=1, sampling=sampling, device=device)
     loss = NSLoss(viscosity=1.0 / re, boundary_weight=boundary_weight)
     if world > 1:
         from flashns_b200.distributed import DistributedEvaluator
@@ -183,7 +183,8 @@ def main():
     ap.add_argument("--history", type=int, default=50)
     ap.add_argument("--time-limit", type=float, default=None)
     ap.add_argument("--optimizer", choices=["device", "torch"], default="device")
-    ap.add_argument("--sampling", choices=["uniform", "sobol"], default="uniform")
+    ap.add_argument("--sampling", choices=list(SAMPLINGS), default="uniform",
+                    help="uniform: torch CPU generator; sobol / philox: drawn on the device")
     ap.add_argument("--initial", type=Path, default=None, help="start from a checkpoint's flat parameters")
     ap.add_argument("--output", type=Path, default=None,
                     help="write OUTPUT.pt (final parameters + run description) and OUTPUT.json (result)")

@@ -221,6 +221,29 @@ int flashns_b200_lbfgs_step_point(const double* x0, const double* scal, const do
 int flashns_b200_adam_step(double* x, const double* g, double* m, double* v, int64_t n, double lr, double beta1,
                            double beta2, double eps, int64_t step, cudaStream_t stream);
 
+/* ---- data preparation on the device (flashns_b200/csrc/sampling.cu) ----
+ * Points i = 0 .. n-1 go to out[i * ld + d] (d < dim <= 8) as lo[d] + span[d] * u, the
+ * product and the sum rounded separately; lo == NULL drops the sum, span == NULL the
+ * product.  `directions`, `shift`, `lo` and `span` are HOST arrays, read at the call. */
+
+/* Scrambled Sobol points first .. first+n-1 (first + n <= 2^30), bit-identical to
+ * torch.quasirandom.SobolEngine(dim, scramble=True, seed).draw() after `first` earlier
+ * draws, as the reference solver samples (experiments/pinn_solver/problem.py:68-99).
+ * directions = the engine's sobolstate [dim][30], shift = its shift [dim]. */
+int flashns_b200_sobol_points(const int64_t* directions, const int64_t* shift, int dim, int64_t first, int64_t n,
+                              const double* lo, const double* span, double* out, int64_t ld, cudaStream_t stream);
+
+/* Uniform points from Philox4x64-10 keyed by (key0, key1): coordinate d of point i is
+ * word (first + i) * dim + d of numpy.random.Generator(numpy.random.Philox(key=key0 +
+ * 2^64 key1)).random()'s stream, (word >> 11) * 2^-53. */
+int flashns_b200_philox_points(uint64_t key0, uint64_t key1, int dim, int64_t first, int64_t n, const double* lo,
+                               const double* span, double* out, int64_t ld, cudaStream_t stream);
+
+/* PackedLayout.coordinates (src/flashns/jet_packed.py:43-53) of x [full_points +
+ * value_points][dim]: out [full_points * Q + value_points][dim], Q = C(dim + 3, 3). */
+int flashns_b200_pack_coordinates(const double* x, int64_t full_points, int64_t value_points, int dim, double* out,
+                                  cudaStream_t stream);
+
 /* shared memory the dense dgrad uses per block (0: this implementation stages none) */
 int flashns_stable_dgrad_shared_bytes(void);
 
