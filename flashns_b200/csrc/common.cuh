@@ -67,6 +67,23 @@ __device__ __forceinline__ void bulk_g2s(void* smem, const void* gmem, unsigned 
       : "memory");
 }
 
+// ---- named barriers (ids 1..15) over some of the block's warps: `count` threads, a
+// multiple of 32, every warp taking part whole.  bar.arrive counts without waiting.
+__device__ __forceinline__ void named_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void named_arrive(int id, int count) {
+  asm volatile("bar.arrive %0, %1;\n" ::"r"(id), "r"(count) : "memory");
+}
+// named_sync that also tells whether any of the `count` threads passed `v` = true
+__device__ __forceinline__ bool named_sync_or(int id, int count, bool v) {
+  unsigned r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n bar.red.or.pred p, %2, %3, q;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(r) : "r"(unsigned(v)), "r"(id), "r"(count) : "memory");
+  return r != 0;
+}
+
 // orders this thread's earlier generic-proxy shared-memory accesses before its later
 // async-proxy (TMA) ones
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }

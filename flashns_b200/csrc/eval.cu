@@ -117,6 +117,17 @@ struct Tiles {
   static constexpr int PS = Q / QB;
   __host__ __device__ static int64_t interior(int64_t ni) { return (ni + TC - 1) / TC; }
   __host__ __device__ static int64_t boundary(int64_t nb) { return (nb + int64_t(TC) * PS - 1) / (int64_t(TC) * PS); }
+  // the tile's points: the first packed point index (interior, then boundary) and the count
+  __device__ static void points(const Geometry& g, int64_t nint, int64_t tile, int64_t& p0, int64_t& n) {
+    if (tile < nint) {
+      p0 = tile * TC;
+      n = (g.ni - p0) < TC ? (g.ni - p0) : TC;
+    } else {
+      const int64_t b0 = (tile - nint) * (int64_t(TC) * PS);
+      n = (g.nb - b0) < int64_t(TC) * PS ? (g.nb - b0) : int64_t(TC) * PS;
+      p0 = g.ni + b0;
+    }
+  }
   __device__ static int64_t row(const Geometry& g, int64_t nint, int64_t tile, int tc, int s) {
     if (tile < nint) {
       const int64_t p = tile * TC + tc;
@@ -430,14 +441,7 @@ __global__ void __launch_bounds__(BwdTile<DIM, CP>::THREADS, 1)
     if (valid && tid == 0) {
       // the epilogue reads this tile's a1 rows (a contiguous range): bring them into L2
       int64_t pt0, pts;
-      if (tile < nint) {
-        pt0 = tile * T::TC;
-        pts = (geo.ni - pt0) < T::TC ? (geo.ni - pt0) : T::TC;
-      } else {
-        const int64_t b0 = (tile - nint) * (int64_t(T::TC) * TL::PS);
-        pts = (geo.nb - b0) < int64_t(T::TC) * TL::PS ? (geo.nb - b0) : int64_t(T::TC) * TL::PS;
-        pt0 = geo.ni + b0;
-      }
+      TL::points(geo, nint, tile, pt0, pts);
       prefetch_l2(a1cur + pt0 * CP, uint32_t(pts * CP * sizeof(double)));
     }
     if (valid) {
@@ -733,6 +737,11 @@ __global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
   const double* hcol = sH + (wn >> 2) * TR * LDC + ((8 * wn) & (KC - 1)) + g;
   for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     const bool has_next = tile + gridDim.x < ntiles;
+    if (tid == 0) {  // the epilogue reads this tile's a1 rows (a contiguous range): bring them into L2
+      int64_t pt0, pts;
+      TL::points(geo, nint, tile, pt0, pts);
+      prefetch_l2(a1cur + pt0 * CP, uint32_t(pts * CP * sizeof(double)));
+    }
     double acc[T::MT][T::NT][4];
 #pragma unroll
     for (int i = 0; i < T::MT; ++i)
@@ -914,6 +923,337 @@ __global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
     mbar_inval(&bars[0]);
     mbar_inval(&bars[1]);
   }
+}
+
+// Two-group ("ping-pong") form of the fused backward for 2-D 64-wide layers.  The CTA's
+// 16 warps form two groups of 8; each group works on its own 80-row half tiles with its
+// own seed / H_l planes and barriers, and W_l is shared.  Eight warps keep the FP64 tensor
+// pipe full, so the groups take turns on it: a group runs its dgrad + wgrad only while it
+// holds the turn, and hands the turn over before its jet-VJP epilogue.  The epilogue (and
+// the next tile's copies) of one group then overlaps the other group's MMAs instead of
+// leaving the pipe idle.  The turn is a pair of named barriers (one per group, all 512
+// threads: the waiting group syncs, the other arrives); every group syncs and arrives a
+// fixed number of times, so the counts always match (see the end of the kernel).
+//
+// The CTA's half tiles are blockIdx.x + k * gridDim.x; group 0 takes even k, group 1 odd
+// k, so the groups of a CTA differ by at most one half tile.
+struct PPTile : MmaTile<2, kFusedWidth, 8> {};
+constexpr int kPPGroups = 2;
+constexpr int kPPThreads = kPPGroups * PPTile::THREADS;
+enum { kPPBarGroup = 1, kPPBarTurn = 3 };  // named barriers: 1 + group (256), 3 + group (512)
+
+template <int BO>
+constexpr int pp_boundary_box_rows() {
+  using TL = Tiles<2, BO, PPTile::TC>;
+  return TL::PS * TL::QB == PPTile::S ? PPTile::TR : TL::PS * TL::QB;
+}
+
+constexpr size_t pp_smem_bytes() {
+  using T = PPTile;
+  constexpr size_t planes = size_t(kFusedWidth / KC) * size_t(T::TR) * LDC;  // one tensor's half tile
+  constexpr size_t wres = size_t(kFusedWidth) * (kFusedWidth + 4);           // resident W_l
+  constexpr size_t a = sizeof(double) * (kPPGroups * 2 * planes + wres + 2 * kPPGroups);  // + mbarriers
+  constexpr size_t red = sizeof(double) * (kPPGroups * T::WR * kFusedWidth * 3 + 8 * (kFusedWidth / 16) * 4 * 32);
+  return a > red ? a : red;
+}
+
+template <int BO, bool FIRST>
+__global__ void __launch_bounds__(kPPThreads, 1)
+    bwd_pingpong(const __grid_constant__ CUtensorMap tm_seed_i, const __grid_constant__ CUtensorMap tm_seed_b,
+                 const __grid_constant__ CUtensorMap tm_h_i, const __grid_constant__ CUtensorMap tm_h_b,
+                 const double* __restrict__ dnext, const double* __restrict__ hcur, const double* __restrict__ w,
+                 const double* __restrict__ a1cur, double* __restrict__ dcur, const double* __restrict__ x,
+                 double* __restrict__ partial, double* __restrict__ wpart, Geometry geo) {
+  constexpr int DIM = 2, CP = kFusedWidth;
+  using T = PPTile;
+  using TL = Tiles<DIM, BO, T::TC>;
+  constexpr int S = T::S, TR = T::TR, Q = TL::Q, QB = TL::QB, PS = TL::PS, LDW = CP + 4;
+  constexpr int NK = CP / KC;  // 32-column planes per tile
+  constexpr int MK = KC / 16;  // m16 tiles of output channels per plane
+  constexpr int NM = CP / 16;  // m16 tiles of output channels
+  constexpr int NV = FIRST ? DIM + 1 : 1;
+  constexpr int BB = pp_boundary_box_rows<BO>();
+  constexpr bool SPLIT = BB != TR;  // boundary tiles whose points leave slots empty: cp.async
+  constexpr int GT = T::THREADS;    // threads per group
+  constexpr int PLANES = NK * TR * LDC;
+  static_assert(CP / 8 == T::NWARPS && TR % 16 == 0, "wgrad: warp w of a group owns dW columns 8w..8w+7");
+  static_assert(NK == 2 && KC == 32 && TR <= 256, "TMA boxes: 36 columns, at most 256 rows");
+  static_assert((size_t(TR) * LDC * sizeof(double)) % 128 == 0, "every TMA destination on a 128-byte boundary");
+  extern __shared__ __align__(128) double smem[];
+  if (smem_u32(smem) & 127) {  // TMA destinations need 128-byte alignment: refuse, never fault
+    if (threadIdx.x == 0) atomicExch(&g_device_fault, 2);
+    return;
+  }
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  const int gp = warp / T::NWARPS, lw = warp % T::NWARPS, gtid = tid % GT;
+  const int wc = lw % T::WC, wr = lw / T::WC;
+  double* sB = smem + gp * 2 * PLANES;  // this group's seed planes [NK][TR][LDC]
+  double* sH = sB + PLANES;             // this group's H_l planes  [NK][TR][LDC]
+  double* sW = smem + kPPGroups * 2 * PLANES;                    // W_l [CP][LDW], shared
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sW + CP * LDW);  // [2 group + 0] seed, [2 group + 1] H_l
+  uint64_t* bar_seed = bars + 2 * gp;
+  uint64_t* bar_h = bars + 2 * gp + 1;
+  const int bar_group = kPPBarGroup + gp;
+  const int64_t nint = TL::interior(geo.ni);
+  const int64_t nht = nint + TL::boundary(geo.nb);
+  const int64_t mine = int64_t(blockIdx.x) < nht ? (nht - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int64_t n0 = (mine + 1) / 2, n1 = mine / 2;  // half tiles of group 0 / group 1
+  const int64_t nmy = gp == 0 ? n0 : n1;
+  auto tile_of = [&](int64_t k) { return int64_t(blockIdx.x) + (2 * k + gp) * int64_t(gridDim.x); };
+  double cacc[2][NV];
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+    for (int a = 0; a < NV; ++a) cacc[hh][a] = 0.0;
+  double wacc[NM][4];  // dW rows 16m+{g,g+8}, columns 8*lw+{2t,2t+1}, rows of this group
+#pragma unroll
+  for (int m = 0; m < NM; ++m)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) wacc[m][e] = 0.0;
+
+  // One tensor's half tile into this group's planes; every thread of the group calls it.
+  auto tma_tile = [&](int64_t tile) { return !SPLIT || tile < nint; };
+  auto load_tile = [&](int64_t tile, double* dst, const CUtensorMap* mi, const CUtensorMap* mb, uint64_t* bar,
+                       const double* src) {
+    const bool interior = tile < nint;
+    if (SPLIT && !interior) {
+      const int64_t b0 = (tile - nint) * (int64_t(T::TC) * PS);
+      for (int i = gtid; i < NK * TR * (KC / 2); i += GT) {
+        const int kc = i / (TR * (KC / 2)), rem = i % (TR * (KC / 2));
+        const int r = rem / (KC / 2), q = rem % (KC / 2);
+        const int tc = r / S, sl = r % S;
+        const int64_t b = b0 + int64_t(tc) * PS + sl / QB;
+        const bool ok = sl < PS * QB && b < geo.nb;
+        const int64_t gr = ok ? geo.ni * Q + b * QB + sl % QB : 0;
+        cp_async16(dst + kc * TR * LDC + r * LDC + 2 * q, src + gr * CP + kc * KC + 2 * q, ok);
+      }
+      cp_async_commit();
+      return;
+    }
+    if (gtid != 0) return;
+    fence_proxy_async();  // the planes' last readers finished before the barrier that led here
+    const int y = interior ? int(tile * T::TC * Q) : int((tile - nint) * (int64_t(T::TC) * PS) * QB);
+    mbar_arrive_expect_tx(bar, NK * TR * LDC * sizeof(double));
+#pragma unroll
+    for (int kc = 0; kc < NK; ++kc) tma_load_2d(dst + kc * TR * LDC, interior ? mi : mb, kc * KC, y, bar);
+  };
+  // bounded wait for a half tile that arrived by TMA (phase bit of its barrier) or cp.async
+  auto wait_tile = [&](int64_t tile, uint64_t* bar, unsigned& ph, bool last_group) {
+    bool ok = true;
+    if (tma_tile(tile)) {
+      ok = mbar_wait(bar, ph);
+      ph ^= 1u;
+    } else if (last_group) {
+      cp_async_wait<0>();
+    } else {
+      cp_async_wait<1>();  // the seed group; the H_l group may still be in flight
+    }
+    return ok;
+  };
+  for (int i = tid; i < CP * (CP / 2); i += kPPThreads) {  // W_l, resident
+    const int r = i / (CP / 2), p = i % (CP / 2);
+    cp_async16(sW + r * LDW + 2 * p, w + int64_t(r) * CP + 2 * p, true);
+  }
+  cp_async_commit();
+  if (tid == 0)
+    for (int b = 0; b < 2 * kPPGroups; ++b) mbar_init(&bars[b], 1);
+  cp_async_wait<0>();
+  __syncthreads();  // W_l and the barriers visible
+  pdl_wait();  // D_{l+1} is the predecessor's output
+  pdl_trigger();
+  if (nmy > 0) {
+    load_tile(tile_of(0), sB, &tm_seed_i, &tm_seed_b, bar_seed, dnext);
+    load_tile(tile_of(0), sH, &tm_h_i, &tm_h_b, bar_h, hcur);
+  }
+  unsigned ph_seed = 0, ph_h = 0;
+  bool dead = false;  // a bounded wait ran out: skip the work, keep the turn protocol
+  // B fragments of the dgrad: column g of an n8 tile is slot 2j + (g & 1) of thread
+  // column wr*4 + (g >> 1)
+  const int brow = (wr * 4 + (g >> 1)) * S + (g & 1);
+  // wgrad B fragments: H_l columns 8*lw + g live in plane lw / 4
+  const double* hcol = sH + (lw >> 2) * TR * LDC + ((8 * lw) & (KC - 1)) + g;
+  if (gp == 1) named_arrive(kPPBarTurn + 0, kPPThreads);  // group 0 takes the first turn
+  for (int64_t k = 0; k < nmy; ++k) {
+    const int64_t tile = tile_of(k);
+    const bool has_next = k + 1 < nmy;
+    if (gtid == 0 && !dead) {  // the epilogue reads this tile's a1 rows (a contiguous range): into L2
+      int64_t pt0, pts;
+      TL::points(geo, nint, tile, pt0, pts);
+      prefetch_l2(a1cur + pt0 * CP, uint32_t(pts * CP * sizeof(double)));
+    }
+    double acc[T::NT][4];
+#pragma unroll
+    for (int j = 0; j < T::NT; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[j][e] = 0.0;
+    if (!dead) dead = named_sync_or(bar_group, GT, !wait_tile(tile, bar_seed, ph_seed, false));
+    named_sync(kPPBarTurn + gp, kPPThreads);  // this group's turn on the tensor pipe
+    if (!dead) {
+      // dgrad: dH[ch][rows] += W_l^T[ch][cout plane] D^T[cout plane][rows]
+#pragma unroll
+      for (int kc = 0; kc < NK; ++kc) {
+        const double* cB = sB + kc * TR * LDC + brow * LDC;
+        const double* cA = sW + kc * KC * LDW + wc * T::WCH;
+#pragma unroll
+        for (int kk = 0; kk < KC; kk += 8) {
+          double a[4];
+          a[0] = cA[(kk + t) * LDW + g];
+          a[1] = cA[(kk + t) * LDW + g + 8];
+          a[2] = cA[(kk + t + 4) * LDW + g];
+          a[3] = cA[(kk + t + 4) * LDW + g + 8];
+#pragma unroll
+          for (int j = 0; j < T::NT; ++j) mma_m16n8k8(acc[j], a, cB[2 * j * LDC + kk + t], cB[2 * j * LDC + kk + t + 4]);
+        }
+      }
+      dead = named_sync_or(bar_group, GT, !wait_tile(tile, bar_h, ph_h, true));  // H_l landed
+    }
+    if (!dead) {
+      // wgrad: dW[cout][8*lw..+8] += D^T[cout][rows] H[rows][cin] over the half tile's rows
+      // (each row step feeds all NM accumulators from one B fragment: NM MMAs in flight)
+#pragma unroll 2
+      for (int r = 0; r < TR; r += 8) {
+        const double b0 = hcol[(r + t) * LDC];
+        const double b1 = hcol[(r + t + 4) * LDC];
+#pragma unroll
+        for (int m = 0; m < NM; ++m) {  // output channels 16m..: plane m / MK
+          const double* cD = sB + (m / MK) * TR * LDC + 16 * (m % MK);
+          double a[4];
+          a[0] = cD[(r + t) * LDC + g];
+          a[1] = cD[(r + t) * LDC + g + 8];
+          a[2] = cD[(r + t + 4) * LDC + g];
+          a[3] = cD[(r + t + 4) * LDC + g + 8];
+          mma_m16n8k8(wacc[m], a, b0, b1);
+        }
+      }
+    }
+    named_arrive(kPPBarTurn + (1 - gp), kPPThreads);  // the other group's turn
+    named_sync(bar_group, GT);                         // this group's seed planes free
+    if (has_next && !dead) load_tile(tile_of(k + 1), sB, &tm_seed_i, &tm_seed_b, bar_seed, dnext);
+    if (!dead) {
+      // epilogue: jet VJP of this half tile; H_l from the shared planes (slot s of thread
+      // column wr*4+t is row (wr*4+t)*S + s)
+      const int tc = wr * 4 + t;
+      const double* hrow = sH + (tc * S) * LDC;
+      auto hslot = [&](int s, int ch) { return hrow[(ch >> 5) * TR * LDC + s * LDC + (ch & (KC - 1))]; };
+      const bool interior = tile < nint;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int ch = wc * T::WCH + 8 * hh + g;
+        double dh[S];
+#pragma unroll
+        for (int s = 0; s < S; ++s) dh[s] = acc[s >> 1][2 * hh + (s & 1)];
+        if (interior) {
+          const int64_t p = tile * T::TC + tc;
+          if (p < geo.ni) {
+            double hv[Q], zb[Q];
+#pragma unroll
+            for (int s = 0; s < Q; ++s) hv[s] = hslot(s, ch);
+            Jet<DIM, 3>::vjp(hv, a1cur[p * CP + ch], dh, zb);
+            if constexpr (FIRST) {
+              cacc[hh][DIM] += zb[0];
+#pragma unroll
+              for (int a = 0; a < DIM; ++a) cacc[hh][a] += zb[0] * x[p * DIM + a] + zb[unit_row<DIM>(a)];
+            } else {
+              double* dst = dcur + p * Q * CP + ch;
+#pragma unroll
+              for (int s = 0; s < Q; ++s) dst[int64_t(s) * CP] = zb[s];
+              cacc[hh][0] += zb[0];
+            }
+          }
+        } else {
+#pragma unroll
+          for (int kq = 0; kq < PS; ++kq) {
+            const int64_t b = (tile - nint) * (int64_t(T::TC) * PS) + int64_t(tc) * PS + kq;
+            if (b < geo.nb) {
+              double hv[QB], zb[QB];
+#pragma unroll
+              for (int c = 0; c < QB; ++c) hv[c] = hslot(kq * QB + c, ch);
+              Jet<DIM, BO ? 1 : 0>::vjp(hv, a1cur[(geo.ni + b) * CP + ch], dh + kq * QB, zb);
+              if constexpr (FIRST) {
+                cacc[hh][DIM] += zb[0];
+#pragma unroll
+                for (int a = 0; a < DIM; ++a) {
+                  double v = zb[0] * x[(geo.ni + b) * DIM + a];
+                  if constexpr (BO) v += zb[unit_row<DIM>(a)];
+                  cacc[hh][a] += v;
+                }
+              } else {
+                double* dst = dcur + (geo.ni * Q + b * QB) * CP + ch;
+#pragma unroll
+                for (int c = 0; c < QB; ++c) dst[int64_t(c) * CP] = zb[c];
+                cacc[hh][0] += zb[0];
+              }
+            }
+          }
+        }
+      }
+    }
+    named_sync(bar_group, GT);  // this group's H_l planes free
+    if (has_next && !dead) load_tile(tile_of(k + 1), sH, &tm_h_i, &tm_h_b, bar_h, hcur);
+  }
+  // Turn counts.  Barrier "turn 0" gets n0 syncs from group 0 and 1 + n1 arrivals from
+  // group 1; "turn 1" gets n1 syncs from group 1 and n0 arrivals from group 0.  With
+  // n0 = n1 + 1 turn 0 is balanced and group 1 owes turn 1 one sync; with n0 = n1 group 0
+  // owes turn 0 one sync and turn 1 is balanced.
+  if (gp == 0 && n0 == n1) named_sync(kPPBarTurn + 0, kPPThreads);
+  if (gp == 1 && n0 == n1 + 1) named_sync(kPPBarTurn + 1, kPPThreads);
+  // every tile done: the planes become the reduction scratch.  A group whose wait ran out
+  // set `dead`; the whole CTA then leaves together with the fault word set.
+  if (__syncthreads_or(dead)) {
+    if (tid == 0) atomicExch(&g_device_fault, 1);
+    return;
+  }
+  // weight-gradient partial of this CTA: the two groups' row shares combined in fixed order
+  double* wsh = smem + kPPGroups * T::WR * CP * NV;  // [8 warps][NM][4][32 lanes]
+  if (gp == 1) {
+#pragma unroll
+    for (int m = 0; m < NM; ++m)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) wsh[((lw * NM + m) * 4 + e) * 32 + lane] = wacc[m][e];
+  }
+  __syncthreads();
+  if (gp == 0) {
+    double* wp = wpart + int64_t(blockIdx.x) * CP * CP;
+#pragma unroll
+    for (int m = 0; m < NM; ++m) {
+      double v[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[e] = wacc[m][e] + wsh[((lw * NM + m) * 4 + e) * 32 + lane];
+      const int o = 16 * m + g, c = 8 * lw + 2 * t;
+      wp[o * CP + c] = v[0];
+      wp[o * CP + c + 1] = v[1];
+      wp[(o + 8) * CP + c] = v[2];
+      wp[(o + 8) * CP + c + 1] = v[3];
+    }
+  }
+  // bias / coordinate partials: quad shuffles, then the 4 row groups in fixed order
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+    for (int a = 0; a < NV; ++a) {
+      double v = cacc[hh][a];
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      v += __shfl_xor_sync(0xffffffffu, v, 2);
+      cacc[hh][a] = v;
+    }
+  double* red = smem;  // [groups * WR][CP][NV]
+  const int rg = gp * T::WR + wr;
+  if (t == 0) {
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int ch = wc * T::WCH + 8 * hh + g;
+#pragma unroll
+      for (int a = 0; a < NV; ++a) red[(rg * CP + ch) * NV + a] = cacc[hh][a];
+    }
+  }
+  __syncthreads();
+  for (int idx = tid; idx < CP * NV; idx += kPPThreads) {
+    double s = 0.0;
+    for (int r = 0; r < kPPGroups * T::WR; ++r) s += red[r * CP * NV + idx];
+    partial[int64_t(blockIdx.x) * CP * NV + idx] = s;
+  }
+  if (tid == 0)  // every phase completed before the barriers above
+    for (int b = 0; b < 2 * kPPGroups; ++b) mbar_inval(&bars[b]);
 }
 
 // ----------------------------------------------------------------------------------
@@ -1880,19 +2220,49 @@ struct BwdOps {
 
 template <int DIM, int BO, bool FIRST>
 struct FusedOps {
+  // 2-D: the two-group kernel over 80-row half tiles (a CTA takes about two at a time);
+  // 3-D: one 8-warp group over 160-row tiles
+  static constexpr bool kPingPong = DIM == 2;
   static cudaError_t setup(int& occ) {
-    constexpr size_t smem = fused_smem_bytes<DIM>();
-    cudaError_t e = allow_smem(bwd_fused<DIM, BO, FIRST>, smem);
-    occ = occupancy(bwd_fused<DIM, BO, FIRST>, smem, FusedTile<DIM>::THREADS);
-    return e;
+    if constexpr (kPingPong) {
+      constexpr size_t smem = pp_smem_bytes();
+      static_assert(smem <= kMaxSmem, "two-group backward tile exceeds shared memory");
+      cudaError_t e = allow_smem(bwd_pingpong<BO, FIRST>, smem);
+      occ = occupancy(bwd_pingpong<BO, FIRST>, smem, kPPThreads);
+      return e;
+    } else {
+      constexpr size_t smem = fused_smem_bytes<DIM>();
+      cudaError_t e = allow_smem(bwd_fused<DIM, BO, FIRST>, smem);
+      occ = occupancy(bwd_fused<DIM, BO, FIRST>, smem, FusedTile<DIM>::THREADS);
+      return e;
+    }
   }
   static int64_t tiles(const Geometry& g) {
-    using T = FusedTile<DIM>;
-    using TL = Tiles<DIM, BO, T::TC>;
-    return TL::interior(g.ni) + TL::boundary(g.nb);
+    if constexpr (kPingPong) {
+      using TL = Tiles<2, BO, PPTile::TC>;
+      return (TL::interior(g.ni) + TL::boundary(g.nb) + 1) / 2;
+    } else {
+      using TL = Tiles<DIM, BO, FusedTile<DIM>::TC>;
+      return TL::interior(g.ni) + TL::boundary(g.nb);
+    }
   }
   static cudaError_t launch(int grid, cudaStream_t st, const double* dn, const double* w, const double* h,
                             const double* a1, double* dc, const double* x, double* part, double* wp, Geometry g) {
+    if constexpr (kPingPong) {
+      using TL = Tiles<2, BO, PPTile::TC>;
+      constexpr int TR = PPTile::TR, BB = pp_boundary_box_rows<BO>();
+      const int64_t ri = g.ni * TL::Q, rb = g.nb * TL::QB;  // interior / boundary segment rows
+      if (ri > INT32_MAX - TR || rb > INT32_MAX - TR) return cudaErrorInvalidValue;  // TMA rows are int32
+      CUtensorMap m[4];
+      cudaError_t e;
+      if ((e = row_tensor_map(&m[0], dn, ri, kFusedWidth, LDC, TR)) != cudaSuccess ||
+          (e = row_tensor_map(&m[1], dn + ri * kFusedWidth, rb, kFusedWidth, LDC, BB)) != cudaSuccess ||
+          (e = row_tensor_map(&m[2], h, ri, kFusedWidth, LDC, TR)) != cudaSuccess ||
+          (e = row_tensor_map(&m[3], h + ri * kFusedWidth, rb, kFusedWidth, LDC, BB)) != cudaSuccess)
+        return e;
+      return launch_kernel(bwd_pingpong<BO, FIRST>, grid, kPPThreads, pp_smem_bytes(), st, m[0], m[1], m[2], m[3], dn,
+                           h, w, a1, dc, x, part, wp, g);
+    }
     using T = FusedTile<DIM>;
     using TL = Tiles<DIM, BO, T::TC>;
     constexpr int BB = fused_boundary_box_rows<DIM, BO>();
