@@ -1256,6 +1256,187 @@ __global__ void __launch_bounds__(kPPThreads, 1)
     for (int b = 0; b < 2 * kPPGroups; ++b) mbar_inval(&bars[b]);
 }
 
+// Two-group ("ping-pong") form of the 2-D 64 -> 64 forward layer, on the pattern of
+// bwd_pingpong: two 8-warp groups share the resident W_l and take turns on the tensor pipe;
+// a group's mainloop runs only while it holds the turn, and its jet epilogue (stable tanh,
+// stores of H_{l+1} and a1) overlaps the other group's mainloop.  A group's half tile (80
+// rows, 8 thread columns) arrives by 2-D TMA boxes in global row order (split boundary
+// tiles by cp.async), the permutation folded into the fragment addresses.
+constexpr size_t fpp_smem_bytes() {
+  constexpr size_t planes = size_t(kFusedWidth / KC) * size_t(PPTile::TR) * LDC;  // one half tile
+  constexpr size_t wres = size_t(kFusedWidth) * (kFusedWidth + 4);
+  return sizeof(double) * (kPPGroups * planes + wres + kPPGroups);  // + one mbarrier per group
+}
+
+template <int BO>
+__global__ void __launch_bounds__(kPPThreads, 1)
+    fwd_pingpong(const __grid_constant__ CUtensorMap tm_in_i, const __grid_constant__ CUtensorMap tm_in_b,
+                 const double* __restrict__ hin, const double* __restrict__ w, const double* __restrict__ bias,
+                 double* __restrict__ hout, double* __restrict__ a1out, Geometry geo) {
+  constexpr int DIM = 2, CP = kFusedWidth;
+  using T = PPTile;
+  using TL = Tiles<DIM, BO, T::TC>;
+  constexpr int S = T::S, TR = T::TR, Q = TL::Q, QB = TL::QB, PS = TL::PS, LDW = CP + 4;
+  constexpr int NK = CP / KC;
+  constexpr int BB = pp_boundary_box_rows<BO>();
+  constexpr bool SPLIT = BB != TR;
+  constexpr int GT = T::THREADS;
+  constexpr int PLANES = NK * TR * LDC;
+  static_assert(NK == 2 && KC == 32 && TR <= 256, "TMA boxes: 36 columns, at most 256 rows");
+  static_assert((size_t(TR) * LDC * sizeof(double)) % 128 == 0, "every TMA destination on a 128-byte boundary");
+  extern __shared__ __align__(128) double smem[];
+  if (smem_u32(smem) & 127) {  // TMA destinations need 128-byte alignment: refuse, never fault
+    if (threadIdx.x == 0) atomicExch(&g_device_fault, 2);
+    return;
+  }
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  const int gp = warp / T::NWARPS, lw = warp % T::NWARPS, gtid = tid % GT;
+  const int wc = lw % T::WC, wr = lw / T::WC;
+  double* sB = smem + gp * PLANES;                               // this group's input planes
+  double* sW = smem + kPPGroups * PLANES;                        // W_l [CP][LDW] (row = output channel)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sW + CP * LDW);  // one per group
+  uint64_t* bar_in = bars + gp;
+  const int bar_group = kPPBarGroup + gp;
+  const int64_t nint = TL::interior(geo.ni);
+  const int64_t nht = nint + TL::boundary(geo.nb);
+  const int64_t mine = int64_t(blockIdx.x) < nht ? (nht - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int64_t n0 = (mine + 1) / 2, n1 = mine / 2;
+  const int64_t nmy = gp == 0 ? n0 : n1;
+  auto tile_of = [&](int64_t k) { return int64_t(blockIdx.x) + (2 * k + gp) * int64_t(gridDim.x); };
+  auto load_tile = [&](int64_t tile) {
+    const bool interior = tile < nint;
+    if (SPLIT && !interior) {
+      const int64_t b0 = (tile - nint) * (int64_t(T::TC) * PS);
+      for (int i = gtid; i < NK * TR * (KC / 2); i += GT) {
+        const int kc = i / (TR * (KC / 2)), rem = i % (TR * (KC / 2));
+        const int r = rem / (KC / 2), q = rem % (KC / 2);
+        const int tc = r / S, sl = r % S;
+        const int64_t b = b0 + int64_t(tc) * PS + sl / QB;
+        const bool ok = sl < PS * QB && b < geo.nb;
+        const int64_t gr = ok ? geo.ni * Q + b * QB + sl % QB : 0;
+        cp_async16(sB + kc * TR * LDC + r * LDC + 2 * q, hin + gr * CP + kc * KC + 2 * q, ok);
+      }
+      cp_async_commit();
+      return;
+    }
+    if (gtid != 0) return;
+    fence_proxy_async();  // the planes' last readers finished before the barrier that led here
+    const int y = interior ? int(tile * T::TC * Q) : int((tile - nint) * (int64_t(T::TC) * PS) * QB);
+    mbar_arrive_expect_tx(bar_in, NK * TR * LDC * sizeof(double));
+#pragma unroll
+    for (int kc = 0; kc < NK; ++kc) tma_load_2d(sB + kc * TR * LDC, interior ? &tm_in_i : &tm_in_b, kc * KC, y, bar_in);
+  };
+  unsigned ph = 0;
+  auto wait_tile = [&](int64_t tile) {
+    if (SPLIT && tile >= nint) {
+      cp_async_wait<0>();
+      return true;
+    }
+    const bool ok = mbar_wait(bar_in, ph);
+    ph ^= 1u;
+    return ok;
+  };
+  double bias_r[2];  // a thread's channels are fixed for the whole kernel
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) bias_r[hh] = bias[wc * T::WCH + 8 * hh + g];
+  for (int i = tid; i < CP * (CP / 2); i += kPPThreads) {  // W_l, resident
+    const int r = i / (CP / 2), p = i % (CP / 2);
+    cp_async16(sW + r * LDW + 2 * p, w + int64_t(r) * CP + 2 * p, true);
+  }
+  cp_async_commit();
+  if (tid == 0)
+    for (int b = 0; b < kPPGroups; ++b) mbar_init(&bars[b], 1);
+  cp_async_wait<0>();
+  __syncthreads();  // W_l and the barriers visible
+  pdl_wait();  // H_l is the predecessor's output
+  pdl_trigger();
+  if (nmy > 0) load_tile(tile_of(0));
+  bool dead = false;
+  // B fragments: column g of an n8 tile is slot 2j + (g & 1) of thread column wr*4 + (g >> 1)
+  const int brow = (wr * 4 + (g >> 1)) * S + (g & 1);
+  if (gp == 1) named_arrive(kPPBarTurn + 0, kPPThreads);  // group 0 takes the first turn
+  for (int64_t k = 0; k < nmy; ++k) {
+    const int64_t tile = tile_of(k);
+    double acc[T::NT][4];
+#pragma unroll
+    for (int j = 0; j < T::NT; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[j][e] = 0.0;
+    if (!dead) dead = named_sync_or(bar_group, GT, !wait_tile(tile));
+    named_sync(kPPBarTurn + gp, kPPThreads);  // this group's turn on the tensor pipe
+    if (!dead) {
+      // Z^T[ch][rows] = W_l[ch][cin] H_l^T[cin][rows]
+#pragma unroll
+      for (int kc = 0; kc < NK; ++kc) {
+        const double* cB = sB + kc * TR * LDC + brow * LDC;
+        const double* cA = sW + wc * T::WCH * LDW + kc * KC;
+#pragma unroll
+        for (int kk = 0; kk < KC; kk += 8) {
+          double a[4];
+          a[0] = cA[g * LDW + kk + t];
+          a[1] = cA[(g + 8) * LDW + kk + t];
+          a[2] = cA[g * LDW + kk + t + 4];
+          a[3] = cA[(g + 8) * LDW + kk + t + 4];
+#pragma unroll
+          for (int j = 0; j < T::NT; ++j) mma_m16n8k8(acc[j], a, cB[2 * j * LDC + kk + t], cB[2 * j * LDC + kk + t + 4]);
+        }
+      }
+    }
+    named_arrive(kPPBarTurn + (1 - gp), kPPThreads);  // the other group's turn
+    named_sync(bar_group, GT);                         // this group's input planes free
+    if (k + 1 < nmy && !dead) load_tile(tile_of(k + 1));
+    if (!dead) {
+      // epilogue: bias on the order-0 coefficient, stable tanh jet, store H_{l+1} and a1
+      const int tc = wr * 4 + t;
+      const bool interior = tile < nint;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int ch = wc * T::WCH + 8 * hh + g;
+        double z[S];
+#pragma unroll
+        for (int s = 0; s < S; ++s) z[s] = acc[s >> 1][2 * hh + (s & 1)];
+        if (interior) {
+          const int64_t p = tile * T::TC + tc;
+          if (p < geo.ni) {
+            double hv[Q], a1;
+            z[0] += bias_r[hh];
+            Jet<DIM, 3>::fwd(z, hv, a1);
+            double* dst = hout + p * Q * CP + ch;
+#pragma unroll
+            for (int s = 0; s < Q; ++s) dst[int64_t(s) * CP] = hv[s];
+            a1out[p * CP + ch] = a1;
+          }
+        } else {
+#pragma unroll
+          for (int kq = 0; kq < PS; ++kq) {
+            const int64_t b = (tile - nint) * (int64_t(T::TC) * PS) + int64_t(tc) * PS + kq;
+            if (b < geo.nb) {
+              double zz[QB], hv[QB], a1;
+#pragma unroll
+              for (int c = 0; c < QB; ++c) zz[c] = z[kq * QB + c];
+              zz[0] += bias_r[hh];
+              Jet<DIM, BO ? 1 : 0>::fwd(zz, hv, a1);
+              double* dst = hout + (geo.ni * Q + b * QB) * CP + ch;
+#pragma unroll
+              for (int c = 0; c < QB; ++c) dst[int64_t(c) * CP] = hv[c];
+              a1out[(geo.ni + b) * CP + ch] = a1;
+            }
+          }
+        }
+      }
+    }
+  }
+  // turn counts balanced as in bwd_pingpong
+  if (gp == 0 && n0 == n1) named_sync(kPPBarTurn + 0, kPPThreads);
+  if (gp == 1 && n0 == n1 + 1) named_sync(kPPBarTurn + 1, kPPThreads);
+  if (__syncthreads_or(dead)) {
+    if (tid == 0) atomicExch(&g_device_fault, 1);
+    return;
+  }
+  if (tid == 0)
+    for (int b = 0; b < kPPGroups; ++b) mbar_inval(&bars[b]);
+}
+
 // ----------------------------------------------------------------------------------
 // wgrad: partial[split][o][i] = sum_{rows in split} D[row][o] H[row][i]
 template <int BM, int BN>
@@ -2180,20 +2361,50 @@ template <int DIM, int CP, int BO>
 struct FwdOps {
   using T = FwdTile<DIM, CP>;
   static_assert(fwd_smem_bytes<DIM, CP>(kMaxWidth) <= kMaxSmem, "resident W_l must fit for every input width");
+  // square 64-wide 2-D layers run the two-group kernel over 80-row half tiles
+  static constexpr bool kPingPongShape = DIM == 2 && CP == kFusedWidth;
+  static bool pingpong(int kin) { return kPingPongShape && kin == kFusedWidth; }
   static cudaError_t setup(int& occ, int kin) {
+    if constexpr (kPingPongShape) {
+      if (kin == kFusedWidth) {
+        static_assert(fpp_smem_bytes() <= kMaxSmem, "two-group forward tile exceeds shared memory");
+        cudaError_t e = allow_smem(fwd_pingpong<BO>, fpp_smem_bytes());
+        occ = occupancy(fwd_pingpong<BO>, fpp_smem_bytes(), kPPThreads);
+        return e;
+      }
+    }
     // the attribute is per kernel and shared by all plans: allow the largest input width
     cudaError_t e = allow_smem(fwd_layer<DIM, CP, BO>, fwd_smem_bytes<DIM, CP>(kMaxWidth));
     occ = occupancy(fwd_layer<DIM, CP, BO>, fwd_smem_bytes<DIM, CP>(kin), T::THREADS);
     return e;
   }
-  static int64_t tiles(const Geometry& g) {
+  static int64_t tiles(const Geometry& g, int kin) {
+    if (pingpong(kin)) {
+      using TL = Tiles<2, BO, PPTile::TC>;
+      return (TL::interior(g.ni) + TL::boundary(g.nb) + 1) / 2;
+    }
     using TL = Tiles<DIM, BO, T::TC>;
     return TL::interior(g.ni) + TL::boundary(g.nb);
   }
-  static void launch(int grid, cudaStream_t st, const double* hin, int kin, const double* w, const double* b,
-                     double* hout, double* a1, Geometry g) {
-    launch_kernel(fwd_layer<DIM, CP, BO>, grid, T::THREADS, fwd_smem_bytes<DIM, CP>(kin), st, hin, kin, w, b, hout, a1,
-                  g);
+  static cudaError_t launch(int grid, cudaStream_t st, const double* hin, int kin, const double* w, const double* b,
+                            double* hout, double* a1, Geometry g) {
+    if constexpr (kPingPongShape) {
+      if (kin == kFusedWidth) {
+        using TL = Tiles<2, BO, PPTile::TC>;
+        constexpr int TR = PPTile::TR, BB = pp_boundary_box_rows<BO>();
+        const int64_t ri = g.ni * TL::Q, rb = g.nb * TL::QB;  // interior / boundary segment rows
+        if (ri > INT32_MAX - TR || rb > INT32_MAX - TR) return cudaErrorInvalidValue;  // TMA rows are int32
+        CUtensorMap m[2];
+        cudaError_t e;
+        if ((e = row_tensor_map(&m[0], hin, ri, kFusedWidth, LDC, TR)) != cudaSuccess ||
+            (e = row_tensor_map(&m[1], hin + ri * kFusedWidth, rb, kFusedWidth, LDC, BB)) != cudaSuccess)
+          return e;
+        return launch_kernel(fwd_pingpong<BO>, grid, kPPThreads, fpp_smem_bytes(), st, m[0], m[1], hin, w, b, hout,
+                             a1, g);
+      }
+    }
+    return launch_kernel(fwd_layer<DIM, CP, BO>, grid, T::THREADS, fwd_smem_bytes<DIM, CP>(kin), st, hin, kin, w, b,
+                         hout, a1, g);
   }
 };
 
@@ -2465,7 +2676,7 @@ int flashns_b200_plan_create(int dim, int head, int boundary_order, int n_affine
       int occ = 1;
       cudaError_t e = ops.setup(occ, p->padded[l]);
       if (e != cudaSuccess) err = e;
-      const int64_t t = ops.tiles(p->geo);
+      const int64_t t = ops.tiles(p->geo, p->padded[l]);
       p->grid_fwd[l] = int(std::max<int64_t>(1, std::min<int64_t>(t, int64_t(occ) * p->sms)));
     });
   }
@@ -2695,10 +2906,12 @@ static int run_eval(const flashns_b200_plan* p, const double* coordinates, const
     for (int l = 1; l < nh - (p->fused_head ? 1 : 0); ++l) {
       const LayerDesc& L = tab.l[l];
       mark();
+      cudaError_t le = cudaSuccess;
       with_fwd<FwdOps>(p->dim, p->padded[l + 1], p->bo, [&](auto ops) {
-        ops.launch(p->grid_fwd[l], stream, ws + p->off_h[l], p->padded[l], Wp(L), Bp(L),
-                   ws + p->off_h[l + 1], ws + p->off_a1[l + 1], g);
+        le = ops.launch(p->grid_fwd[l], stream, ws + p->off_h[l], p->padded[l], Wp(L), Bp(L),
+                        ws + p->off_h[l + 1], ws + p->off_a1[l + 1], g);
       });
+      if (le != cudaSuccess) return int(le);
       if ((e = cudaGetLastError()) != cudaSuccess) return int(e);
     }
     if (p->fused_head) {
@@ -2919,10 +3132,12 @@ extern "C" int flashns_b200_fields(const flashns_b200_plan* p, const double* coo
   if (r) return r;
   for (int l = 1; l < nh; ++l) {
     const LayerDesc& L = tab.l[l];
+    cudaError_t le = cudaSuccess;
     with_fwd<FwdOps>(p->dim, p->padded[l + 1], p->bo, [&](auto ops) {
-      ops.launch(p->grid_fwd[l], stream, ws + p->off_h[l], p->padded[l], ws + L.w_buf, ws + L.b_buf,
-                 ws + p->off_h[l + 1], ws + p->off_a1[l + 1], g);
+      le = ops.launch(p->grid_fwd[l], stream, ws + p->off_h[l], p->padded[l], ws + L.w_buf, ws + L.b_buf,
+                      ws + p->off_h[l + 1], ws + p->off_a1[l + 1], g);
     });
+    if (le != cudaSuccess) return int(le);
     if ((e = cudaGetLastError()) != cudaSuccess) return int(e);
   }
   const LayerDesc& LL = tab.l[nh];
