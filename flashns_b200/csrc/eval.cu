@@ -2104,6 +2104,370 @@ __global__ void __launch_bounds__(HeadTile<DIM>::THREADS, HeadTile<DIM>::MINB)
   }
 }
 
+// Two-group ("ping-pong") form of fwd_head for 2-D: the last hidden layer, the output
+// layer, the residual seeds, the output-layer gradients and the VJP into layer L, with the
+// CTA's 16 warps in two 8-warp groups that take turns on the tensor pipe as in
+// bwd_pingpong.  Each group has its own input planes (TMA, rows in global order), H_L
+// tile, Y and dY; W_{L-1} and W_L are shared.  A group's mainloop runs while it holds the
+// turn; its whole epilogue (jet, output contraction, seeds, output gradients, VJP and the
+// stores of D_L) overlaps the other group's mainloop.
+template <int NF>
+constexpr size_t hpp_group_doubles() {
+  return size_t(kFusedWidth / KC) * PPTile::TR * LDC + size_t(PPTile::TR) * (kFusedWidth + 4) +
+         2 * size_t(PPTile::TR) * NF;
+}
+template <int NF>
+constexpr size_t hpp_smem_bytes() {
+  return sizeof(double) * (kPPGroups * hpp_group_doubles<NF>() + size_t(kFusedWidth) * (kFusedWidth + 4) +
+                           size_t(NF) * kFusedWidth + kPPGroups);
+}
+
+template <int BO, int HEAD>
+__global__ void __launch_bounds__(kPPThreads, 1)
+    head_pingpong(const __grid_constant__ CUtensorMap tm_in_i, const __grid_constant__ CUtensorMap tm_in_b,
+                  const double* __restrict__ hin, const double* __restrict__ w, const double* __restrict__ bias,
+                  const double* __restrict__ wL, const double* __restrict__ bL, const double* __restrict__ pde_w,
+                  const double* __restrict__ bnd_w, const double* __restrict__ target, double nu, double gamma,
+                  double bc, double* __restrict__ dL, double* __restrict__ head_partial, Geometry geo) {
+  constexpr int DIM = 2, CP = kFusedWidth;
+  using T = PPTile;
+  using TL = Tiles<DIM, BO, T::TC>;
+  constexpr int S = T::S, TR = T::TR, Q = TL::Q, QB = TL::QB, PS = TL::PS;
+  constexpr int NF = HeadTraits<HEAD>::NF;
+  constexpr int NFT = (HEAD == FLASHNS_B200_HEAD_PSI && BO) ? 3 : NF;  // boundary target fields
+  constexpr int LDA = CP + 4, LDH = CP + 4;
+  constexpr int PARTIAL = NF * CP + NF + 1 + CP;  // dW_L | db_L | loss | db_{L-1}
+  constexpr int NK = CP / KC;
+  constexpr int BB = pp_boundary_box_rows<BO>();
+  constexpr bool SPLIT = BB != TR;
+  constexpr int GT = T::THREADS;
+  constexpr int PLANES = NK * TR * LDC;
+  static_assert(T::NWARPS == CP / 8 && NF <= 8, "warp w of a group owns output-gradient columns 8w..8w+7");
+  static_assert(NK == 2 && KC == 32 && TR <= 256, "TMA boxes: 36 columns, at most 256 rows");
+  static_assert((hpp_group_doubles<NF>() * sizeof(double)) % 128 == 0, "group buffers on 128-byte boundaries");
+  extern __shared__ __align__(128) double smem[];
+  if (smem_u32(smem) & 127) {  // TMA destinations need 128-byte alignment: refuse, never fault
+    if (threadIdx.x == 0) atomicExch(&g_device_fault, 2);
+    return;
+  }
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  const int gp = warp / T::NWARPS, lw = warp % T::NWARPS, gtid = tid % GT;
+  const int wc = lw % T::WC, wr = lw / T::WC;
+  double* sB = smem + gp * hpp_group_doubles<NF>();  // this group's input planes [NK][TR][LDC]
+  double* sH = sB + PLANES;                          // H_L tile [TR][CP+4], rows in tile order
+  double* sY = sH + TR * LDH;                        // Y  [TR][NF]
+  double* sD = sY + TR * NF;                         // dY [TR][NF]
+  double* sA = smem + kPPGroups * hpp_group_doubles<NF>();  // W_{L-1} [CP][CP+4], shared
+  double* sW = sA + CP * LDA;                                // W_L [NF][CP], shared
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sW + NF * CP);
+  uint64_t* bar_in = bars + gp;
+  const int bar_group = kPPBarGroup + gp;
+  const int64_t nint = TL::interior(geo.ni);
+  const int64_t nht = nint + TL::boundary(geo.nb);
+  const int64_t mine = int64_t(blockIdx.x) < nht ? (nht - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int64_t n0 = (mine + 1) / 2, n1 = mine / 2;
+  const int64_t nmy = gp == 0 ? n0 : n1;
+  auto tile_of = [&](int64_t k) { return int64_t(blockIdx.x) + (2 * k + gp) * int64_t(gridDim.x); };
+  auto load_tile = [&](int64_t tile) {
+    const bool interior = tile < nint;
+    if (SPLIT && !interior) {
+      const int64_t b0 = (tile - nint) * (int64_t(T::TC) * PS);
+      for (int i = gtid; i < NK * TR * (KC / 2); i += GT) {
+        const int kc = i / (TR * (KC / 2)), rem = i % (TR * (KC / 2));
+        const int r = rem / (KC / 2), q = rem % (KC / 2);
+        const int tc = r / S, sl = r % S;
+        const int64_t b = b0 + int64_t(tc) * PS + sl / QB;
+        const bool ok = sl < PS * QB && b < geo.nb;
+        const int64_t gr = ok ? geo.ni * Q + b * QB + sl % QB : 0;
+        cp_async16(sB + kc * TR * LDC + r * LDC + 2 * q, hin + gr * CP + kc * KC + 2 * q, ok);
+      }
+      cp_async_commit();
+      return;
+    }
+    if (gtid != 0) return;
+    fence_proxy_async();  // the planes' last readers finished before the barrier that led here
+    const int y = interior ? int(tile * T::TC * Q) : int((tile - nint) * (int64_t(T::TC) * PS) * QB);
+    mbar_arrive_expect_tx(bar_in, NK * TR * LDC * sizeof(double));
+#pragma unroll
+    for (int kc = 0; kc < NK; ++kc) tma_load_2d(sB + kc * TR * LDC, interior ? &tm_in_i : &tm_in_b, kc * KC, y, bar_in);
+  };
+  unsigned ph = 0;
+  auto wait_tile = [&](int64_t tile) {
+    if (SPLIT && tile >= nint) {
+      cp_async_wait<0>();
+      return true;
+    }
+    const bool ok = mbar_wait(bar_in, ph);
+    ph ^= 1u;
+    return ok;
+  };
+  double bias_r[2];  // a thread's channels are fixed for the whole kernel
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) bias_r[hh] = bias[wc * T::WCH + 8 * hh + g];
+  for (int i = tid; i < CP * (CP / 2); i += kPPThreads) {  // W_{L-1}, resident
+    const int r = i / (CP / 2), p = i % (CP / 2);
+    cp_async16(sA + r * LDA + 2 * p, w + int64_t(r) * CP + 2 * p, true);
+  }
+  cp_async_commit();
+  for (int i = tid; i < NF * CP; i += kPPThreads) sW[i] = wL[i];
+  if (tid == 0)
+    for (int b = 0; b < kPPGroups; ++b) mbar_init(&bars[b], 1);
+  cp_async_wait<0>();
+  __syncthreads();  // W_{L-1}, W_L and the barriers visible
+  pdl_wait();  // H_{L-1} is the predecessor's output
+  pdl_trigger();
+  if (nmy > 0) load_tile(tile_of(0));
+  double wacc[4] = {0.0, 0.0, 0.0, 0.0};  // dW_L[g][8 lw + 2t (+1)] (rows g < NF)
+  double bacc = 0.0, lacc = 0.0, cacc[2] = {0.0, 0.0};
+  bool dead = false;
+  // B fragments: column g of an n8 tile is slot 2j + (g & 1) of thread column wr*4 + (g >> 1)
+  const int brow = (wr * 4 + (g >> 1)) * S + (g & 1);
+  if (gp == 1) named_arrive(kPPBarTurn + 0, kPPThreads);  // group 0 takes the first turn
+  for (int64_t k = 0; k < nmy; ++k) {
+    const int64_t tile = tile_of(k);
+    double acc[T::NT][4];
+#pragma unroll
+    for (int j = 0; j < T::NT; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[j][e] = 0.0;
+    if (!dead) dead = named_sync_or(bar_group, GT, !wait_tile(tile));
+    named_sync(kPPBarTurn + gp, kPPThreads);  // this group's turn on the tensor pipe
+    if (!dead) {
+      // Z^T[ch][rows] = W_{L-1}[ch][cin] H_{L-1}^T[cin][rows]
+#pragma unroll
+      for (int kc = 0; kc < NK; ++kc) {
+        const double* cB = sB + kc * TR * LDC + brow * LDC;
+        const double* cA = sA + wc * T::WCH * LDA + kc * KC;
+#pragma unroll
+        for (int kk = 0; kk < KC; kk += 8) {
+          double a[4];
+          a[0] = cA[g * LDA + kk + t];
+          a[1] = cA[(g + 8) * LDA + kk + t];
+          a[2] = cA[g * LDA + kk + t + 4];
+          a[3] = cA[(g + 8) * LDA + kk + t + 4];
+#pragma unroll
+          for (int j = 0; j < T::NT; ++j) mma_m16n8k8(acc[j], a, cB[2 * j * LDC + kk + t], cB[2 * j * LDC + kk + t + 4]);
+        }
+      }
+    }
+    named_arrive(kPPBarTurn + (1 - gp), kPPThreads);  // the other group's turn
+    named_sync(bar_group, GT);                         // this group's input planes free
+    if (k + 1 < nmy && !dead) load_tile(tile_of(k + 1));
+    if (!dead) {
+      const int tc = wr * 4 + t;
+      const bool interior = tile < nint;
+      const int64_t p0 = interior ? tile * T::TC : (tile - nint) * (int64_t(T::TC) * PS);
+      const int64_t left = interior ? geo.ni - p0 : geo.nb - p0;
+      const int npts = int(left < (interior ? T::TC : T::TC * PS) ? left : (interior ? T::TC : T::TC * PS));
+      const int step = interior ? Q : QB;
+      const int nrows = npts * step;
+      // 1. bias on the order-0 coefficient, stable tanh jet; H_L into the shared tile
+      double a1r[2][PS];
+  #pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int ch = wc * T::WCH + 8 * hh + g;
+        double z[S];
+  #pragma unroll
+        for (int s = 0; s < S; ++s) z[s] = acc[s >> 1][2 * hh + (s & 1)];
+        if (interior) {
+          if (tc < npts) {
+            double hv[Q];
+            z[0] += bias_r[hh];
+            Jet<DIM, 3>::fwd(z, hv, a1r[hh][0]);
+  #pragma unroll
+            for (int s = 0; s < Q; ++s) sH[(tc * Q + s) * LDH + ch] = hv[s];
+          } else {  // rows of points past the segment stay finite for the row contractions
+  #pragma unroll
+            for (int s = 0; s < Q; ++s) sH[(tc * Q + s) * LDH + ch] = 0.0;
+          }
+        } else {
+  #pragma unroll
+          for (int kq = 0; kq < PS; ++kq) {
+            const int lp = tc * PS + kq;
+            if (lp < npts) {
+              double zz[QB], hv[QB];
+  #pragma unroll
+              for (int c = 0; c < QB; ++c) zz[c] = z[kq * QB + c];
+              zz[0] += bias_r[hh];
+              Jet<DIM, BO ? 1 : 0>::fwd(zz, hv, a1r[hh][kq]);
+  #pragma unroll
+              for (int c = 0; c < QB; ++c) sH[(lp * QB + c) * LDH + ch] = hv[c];
+            } else {
+  #pragma unroll
+              for (int c = 0; c < QB; ++c) sH[(lp * QB + c) * LDH + ch] = 0.0;
+            }
+          }
+        }
+      }
+      named_sync(bar_group, GT);
+      // 2. outputs Y^T[o][r] = W_L[o] . H[r] (+ b_L on order-0 rows) as DMMA tiles:
+      //    M = outputs (rows >= NF zero), N = tile rows (n8 tile j per warp), K = channels
+      const int kend = (nrows + 7) & ~7;
+      for (int j = lw; j < kend / 8; j += T::NWARPS) {
+        double c[4] = {0.0, 0.0, 0.0, 0.0};
+  #pragma unroll
+        for (int kk = 0; kk < CP; kk += 8) {
+          const double a[4] = {g < NF ? sW[g * CP + kk + t] : 0.0, 0.0, g < NF ? sW[g * CP + kk + t + 4] : 0.0, 0.0};
+          mma_m16n8k8(c, a, sH[(8 * j + g) * LDH + kk + t], sH[(8 * j + g) * LDH + kk + t + 4]);
+        }
+        if (g < NF) {
+          const int r0 = 8 * j + 2 * t;
+          if (r0 < nrows) sY[r0 * NF + g] = c[0] + (r0 % step == 0 ? bL[g] : 0.0);
+          if (r0 + 1 < nrows) sY[(r0 + 1) * NF + g] = c[1] + ((r0 + 1) % step == 0 ? bL[g] : 0.0);
+        }
+      }
+      named_sync(bar_group, GT);
+      // 3. residual seeds, one point per thread (dY rows up to the next multiple of 8 zeroed)
+      for (int i = gtid; i < (kend - nrows) * NF; i += GT) sD[nrows * NF + i] = 0.0;
+      if (interior) {
+        if (gtid < npts) {
+          double y[Q * NF], dy[Q * NF];
+  #pragma unroll
+          for (int k = 0; k < Q * NF; ++k) y[k] = sY[gtid * Q * NF + k];
+          lacc += interior_seed<DIM, HEAD>(y, pde_w[p0 + gtid], nu, gamma, dy);
+  #pragma unroll
+          for (int k = 0; k < Q * NF; ++k) sD[gtid * Q * NF + k] = dy[k];
+        }
+      } else {
+        for (int pt = gtid; pt < npts; pt += GT) {
+          const int64_t b = p0 + pt;
+          const double* yr = sY + pt * QB * NF;
+          double* dr = sD + pt * QB * NF;
+  #pragma unroll
+          for (int k = 0; k < QB * NF; ++k) dr[k] = 0.0;
+          double f[NFT];
+          if constexpr (BO == 0) {
+  #pragma unroll
+            for (int o = 0; o < NF; ++o) f[o] = yr[o];
+          } else {
+            f[0] = yr[unit_row<DIM>(1) * NF + 0];   // u = psi_y
+            f[1] = -yr[unit_row<DIM>(0) * NF + 0];  // v = -psi_x
+            f[2] = yr[1];                           // p
+          }
+          double gsd[NFT];
+  #pragma unroll
+          for (int o = 0; o < NFT; ++o) {
+            const double err = f[o] - target[b * NFT + o];
+            const double wgt = bnd_w[b * NFT + o];
+            lacc += bc * wgt * err * err;
+            gsd[o] = 2.0 * bc * wgt * err;
+          }
+          if constexpr (BO == 0) {
+  #pragma unroll
+            for (int o = 0; o < NF; ++o) dr[o] = gsd[o];
+          } else {
+            dr[unit_row<DIM>(1) * NF + 0] = gsd[0];
+            dr[unit_row<DIM>(0) * NF + 0] = -gsd[1];
+            dr[1] = gsd[2];
+          }
+        }
+      }
+      named_sync(bar_group, GT);
+      // 4. output-layer gradients dW_L[o][c] += sum_r dY[r][o] H[r][c] as DMMA tiles (M =
+      //    outputs, N = channels 8 lw.., K = tile rows); db_L over order-0 rows
+      for (int k0 = 0; k0 < kend; k0 += 8) {
+        const double a[4] = {g < NF ? sD[(k0 + t) * NF + g] : 0.0, 0.0, g < NF ? sD[(k0 + t + 4) * NF + g] : 0.0, 0.0};
+        mma_m16n8k8(wacc, a, sH[(k0 + t) * LDH + 8 * lw + g], sH[(k0 + t + 4) * LDH + 8 * lw + g]);
+      }
+      if (gtid < NF)
+        for (int r = 0; r < nrows; r += step) bacc += sD[r * NF + gtid];
+      // 5. dgrad through W_L and the jet VJP of layer L on the owned (point, channel) pairs
+  #pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int ch = wc * T::WCH + 8 * hh + g;
+        if (interior) {
+          if (tc < npts) {
+            double hv[Q], dh[Q], zb[Q];
+  #pragma unroll
+            for (int s = 0; s < Q; ++s) {
+              const int r = tc * Q + s;
+              double v = 0.0;
+  #pragma unroll
+              for (int o = 0; o < NF; ++o) v += sD[r * NF + o] * sW[o * CP + ch];
+              dh[s] = v;
+              hv[s] = sH[r * LDH + ch];
+            }
+            Jet<DIM, 3>::vjp(hv, a1r[hh][0], dh, zb);
+            double* dst = dL + (p0 + tc) * Q * CP + ch;
+  #pragma unroll
+            for (int s = 0; s < Q; ++s) dst[int64_t(s) * CP] = zb[s];
+            cacc[hh] += zb[0];
+          }
+        } else {
+  #pragma unroll
+          for (int kq = 0; kq < PS; ++kq) {
+            const int lp = tc * PS + kq;
+            if (lp < npts) {
+              double hv[QB], dh[QB], zb[QB];
+  #pragma unroll
+              for (int c = 0; c < QB; ++c) {
+                const int r = lp * QB + c;
+                double v = 0.0;
+  #pragma unroll
+                for (int o = 0; o < NF; ++o) v += sD[r * NF + o] * sW[o * CP + ch];
+                dh[c] = v;
+                hv[c] = sH[r * LDH + ch];
+              }
+              Jet<DIM, BO ? 1 : 0>::vjp(hv, a1r[hh][kq], dh, zb);
+              double* dst = dL + (geo.ni * Q + (p0 + lp) * QB) * CP + ch;
+  #pragma unroll
+              for (int c = 0; c < QB; ++c) dst[int64_t(c) * CP] = zb[c];
+              cacc[hh] += zb[0];
+            }
+          }
+        }
+      }
+    }
+  }
+  // turn counts balanced as in bwd_pingpong
+  if (gp == 0 && n0 == n1) named_sync(kPPBarTurn + 0, kPPThreads);
+  if (gp == 1 && n0 == n1 + 1) named_sync(kPPBarTurn + 1, kPPThreads);
+  if (__syncthreads_or(dead)) {
+    if (tid == 0) atomicExch(&g_device_fault, 1);
+    return;
+  }
+  // per-CTA partials, fixed-order reductions over the two groups
+  double* out = head_partial + int64_t(blockIdx.x) * PARTIAL;
+  double* red = smem;                          // [512] loss partials
+  double* cred = red + kPPThreads;             // [groups * WR][CP] bias partials of layer L-1
+  double* wsh = cred + kPPGroups * T::WR * CP;  // [8 warps][32 lanes][2] group 1's dW_L
+  double* bsh = wsh + T::NWARPS * 32 * 2;       // [NF] group 1's db_L
+  if (gp == 1) {
+    wsh[(lw * 32 + lane) * 2] = wacc[0];
+    wsh[(lw * 32 + lane) * 2 + 1] = wacc[1];
+    if (gtid < NF) bsh[gtid] = bacc;
+  }
+  red[tid] = lacc;
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    double v = cacc[hh];
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    if (t == 0) cred[(gp * T::WR + wr) * CP + wc * T::WCH + 8 * hh + g] = v;
+  }
+  __syncthreads();
+  if (gp == 0) {
+    if (g < NF) {
+      out[g * CP + 8 * lw + 2 * t] = wacc[0] + wsh[(lw * 32 + lane) * 2];
+      out[g * CP + 8 * lw + 2 * t + 1] = wacc[1] + wsh[(lw * 32 + lane) * 2 + 1];
+    }
+    if (gtid < NF) out[NF * CP + gtid] = bacc + bsh[gtid];
+  }
+  if (tid == 0) {
+    double sum = 0.0;
+    for (int i = 0; i < kPPThreads; ++i) sum += red[i];
+    out[NF * CP + NF] = sum;
+  }
+  for (int c = tid; c < CP; c += kPPThreads) {
+    double sum = 0.0;
+    for (int r = 0; r < kPPGroups * T::WR; ++r) sum += cred[r * CP + c];
+    out[NF * CP + NF + 1 + c] = sum;
+  }
+  if (tid == 0)
+    for (int b = 0; b < kPPGroups; ++b) mbar_inval(&bars[b]);
+}
+
+
 // ----------------------------------------------------------------------------------
 // first layer: coordinates -> affine jet -> stable tanh jet
 template <int DIM, int BO>
@@ -2525,22 +2889,50 @@ struct HeadOps {
 template <int DIM, int BO, int HEAD>
 struct FwdHeadOps {
   static constexpr int NF = HeadTraits<HEAD>::NF;
+  static constexpr bool kPingPong = DIM == 2;  // 2-D: the two-group kernel over 80-row half tiles
   static cudaError_t setup(int& occ) {
-    constexpr size_t smem = fwd_head_smem_bytes<DIM, NF>();
-    static_assert(smem <= kMaxSmem, "fused head tile exceeds shared memory");
-    cudaError_t e = allow_smem(fwd_head<DIM, BO, HEAD>, smem);
-    occ = occupancy(fwd_head<DIM, BO, HEAD>, smem, HeadTile<DIM>::THREADS);
-    return e;
+    if constexpr (kPingPong) {
+      constexpr size_t smem = hpp_smem_bytes<NF>();
+      static_assert(smem <= kMaxSmem, "two-group head tile exceeds shared memory");
+      cudaError_t e = allow_smem(head_pingpong<BO, HEAD>, smem);
+      occ = occupancy(head_pingpong<BO, HEAD>, smem, kPPThreads);
+      return e;
+    } else {
+      constexpr size_t smem = fwd_head_smem_bytes<DIM, NF>();
+      static_assert(smem <= kMaxSmem, "fused head tile exceeds shared memory");
+      cudaError_t e = allow_smem(fwd_head<DIM, BO, HEAD>, smem);
+      occ = occupancy(fwd_head<DIM, BO, HEAD>, smem, HeadTile<DIM>::THREADS);
+      return e;
+    }
   }
   static int64_t tiles(const Geometry& g) {
-    using TL = Tiles<DIM, BO, HeadTile<DIM>::TC>;
-    return TL::interior(g.ni) + TL::boundary(g.nb);
+    if constexpr (kPingPong) {
+      using TL = Tiles<2, BO, PPTile::TC>;
+      return (TL::interior(g.ni) + TL::boundary(g.nb) + 1) / 2;
+    } else {
+      using TL = Tiles<DIM, BO, HeadTile<DIM>::TC>;
+      return TL::interior(g.ni) + TL::boundary(g.nb);
+    }
   }
-  static void launch(int grid, cudaStream_t st, const double* hin, const double* w, const double* b,
-                     const double* wl, const double* bl, const double* pw, const double* bw, const double* tg,
-                     double nu, double gm, double bc, double* dl, double* hpart, Geometry g) {
-    launch_kernel(fwd_head<DIM, BO, HEAD>, grid, HeadTile<DIM>::THREADS, fwd_head_smem_bytes<DIM, NF>(), st, hin, w, b,
-                  wl, bl, pw, bw, tg, nu, gm, bc, dl, hpart, g);
+  static cudaError_t launch(int grid, cudaStream_t st, const double* hin, const double* w, const double* b,
+                            const double* wl, const double* bl, const double* pw, const double* bw, const double* tg,
+                            double nu, double gm, double bc, double* dl, double* hpart, Geometry g) {
+    if constexpr (kPingPong) {
+      using TL = Tiles<2, BO, PPTile::TC>;
+      constexpr int TR = PPTile::TR, BB = pp_boundary_box_rows<BO>();
+      const int64_t ri = g.ni * TL::Q, rb = g.nb * TL::QB;  // interior / boundary segment rows
+      if (ri > INT32_MAX - TR || rb > INT32_MAX - TR) return cudaErrorInvalidValue;  // TMA rows are int32
+      CUtensorMap m[2];
+      cudaError_t e;
+      if ((e = row_tensor_map(&m[0], hin, ri, kFusedWidth, LDC, TR)) != cudaSuccess ||
+          (e = row_tensor_map(&m[1], hin + ri * kFusedWidth, rb, kFusedWidth, LDC, BB)) != cudaSuccess)
+        return e;
+      return launch_kernel(head_pingpong<BO, HEAD>, grid, kPPThreads, hpp_smem_bytes<NF>(), st, m[0], m[1], hin, w,
+                           b, wl, bl, pw, bw, tg, nu, gm, bc, dl, hpart, g);
+    } else {
+      return launch_kernel(fwd_head<DIM, BO, HEAD>, grid, HeadTile<DIM>::THREADS, fwd_head_smem_bytes<DIM, NF>(), st,
+                           hin, w, b, wl, bl, pw, bw, tg, nu, gm, bc, dl, hpart, g);
+    }
   }
 };
 
@@ -2918,11 +3310,13 @@ static int run_eval(const flashns_b200_plan* p, const double* coordinates, const
       const LayerDesc& L = tab.l[nh - 1];
       const LayerDesc& H = tab.l[nh];
       mark();
+      cudaError_t le = cudaSuccess;
       with_fwd_head(p->dim, p->bo, p->head, [&](auto ops) {
-        ops.launch(p->grid_head, stream, ws + p->off_h[nh - 1], Wp(L), Bp(L), Wp(H),
-                   Bp(H), pde_weights, boundary_weights, target, p->nu, p->gamma, p->bc,
-                   ws + p->off_d[nh % 2], ws + p->off_head, g);
+        le = ops.launch(p->grid_head, stream, ws + p->off_h[nh - 1], Wp(L), Bp(L), Wp(H),
+                        Bp(H), pde_weights, boundary_weights, target, p->nu, p->gamma, p->bc,
+                        ws + p->off_d[nh % 2], ws + p->off_head, g);
       });
+      if (le != cudaSuccess) return int(le);
       if ((e = cudaGetLastError()) != cudaSuccess) return int(e);
     } else {
       const LayerDesc& L = tab.l[nh];
