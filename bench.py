@@ -286,20 +286,19 @@ def main():
     ms_step = float(elapsed) / args.steps
     clocks = sampler.stop()
 
-    # end to end: host (pinned) inputs -> device, evaluation, all-reduce, result -> host, every step
-    hx = ev.x.cpu().pin_memory(); hpw = ev.pde_weights.cpu().pin_memory()
-    hbw = ev.boundary_weights.cpu().pin_memory(); htg = ev.target.cpu().pin_memory()
-    hp = params_host.pin_memory(); hout = torch.empty(ev.parameters + 1, dtype=torch.float64).pin_memory()
-    h2d = sum(t.numel() * 8 for t in (hx, hpw, hbw, htg, hp))
+    # end to end: every step copies all inputs (coordinates, weights, targets, parameters)
+    # from one pinned host staging buffer to the device in a single transfer, evaluates,
+    # all-reduces and reads [grad, loss] back to the host
+    hin, din, dparams = ev.input_arena(params_host)
+    hout = torch.empty(ev.parameters + 1, dtype=torch.float64).pin_memory()
+    h2d = hin.numel() * 8
     d2h = hout.numel() * 8
 
     def e2e_step():
-        ev.x.copy_(hx, non_blocking=True)
-        ev.pde_weights.copy_(hpw, non_blocking=True)
-        ev.boundary_weights.copy_(hbw, non_blocking=True)
-        ev.target.copy_(htg, non_blocking=True)
-        params.copy_(hp, non_blocking=True)
-        step()
+        din.copy_(hin, non_blocking=True)
+        ev(dparams, out)
+        if world > 1:
+            dist.all_reduce(out)
         hout.copy_(out, non_blocking=True)
         stream.synchronize()
 

@@ -141,6 +141,31 @@ class PackedEvaluator:
         _lib.check(status, "flashns_b200_eval")
         return out
 
+    def input_arena(self, flat):
+        """Stage every input of a step in one buffer pair: a pinned host buffer and a device
+        buffer, both ``[x | pde_weights | boundary_weights | target | parameters]`` with each
+        segment starting on a 16-byte boundary.  The evaluator's inputs become views of the
+        device buffer, so one host-to-device copy refreshes all of them.  Returns
+        ``(host, device, parameters view)``; ``flat`` is copied into both buffers."""
+        parts = [self.x, self.pde_weights, self.boundary_weights, self.target,
+                 flat.detach().to(dtype=torch.float64).reshape(-1)]
+        if parts[-1].numel() != self.parameters:
+            raise ValueError(f"flat FP64 parameters [{self.parameters}] required")
+        sizes = [t.numel() for t in parts]
+        offsets, off = [], 0
+        for n in sizes:
+            offsets.append(off)
+            off += n + (n & 1)  # even number of doubles: every segment 16-byte aligned
+        device = torch.empty(max(off, 2), dtype=torch.float64, device=self.device)
+        views = [device[o:o + n] for o, n in zip(offsets, sizes)]
+        for v, t in zip(views, parts):
+            v.copy_(t.reshape(-1))
+        shapes = [t.shape for t in parts[:4]]
+        self.x, self.pde_weights, self.boundary_weights, self.target = (
+            v.view(shape) for v, shape in zip(views[:4], shapes))
+        host = device.cpu().pin_memory()
+        return host, device, views[4]
+
     def split(self, out):
         """Views ``(loss, [dW_0..dW_L, db_0..db_L])`` of an output buffer."""
         grads, offset = [], 0

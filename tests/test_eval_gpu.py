@@ -217,3 +217,35 @@ def test_unaligned_parameter_view(cuda):
     out = ev(view)
     torch.cuda.synchronize()
     np.testing.assert_array_equal(out.cpu().numpy(), ref)
+
+
+def test_input_arena_single_copy_refreshes_every_input(cuda):
+    """PackedEvaluator.input_arena: the inputs become views of one device buffer, results
+    are unchanged, and one host-to-device copy of new host values is what the next
+    evaluation sees."""
+    import torch
+    from flashns_b200.evaluator import PackedEvaluator, flat_parameters, xavier_normal
+    from flashns_b200.ns_seed import NSLoss
+    from flashns_b200.problems import kovasznay
+    widths = [2, 64, 64, 64, 2]
+    a, b = kovasznay(301, 77, seed=11), kovasznay(301, 77, seed=12)
+    make = lambda pts: PackedEvaluator(pts.x, pts.interior_count, pts.pde_weights, pts.boundary_weights, pts.target,
+                                       widths, head="psi", boundary_order=1, loss=NSLoss(0.05, 0.0, 5.0), device=cuda)
+    ev, ev_b = make(a), make(b)
+    ws, bs = xavier_normal(widths, 0)
+    p = flat_parameters(ws, bs)
+    before = ev(p.to(cuda)).cpu()
+    host, device, dparams = ev.input_arena(p)
+    assert host.is_pinned() and device.is_cuda and dparams.data_ptr() % 16 == 0
+    assert ev.x.data_ptr() == device.data_ptr()
+    assert torch.equal(ev(dparams).cpu(), before)
+    # stage point set b and new parameters on the host, then one copy
+    p2 = p * 0.9
+    n = [a.x.numel(), a.pde_weights.numel(), a.boundary_weights.numel(), a.target.numel()]
+    o = 0
+    for t, k in zip([b.x, b.pde_weights, b.boundary_weights, b.target], n):
+        host[o:o + k] = t.reshape(-1)
+        o += k + (k & 1)
+    host[o:o + p2.numel()] = p2
+    device.copy_(host)
+    assert torch.equal(ev(dparams).cpu(), ev_b(p2.to(cuda)).cpu())
