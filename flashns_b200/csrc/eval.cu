@@ -2263,37 +2263,37 @@ __global__ void __launch_bounds__(kPPThreads, 1)
       const int nrows = npts * step;
       // 1. bias on the order-0 coefficient, stable tanh jet; H_L into the shared tile
       double a1r[2][PS];
-  #pragma unroll
+#pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const int ch = wc * T::WCH + 8 * hh + g;
         double z[S];
-  #pragma unroll
+#pragma unroll
         for (int s = 0; s < S; ++s) z[s] = acc[s >> 1][2 * hh + (s & 1)];
         if (interior) {
           if (tc < npts) {
             double hv[Q];
             z[0] += bias_r[hh];
             Jet<DIM, 3>::fwd(z, hv, a1r[hh][0]);
-  #pragma unroll
+#pragma unroll
             for (int s = 0; s < Q; ++s) sH[(tc * Q + s) * LDH + ch] = hv[s];
           } else {  // rows of points past the segment stay finite for the row contractions
-  #pragma unroll
+#pragma unroll
             for (int s = 0; s < Q; ++s) sH[(tc * Q + s) * LDH + ch] = 0.0;
           }
         } else {
-  #pragma unroll
+#pragma unroll
           for (int kq = 0; kq < PS; ++kq) {
             const int lp = tc * PS + kq;
             if (lp < npts) {
               double zz[QB], hv[QB];
-  #pragma unroll
+#pragma unroll
               for (int c = 0; c < QB; ++c) zz[c] = z[kq * QB + c];
               zz[0] += bias_r[hh];
               Jet<DIM, BO ? 1 : 0>::fwd(zz, hv, a1r[hh][kq]);
-  #pragma unroll
+#pragma unroll
               for (int c = 0; c < QB; ++c) sH[(lp * QB + c) * LDH + ch] = hv[c];
             } else {
-  #pragma unroll
+#pragma unroll
               for (int c = 0; c < QB; ++c) sH[(lp * QB + c) * LDH + ch] = 0.0;
             }
           }
@@ -2305,7 +2305,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
       const int kend = (nrows + 7) & ~7;
       for (int j = lw; j < kend / 8; j += T::NWARPS) {
         double c[4] = {0.0, 0.0, 0.0, 0.0};
-  #pragma unroll
+#pragma unroll
         for (int kk = 0; kk < CP; kk += 8) {
           const double a[4] = {g < NF ? sW[g * CP + kk + t] : 0.0, 0.0, g < NF ? sW[g * CP + kk + t + 4] : 0.0, 0.0};
           mma_m16n8k8(c, a, sH[(8 * j + g) * LDH + kk + t], sH[(8 * j + g) * LDH + kk + t + 4]);
@@ -2322,10 +2322,10 @@ __global__ void __launch_bounds__(kPPThreads, 1)
       if (interior) {
         if (gtid < npts) {
           double y[Q * NF], dy[Q * NF];
-  #pragma unroll
+#pragma unroll
           for (int k = 0; k < Q * NF; ++k) y[k] = sY[gtid * Q * NF + k];
           lacc += interior_seed<DIM, HEAD>(y, pde_w[p0 + gtid], nu, gamma, dy);
-  #pragma unroll
+#pragma unroll
           for (int k = 0; k < Q * NF; ++k) sD[gtid * Q * NF + k] = dy[k];
         }
       } else {
@@ -2333,11 +2333,11 @@ __global__ void __launch_bounds__(kPPThreads, 1)
           const int64_t b = p0 + pt;
           const double* yr = sY + pt * QB * NF;
           double* dr = sD + pt * QB * NF;
-  #pragma unroll
+#pragma unroll
           for (int k = 0; k < QB * NF; ++k) dr[k] = 0.0;
           double f[NFT];
           if constexpr (BO == 0) {
-  #pragma unroll
+#pragma unroll
             for (int o = 0; o < NF; ++o) f[o] = yr[o];
           } else {
             f[0] = yr[unit_row<DIM>(1) * NF + 0];   // u = psi_y
@@ -2345,7 +2345,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
             f[2] = yr[1];                           // p
           }
           double gsd[NFT];
-  #pragma unroll
+#pragma unroll
           for (int o = 0; o < NFT; ++o) {
             const double err = f[o] - target[b * NFT + o];
             const double wgt = bnd_w[b * NFT + o];
@@ -2353,7 +2353,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
             gsd[o] = 2.0 * bc * wgt * err;
           }
           if constexpr (BO == 0) {
-  #pragma unroll
+#pragma unroll
             for (int o = 0; o < NF; ++o) dr[o] = gsd[o];
           } else {
             dr[unit_row<DIM>(1) * NF + 0] = gsd[0];
@@ -2372,45 +2372,45 @@ __global__ void __launch_bounds__(kPPThreads, 1)
       if (gtid < NF)
         for (int r = 0; r < nrows; r += step) bacc += sD[r * NF + gtid];
       // 5. dgrad through W_L and the jet VJP of layer L on the owned (point, channel) pairs
-  #pragma unroll
+#pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const int ch = wc * T::WCH + 8 * hh + g;
         if (interior) {
           if (tc < npts) {
             double hv[Q], dh[Q], zb[Q];
-  #pragma unroll
+#pragma unroll
             for (int s = 0; s < Q; ++s) {
               const int r = tc * Q + s;
               double v = 0.0;
-  #pragma unroll
+#pragma unroll
               for (int o = 0; o < NF; ++o) v += sD[r * NF + o] * sW[o * CP + ch];
               dh[s] = v;
               hv[s] = sH[r * LDH + ch];
             }
             Jet<DIM, 3>::vjp(hv, a1r[hh][0], dh, zb);
             double* dst = dL + (p0 + tc) * Q * CP + ch;
-  #pragma unroll
+#pragma unroll
             for (int s = 0; s < Q; ++s) dst[int64_t(s) * CP] = zb[s];
             cacc[hh] += zb[0];
           }
         } else {
-  #pragma unroll
+#pragma unroll
           for (int kq = 0; kq < PS; ++kq) {
             const int lp = tc * PS + kq;
             if (lp < npts) {
               double hv[QB], dh[QB], zb[QB];
-  #pragma unroll
+#pragma unroll
               for (int c = 0; c < QB; ++c) {
                 const int r = lp * QB + c;
                 double v = 0.0;
-  #pragma unroll
+#pragma unroll
                 for (int o = 0; o < NF; ++o) v += sD[r * NF + o] * sW[o * CP + ch];
                 dh[c] = v;
                 hv[c] = sH[r * LDH + ch];
               }
               Jet<DIM, BO ? 1 : 0>::vjp(hv, a1r[hh][kq], dh, zb);
               double* dst = dL + (geo.ni * Q + (p0 + lp) * QB) * CP + ch;
-  #pragma unroll
+#pragma unroll
               for (int c = 0; c < QB; ++c) dst[int64_t(c) * CP] = zb[c];
               cacc[hh] += zb[0];
             }
