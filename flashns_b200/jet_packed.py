@@ -12,6 +12,7 @@ from functools import lru_cache
 import torch
 
 from flashns_b200.jet_spec import JetSpec
+from flashns_b200.jet_stable import stable_a1  # noqa: F401  (the reference exports it here too)
 
 
 @dataclass(frozen=True)

@@ -148,3 +148,22 @@ def test_solver_checkpoint_round_trip(tmp_path):
     assert digest == hashlib.sha256((tmp_path / "run.pt").read_bytes()).hexdigest()
     back = load_checkpoint(tmp_path / "run.pt")
     assert torch.equal(back["flat_parameters"], flat) and back["problem"]["re"] == 20.0 and back["seed"] == 1
+
+
+def test_jet_multiply_and_manifest():
+    """jet_stable.multiply is the truncated Cauchy product of the oracle
+    (src/flashns/jet_stable.py:52-59); the activation manifest keeps the reference's keys."""
+    import numpy as np
+    import torch
+
+    from flashns_b200 import jet_packed, jet_stable
+    from oracle import jets as J
+    for dim in (2, 3):
+        gen = torch.Generator().manual_seed(dim)
+        a = torch.randn(7, J.q(dim), 3, dtype=torch.float64, generator=gen)
+        b = torch.randn(7, J.q(dim), 3, dtype=torch.float64, generator=gen)
+        np.testing.assert_allclose(jet_stable.multiply(a, b, dim).numpy(), J.cauchy(a.numpy(), b.numpy(), dim, 3),
+                                   rtol=1e-15, atol=1e-15)
+    m = jet_stable.manifest(2, "a" * 64)
+    assert m["activation_aux_state"]["strategy"] == "stable_aux_a1" and m["q"] == 10
+    assert jet_packed.stable_a1 is jet_stable.stable_a1
