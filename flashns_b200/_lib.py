@@ -54,6 +54,11 @@ SIGNATURES = {
     "flashns_stable_tail3": [_c_int, ctypes.c_bool] + [_c_ptr] * 5 + [_c_size, _c_size, _c_ptr],
     "flashns_stable_dgrad_vjp": [_c_int, ctypes.c_bool] + [_c_ptr] * 5 + [_c_int] * 3 + [_c_ptr],
     "flashns_stable_dgrad_shared_bytes": [],
+    # the reference's Hopper plan names (experiments/cuda_jet_hopper/hopper.py:37-63)
+    "flashns_hopper_initialize": [],
+    "flashns_hopper_resources": [_c_int, ctypes.c_bool, ctypes.POINTER(ctypes.c_longlong)],
+    "flashns_hopper_create": [_c_int, _c_ptr, _c_ptr, _c_int, _c_int, _c_int, ctypes.POINTER(_c_ptr)],
+    "flashns_hopper_launch": [_c_ptr, _c_int, ctypes.c_bool, _c_ptr, _c_ptr, _c_ptr, _c_ptr],
 }
 
 KERNEL_KINDS = {0: "pack", 1: "first", 2: "forward", 3: "head", 4: "backward", 5: "wgrad", 6: "reduce",
@@ -74,6 +79,8 @@ def library():
             fn = getattr(lib, name)
             fn.argtypes = argtypes
             fn.restype = ctypes.c_int
+        lib.flashns_hopper_destroy.argtypes = [_c_ptr]  # void, as the reference declares it
+        lib.flashns_hopper_destroy.restype = None
         _library = lib
     return _library
 

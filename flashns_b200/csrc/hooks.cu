@@ -12,7 +12,10 @@
 //   flashns_v8_loss_seed                                          :325-337
 //   flashns_stable_activation / _tail3    experiments/cuda_jet_h100/stable_kernels.cu:93-131
 //   flashns_stable_dgrad_vjp                                      stable_dgrad.cu:150-174
+//   flashns_hopper_initialize / _resources / _create / _destroy / _launch
+//                                         experiments/cuda_jet_hopper/hopper.cu:287-353
 #include <climits>
+#include <new>
 #include <cstddef>
 #include <cstdint>
 
@@ -649,3 +652,74 @@ extern "C" int flashns_b200_residuals(int head, int dim, const double* jets, dou
   else residual_values<FLASHNS_B200_HEAD_PSI, 3><<<g, kHookThreads, 0, stream>>>(jets, nu, out, n);
   return int(cudaGetLastError());
 }
+
+// ---- plan-based dense dgrad (+ jet VJP) under the reference's Hopper names
+// (experiments/cuda_jet_hopper/hopper.cu:287-353): the same argument meaning, limits and
+// error codes, so the reference's binding (experiments/cuda_jet_hopper/hopper.py) can load
+// this library on B200.  The plan keeps D, W and the sizes; a launch runs dense_dgrad.
+namespace flashns_b200 {
+namespace {
+struct DgradPlan {
+  const double* d;
+  const double* w;
+  int batch, cout, cin, q;
+};
+
+template <int DIM, bool FUSED>
+int dgrad_resources(long long* values) {
+  cudaFuncAttributes attr;
+  cudaError_t e = cudaFuncGetAttributes(&attr, dense_dgrad<DIM, FUSED>);
+  if (e != cudaSuccess) return int(e);
+  int blocks = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, dense_dgrad<DIM, FUSED>, kHookThreads, 0);
+  if (e != cudaSuccess) return int(e);
+  values[0] = attr.numRegs;
+  values[1] = kHookThreads;
+  values[2] = 0;  // no dynamic shared memory
+  values[3] = attr.sharedSizeBytes;
+  values[4] = attr.localSizeBytes;
+  values[5] = blocks;
+  values[6] = attr.maxDynamicSharedSizeBytes;
+  values[7] = attr.binaryVersion;
+  values[8] = attr.ptxVersion;
+  return int(cudaSuccess);
+}
+}  // namespace
+}  // namespace flashns_b200
+
+extern "C" {
+
+int flashns_hopper_initialize(void) { return int(cudaSuccess); }  // no kernel attribute to set
+
+int flashns_hopper_resources(int dim, bool fused, long long* values) {
+  using namespace flashns_b200;
+  if (!values || (dim != 2 && dim != 3)) return int(cudaErrorInvalidValue);
+  if (dim == 2) return fused ? dgrad_resources<2, true>(values) : dgrad_resources<2, false>(values);
+  return fused ? dgrad_resources<3, true>(values) : dgrad_resources<3, false>(values);
+}
+
+int flashns_hopper_create(int dim, const double* d, const double* w, int batch, int cout, int cin, void** result) {
+  using namespace flashns_b200;
+  if (!result) return int(cudaErrorInvalidValue);
+  *result = nullptr;
+  if ((dim != 2 && dim != 3) || !d || !w || batch <= 0 || batch > INT_MAX / 20 || (cout != 32 && cout != 64) ||
+      (cin != 32 && cin != 64) || (reinterpret_cast<uintptr_t>(d) & 15) || (reinterpret_cast<uintptr_t>(w) & 15))
+    return int(cudaErrorInvalidValue);
+  DgradPlan* plan = new (std::nothrow) DgradPlan{d, w, batch, cout, cin, dim == 2 ? 10 : 20};
+  if (!plan) return int(cudaErrorMemoryAllocation);
+  *result = plan;
+  return int(cudaSuccess);
+}
+
+void flashns_hopper_destroy(void* plan) { delete static_cast<flashns_b200::DgradPlan*>(plan); }
+
+int flashns_hopper_launch(void* handle, int dim, bool fused, const double* hidden, const double* aux, double* output,
+                          cudaStream_t stream) {
+  using namespace flashns_b200;
+  if (!handle || !output || (dim != 2 && dim != 3) || (fused && (!hidden || !aux))) return int(cudaErrorInvalidValue);
+  const DgradPlan& p = *static_cast<const DgradPlan*>(handle);
+  if (p.q != (dim == 2 ? 10 : 20)) return int(cudaErrorInvalidValue);
+  return flashns_stable_dgrad_vjp(dim, fused, p.d, p.w, hidden, aux, output, p.batch, p.cout, p.cin, stream);
+}
+
+}  // extern "C"

@@ -247,6 +247,21 @@ int flashns_b200_pack_coordinates(const double* x, int64_t full_points, int64_t 
 /* shared memory the dense dgrad uses per block (0: this implementation stages none) */
 int flashns_stable_dgrad_shared_bytes(void);
 
+/* Plan-based dense dgrad under the reference's Hopper names
+ * (experiments/cuda_jet_hopper/hopper.cu:287-353, bound by
+ * experiments/cuda_jet_hopper/hopper.py:37-63): create keeps D [batch*Q, cout] and
+ * W [cout, cin] (cout, cin in {32, 64}; both 16-byte aligned; 0 < batch <= INT_MAX/20);
+ * launch writes out [batch*Q, cin] = D W, followed by the jet VJP with hidden [batch*Q, cin]
+ * and aux [batch, cin] when fused.  resources fills 9 values: registers per thread, threads
+ * per CTA, dynamic and static shared bytes, local bytes per thread, predicted CTAs per SM,
+ * max dynamic shared bytes, binary and PTX versions. */
+int flashns_hopper_initialize(void);
+int flashns_hopper_resources(int dim, bool fused, long long* values);
+int flashns_hopper_create(int dim, const double* d, const double* w, int batch, int cout, int cin, void** plan);
+void flashns_hopper_destroy(void* plan);
+int flashns_hopper_launch(void* plan, int dim, bool fused, const double* hidden, const double* aux, double* output,
+                          cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

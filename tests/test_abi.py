@@ -12,7 +12,7 @@ ROOT = Path(__file__).resolve().parents[1]
 def declared():
     names = []
     for header in sorted((ROOT / "include").glob("*.h")):
-        names += re.findall(r"^int\s+(\w+)\s*\(", header.read_text(), flags=re.M)
+        names += re.findall(r"^(?:int|void)\s+(\w+)\s*\(", header.read_text(), flags=re.M)
     return names
 
 
@@ -69,3 +69,27 @@ def test_no_fallback_when_library_missing(tmp_path, monkeypatch):
     monkeypatch.setattr(_lib, "_library", None)
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         _lib.library()
+
+
+def test_hopper_plan_names_reject_bad_arguments(library):
+    """The reference's Hopper plan limits (experiments/cuda_jet_hopper/hopper.cu:303-310),
+    checked on the host before any CUDA call."""
+    from flashns_b200 import _lib
+    lib = _lib.library()
+    plan = ctypes.c_void_p()
+    p16, p8 = ctypes.c_void_p(16), ctypes.c_void_p(24)
+    assert lib.flashns_hopper_create(2, p16, p16, 10, 48, 64, ctypes.byref(plan)) == 1   # cout not 32/64
+    assert lib.flashns_hopper_create(2, p16, p16, 10, 64, 16, ctypes.byref(plan)) == 1   # cin not 32/64
+    assert lib.flashns_hopper_create(4, p16, p16, 10, 64, 64, ctypes.byref(plan)) == 1   # dim
+    assert lib.flashns_hopper_create(2, p16, p16, 0, 64, 64, ctypes.byref(plan)) == 1    # empty batch
+    assert lib.flashns_hopper_create(2, p8, p16, 10, 64, 64, ctypes.byref(plan)) == 1    # D not 16-byte aligned
+    assert lib.flashns_hopper_create(2, None, p16, 10, 64, 64, ctypes.byref(plan)) == 1
+    assert lib.flashns_hopper_create(2, p16, p16, 10, 64, 64, None) == 1
+    assert lib.flashns_hopper_create(3, p16, p16, 10, 32, 64, ctypes.byref(plan)) == 0 and plan.value
+    try:
+        assert lib.flashns_hopper_launch(plan, 2, False, None, None, p16, None) == 1      # plan is 3-D
+        assert lib.flashns_hopper_launch(plan, 3, True, None, None, p16, None) == 1       # fused needs H, a1
+        assert lib.flashns_hopper_launch(plan, 3, False, None, None, None, None) == 1     # no output
+        assert lib.flashns_hopper_launch(None, 3, False, None, None, p16, None) == 1
+    finally:
+        lib.flashns_hopper_destroy(plan)

@@ -179,3 +179,53 @@ def test_coordinate_hooks_handle_empty_and_value_only(cuda):
         coords = layout.coordinates(x)
         assert close_ratio(dw.cpu(), (d.T @ coords).cpu()) <= 1
         assert close_ratio(db.cpu(), d[zero].sum(0).cpu()) <= 1
+
+
+def test_hopper_plan_names_match_oracle(cuda):
+    """flashns_hopper_create / _launch / _destroy (the reference's Hopper plan ABI,
+    experiments/cuda_jet_hopper/hopper.cu:287-353): D W, fused with the jet VJP or not, on
+    the oracle; resources fills the nine values the reference's binding reads."""
+    import ctypes
+
+    import torch
+
+    from flashns_b200 import _lib
+    from oracle import jets as J
+    lib = _lib.library()
+    assert lib.flashns_hopper_initialize() == 0
+    for dim in (2, 3):
+        for fused in (False, True):
+            vals = (ctypes.c_longlong * 9)()
+            assert lib.flashns_hopper_resources(dim, fused, vals) == 0
+            assert vals[1] > 0 and vals[0] > 0 and vals[5] >= 1
+    rng = np.random.default_rng(11)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)
+    for dim in (2, 3):
+        q = J.q(dim)
+        for cout, cin in ((32, 64), (64, 32), (64, 64)):
+            batch = 37
+            z = rng.normal(size=(batch, q, cin)) * 0.4
+            h, a1 = J.tanh_jet(z, dim)
+            d = rng.normal(size=(batch, q, cout))
+            w = rng.normal(size=(cout, cin)) / np.sqrt(cout)
+            dg, wg, hg, ag = (T(v, cuda) for v in (d, w, h, a1))
+            plan = ctypes.c_void_p()
+            assert lib.flashns_hopper_create(dim, _lib_ptr(dg), _lib_ptr(wg), batch, cout, cin, ctypes.byref(plan)) == 0
+            try:
+                for fused in (False, True):
+                    out = torch.full((batch, q, cin), float("nan"), dtype=torch.float64, device=cuda)
+                    assert lib.flashns_hopper_launch(plan, dim, fused, _lib_ptr(hg), _lib_ptr(ag), _lib_ptr(out),
+                                                     stream) == 0
+                    torch.cuda.synchronize()
+                    expect = J.tanh_vjp(h, a1, d @ w, dim) if fused else d @ w
+                    assert close_ratio(out.cpu(), expect) <= 1, (dim, cout, cin, fused)
+                # a plan is tied to its jet size: the other dimension is refused
+                out = torch.empty((batch, q, cin), dtype=torch.float64, device=cuda)
+                assert lib.flashns_hopper_launch(plan, 5 - dim, False, None, None, _lib_ptr(out), stream) == 1
+            finally:
+                lib.flashns_hopper_destroy(plan)
+
+
+def _lib_ptr(t):
+    import ctypes
+    return ctypes.c_void_p(t.data_ptr())
