@@ -27,7 +27,9 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("FLASHNS_REFERENCE", "/root/reference"))
+if "FLASHNS_REFERENCE" not in os.environ:
+    sys.exit("set FLASHNS_REFERENCE to the root of a FlashNS checkout (the directory holding src/flashns)")
+REF = Path(os.environ["FLASHNS_REFERENCE"])
 sys.path.insert(0, str(REF / "src"))
 
 from flashns.jet_packed import PackedLayout, TensorActivation  # noqa: E402
