@@ -1,6 +1,7 @@
 """Benchmark: FP64 loss + parameter-gradient evaluations per second on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg1] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg1]
+                    [--impl ours|reference|reference-gpu] [--route F|B1|v8|v8+]
 
 Workload: the Kovasznay stream-function net
 2->64x4->2 on 16,384 interior points with full third-order Q10 jets plus 4,096
@@ -13,6 +14,12 @@ scaling); ``value`` counts cfg1-sized shard evaluations of all ranks per second.
 
 ``--impl reference`` times the reference algorithm's CPU path (the oracle port of
 ``PackedPINN``, all host threads) on the same workload; rank 0 alone prints.
+
+``--impl reference-gpu --config ref16k`` times one of the reference's own GPU routes on
+this GPU (``--route``: F, its published H100 headline route; B1; the v8 packed route;
+or v8+, the v8 route with every opt-in fused hook), with the reference's kernels compiled from its sources into ``baseline/_ref/``
+by ``baseline/build_reference_gpu.py`` and torch FP64 GEMMs between them, replayed from a
+CUDA graph as the reference's benchmarks do.  Rank 0 alone runs it.
 """
 
 import argparse
@@ -29,6 +36,9 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 REF16K_PUBLISHED_MS = 1.832
+# the reference's published H100 replay times of its routes at 16,384 points
+# (docs/cuda-h100-results.md:54-64); the v8 packed routes have none
+REFERENCE_ROUTE_PUBLISHED_MS = {"F": 1.832, "B1": 1.954}
 METRIC = "FP64 loss+param-gradient evals/sec"
 UNIT = "evals/s"
 
@@ -39,7 +49,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=500)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--config", default="cfg1", choices=["cfg0", "cfg1", "cfg2", "cfg3", "ref16k"])
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-gpu"])
+    ap.add_argument("--route", default="F", choices=["F", "B1", "v8", "v8+"],
+                    help="route of --impl reference-gpu")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="only W warm-up and K timed steps (for ncu launch lists); prints a short line")
@@ -187,12 +199,121 @@ def kernel_times(ev, params, out, steps, stream, torch):
             for k, v in per.items()}
 
 
+def reference_gpu_arm(args, cfg, local):
+    """One of the reference's GPU routes, CUDA-graph replayed on this GPU (rank 0 only)."""
+    import torch
+    from baseline.reference_routes import CapturedRoute, ReferenceKernels, available
+    from flashns_b200.evaluator import PackedEvaluator, flat_parameters
+    from flashns_b200.ns_seed import NSLoss
+    from flashns_b200.problems import CONFIGS, config_options, config_parameters, config_points
+
+    base = {"impl": "reference-gpu", "route": args.route}
+    if args.config != "ref16k":
+        return dict(base, unavailable="the reference's GPU routes implement the (u, v, p) head without boundary "
+                                      "targets on dense routes; run --config ref16k")
+    if not available():
+        return dict(base, unavailable="reference kernels not built (python baseline/build_reference_gpu.py with "
+                                      "FLASHNS_REFERENCE set)")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    kernels = ReferenceKernels()
+    pts = config_points(args.config)
+    head, order, gamma = config_options(args.config)
+    ws_host, bs_host = config_parameters(args.config)
+    dev = lambda t: t.to(device).contiguous()
+    x, pw, bw, target = dev(pts.x), dev(pts.pde_weights), dev(pts.boundary_weights), dev(pts.target)
+    ws, bs = [dev(w) for w in ws_host], [dev(b) for b in bs_host]
+    route = CapturedRoute(args.route, x, pts.interior_count, pw, bw, target, ws, bs, kernels,
+                          nu=pts.viscosity, gamma=gamma)
+    stream = torch.cuda.current_stream(device)
+
+    sampler = ClockSampler(local, "/tmp/flashns_clocks_reference.csv")
+    t_end = time.perf_counter() + 1.0
+    while time.perf_counter() < t_end:
+        for _ in range(20):
+            route.replay()
+        torch.cuda.synchronize()
+    for _ in range(max(args.warmup, 3)):
+        route.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        route.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_step = e0.elapsed_time(e1) / args.steps
+    clocks = sampler.stop()
+
+    # end to end as in our arm: pinned host inputs copied into the graph's static inputs,
+    # one replay, the loss and gradient read back, a synchronize
+    statics = [x] + ws + bs
+    hosts = [t.cpu().pin_memory() for t in statics]
+    outs = [route.loss] + list(route.grads)
+    hout = [t.cpu().pin_memory() for t in outs]
+    h2d = sum(t.numel() * 8 for t in hosts)
+    d2h = sum(t.numel() * 8 for t in hout)
+
+    def e2e_step():
+        for d, h in zip(statics, hosts):
+            d.copy_(h, non_blocking=True)
+        route.refresh()
+        route.replay()
+        for h, d in zip(hout, outs):
+            h.copy_(d, non_blocking=True)
+        stream.synchronize()
+
+    e2e_steps = max(1, min(args.steps, 200))
+    for _ in range(3):
+        e2e_step()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+
+    # agreement with this library's fused evaluation on the same inputs (not timed)
+    loss, grads = route.replay()
+    got = torch.cat([g.reshape(-1) for g in grads] + [loss.reshape(1)]).cpu()
+    ev = PackedEvaluator(x, pts.interior_count, pw, bw, target, CONFIGS[args.config]["widths"], head=head,
+                         boundary_order=order, loss=NSLoss(viscosity=pts.viscosity, gradient_weight=gamma,
+                                                           boundary_weight=5.0), device=device)
+    ours = ev(flat_parameters(ws_host, bs_host).to(device)).cpu()
+    ratio = float(((got - ours).abs() / (2e-12 + 2e-11 * ours.abs())).max())
+    rel = float((got - ours).norm() / ours.norm())
+
+    value = 1e3 / ms_step
+    published = REFERENCE_ROUTE_PUBLISHED_MS.get(args.route)
+    libs = kernels.build["libraries"]
+    return dict(base, **{
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": value / (1e3 / published) if published else None, "dtype": "f64",
+        "data": "synthetic (the reference benchmark's recipe, as in --impl ours --config ref16k)",
+        "config": dict(cfg, parallelism="single"),
+        "e2e": {"value": 1e3 / e2e_ms, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "kernels_from": {k: {"sources": sorted(v["sources"]), "sha256": v["sha256"][:16]} for k, v in libs.items()},
+        "cutlass": kernels.build.get("cutlass"),
+        "agreement_with_flashns_b200": {"max_error_over_tolerance": ratio, "relative_l2": rel,
+                                        "tolerance": "|a-b| <= 2e-12 + 2e-11|b|"},
+        "clocks": clocks,
+        "baseline_note": (f"vs_baseline: this route's published H100 time, {published} ms "
+                          "(docs/cuda-h100-results.md:54-64)" if published else "no published time for this route"),
+    })
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     cfg = workload(args.config)
+
+    if args.impl == "reference-gpu":
+        if rank == 0:
+            print(json.dumps(reference_gpu_arm(args, cfg, local)), flush=True)
+        return
 
     if args.impl == "reference":
         if rank != 0:
