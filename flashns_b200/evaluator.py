@@ -111,7 +111,8 @@ class PackedEvaluator:
             to = lambda t: t.detach().to(device=device, dtype=torch.float64).contiguous()
             self.x, self.pde_weights = to(x), to(pde_weights)
             self.boundary_weights, self.target = to(boundary_weights), to(target)
-            self.workspace = torch.empty(max(1, self.plan.workspace_bytes // 8), dtype=torch.float64, device=device)
+            self.workspace = torch.empty(max(1, (self.plan.workspace_bytes + 7) // 8), dtype=torch.float64,
+                                         device=device)
         self.parameters = self.plan.parameters
         self.launches_per_call = self.plan.launches
 
@@ -206,7 +207,8 @@ class FieldEvaluator:
         with torch.cuda.device(device):
             self.plan = Plan(x.shape[1], head, boundary_order, self.widths, 0, len(x), NSLoss())
             self.x = x.detach().to(device).contiguous()
-            self.workspace = torch.empty(max(1, self.plan.workspace_bytes // 8), dtype=torch.float64, device=device)
+            self.workspace = torch.empty(max(1, (self.plan.workspace_bytes + 7) // 8), dtype=torch.float64,
+                                         device=device)
         self.width = target_width(head, boundary_order)
         self.parameters = self.plan.parameters
 
@@ -215,11 +217,15 @@ class FieldEvaluator:
             raise ValueError(f"flat FP64 parameters [{self.parameters}] on {self.device} required")
         if out is None:
             out = torch.empty((len(self.x), self.width), dtype=torch.float64, device=self.device)
+        elif out.shape != (len(self.x), self.width) or out.dtype != torch.float64 or out.device != self.device \
+                or not out.is_contiguous():
+            raise ValueError(f"out must be a contiguous FP64 [{len(self.x)}, {self.width}] tensor on the device")
+        flat = flat.contiguous()
         lib = self.plan._lib
         with torch.cuda.device(self.device):
             stream = torch.cuda.current_stream()
             status = lib.flashns_b200_fields(self.plan.handle, ctypes.c_void_p(self.x.data_ptr()),
-                                             ctypes.c_void_p(flat.contiguous().data_ptr()),
+                                             ctypes.c_void_p(flat.data_ptr()),
                                              ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(self.workspace.data_ptr()),
                                              self.workspace.numel() * 8, ctypes.c_void_p(stream.cuda_stream))
         _lib.check(status, "flashns_b200_fields")

@@ -99,3 +99,20 @@ def test_field_output_guards(cuda, dim, order):
     assert np.isfinite(got.cpu().numpy()).all()
     np.testing.assert_array_equal(got.cpu().numpy(), expected)
     assert guards_intact(buf, n)
+
+
+def test_field_evaluator_rejects_a_wrong_output_buffer(cuda):
+    """A caller-supplied fields buffer of the wrong shape, dtype or layout is refused
+    before anything is launched (the kernel writes points x F values)."""
+    from flashns_b200.evaluator import FieldEvaluator, flat_parameters, xavier_normal
+
+    widths = [2, 64, 64, 2]
+    x = torch.rand(50, 2, generator=torch.Generator(device="cpu").manual_seed(5), dtype=torch.float64)
+    fe = FieldEvaluator(x, widths, head="psi", boundary_order=1, device=cuda)
+    p = flat_parameters(*xavier_normal(widths, 1)).to(cuda)
+    for bad in (torch.empty(49, 3, dtype=torch.float64, device=cuda),
+                torch.empty(50, 2, dtype=torch.float64, device=cuda),
+                torch.empty(50, 3, dtype=torch.float32, device=cuda),
+                torch.empty(3, 50, dtype=torch.float64, device=cuda).T):
+        with pytest.raises(ValueError):
+            fe(p, bad)
