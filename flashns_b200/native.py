@@ -157,7 +157,7 @@ class NativeCUDA:
     def seed(self, jets, boundary, pde_weights, boundary_weights, target, loss):
         ni, nb = len(jets), len(boundary)
         for t in (jets, boundary, pde_weights, boundary_weights, target):
-            if not t.is_cuda or t.dtype != torch.float64:
+            if not t.is_cuda or t.dtype != torch.float64 or t.device != jets.device:
                 raise ValueError("same-device CUDA FP64 tensors required")
         if jets.shape != (ni, 10, 3) or boundary.shape != (nb, 3) or boundary.stride(-1) != 1:
             raise ValueError("2-D Q10 interior and contiguous-channel boundary fields required")
