@@ -93,3 +93,56 @@ def test_hopper_plan_names_reject_bad_arguments(library):
         assert lib.flashns_hopper_launch(None, 3, False, None, None, p16, None) == 1
     finally:
         lib.flashns_hopper_destroy(plan)
+
+
+def test_hook_entry_points_check_arguments_before_any_launch(library):
+    """The reference's hook ABI (experiments/pinn_v8/native.cu:47-62,97-107,
+    experiments/cuda_jet_h100/stable_kernels.cu:82-131, stable_dgrad.cu:150-174): invalid
+    sizes and missing or aliased buffers return cudaErrorInvalidValue (1), and empty inputs
+    return success, before anything is launched -- so this runs on a CPU host.  The
+    pointers are never dereferenced."""
+    from flashns_b200 import _lib
+    lib = _lib.library()
+    p, q, r = ctypes.c_void_p(4096), ctypes.c_void_p(1 << 20), ctypes.c_void_p(1 << 24)
+    big = 1 << 62
+    act = lib.flashns_v8_activation
+    assert act(4, 0, p, None, None, q, r, 3, 2, 8, None) == 1           # dimension
+    assert act(2, 2, p, None, None, q, r, 3, 2, 8, None) == 1           # backward flag
+    assert act(2, 0, p, None, None, q, r, -1, 2, 8, None) == 1          # negative points
+    assert act(2, 0, p, None, None, q, r, 3, 2, 0, None) == 1           # no channels
+    assert act(2, 0, p, None, None, q, r, big, 0, 8, None) == 1         # rows overflow
+    assert act(2, 0, None, None, None, q, r, 3, 2, 8, None) == 1        # no input
+    assert act(2, 1, p, None, p, q, None, 3, 2, 8, None) == 1           # VJP without a1
+    assert act(3, 1, None, None, None, None, None, 0, 0, 8, None) == 0  # empty: success
+    for fn in (lib.flashns_v8_coordinate_affine,):
+        assert fn(2, p, q, r, p, 3, 2, 0, None) == 1
+        assert fn(2, p, q, None, p, 3, 2, 8, None) == 1                 # no bias
+        assert fn(2, None, None, None, None, 0, 0, 8, None) == 0
+    assert lib.flashns_v8_coordinate_affine_activation(2, p, q, r, p, None, 3, 2, 8, None) == 1  # no a1 out
+    tail = lib.flashns_v8_tail3
+    assert tail(2, 2, p, q, r, p, q, 3, 2, 8, None) == 1                # fused flag
+    assert tail(2, 1, p, q, None, p, q, 3, 2, 8, None) == 1             # fused without H
+    assert tail(2, 0, None, None, None, None, None, 0, 0, 8, None) == 0
+    wg = lib.flashns_v8_coordinate_wgrad
+    assert wg(2, p, q, r, None, p, 3, 2, 8, None) == 1                  # no dW
+    assert wg(2, p, None, r, q, p, 3, 2, 8, None) == 1                  # no coordinates
+    assert wg(5, p, q, r, q, p, 3, 2, 8, None) == 1
+    assert lib.flashns_v8_coordinate_activation_wgrad(2, p, None, p, q, r, q, p, 3, 2, 8, None) == 1  # no a1
+    seed = lib.flashns_v8_loss_seed
+    assert seed(p, p, p, p, p, q, q, r, 4, 2, 2, 0.07, 0.2, 5.0, None) == 1   # boundary stride < 3
+    assert seed(p, p, p, p, p, q, q, r, -1, 2, 3, 0.07, 0.2, 5.0, None) == 1
+    assert seed(p, p, p, p, p, q, q, None, 4, 2, 3, 0.07, 0.2, 5.0, None) == 1  # no loss partials
+    assert seed(p, None, p, p, p, q, q, r, 4, 2, 3, 0.07, 0.2, 5.0, None) == 1  # boundary missing
+    assert seed(None, None, None, None, None, None, None, None, 0, 0, 3, 0.07, 0.2, 5.0, None) == 0
+    sa = lib.flashns_stable_activation
+    assert sa(1, False, p, None, None, q, r, 4, 8, None) == 1
+    assert sa(2, False, p, None, None, p, r, 4, 8, None) == 1           # output aliases input
+    assert sa(2, True, p, q, r, p, None, 4, 8, None) == 1               # output aliases H
+    assert sa(2, False, p, None, None, q, None, 4, 8, None) == 1        # no a1 out
+    assert sa(3, False, None, None, None, None, None, 0, 8, None) == 0
+    dg = lib.flashns_stable_dgrad_vjp
+    assert dg(2, False, p, q, None, None, r, -1, 8, 8, None) == 1
+    assert dg(2, False, p, q, None, None, r, 4, 0, 8, None) == 1        # cout 0
+    assert dg(2, True, p, q, None, None, r, 4, 8, 8, None) == 1         # fused without H, a1
+    assert dg(2, False, p, q, None, None, p, 4, 8, 8, None) == 1        # output aliases D
+    assert dg(2, False, None, None, None, None, None, 0, 8, 8, None) == 0
