@@ -3050,6 +3050,9 @@ int flashns_b200_plan_create(int dim, int head, int boundary_order, int n_affine
   p->ni = interior_points; p->nb = boundary_points;
   p->rows = interior_points * q + boundary_points * qb;
   p->points = interior_points + boundary_points;
+  // the kernels address tile rows with 32-bit TMA coordinates; far more rows than a
+  // 180 GB device can hold checkpoints for, refused here rather than mis-addressed
+  if (p->rows > INT32_MAX) { delete p; return int(cudaErrorInvalidValue); }
   p->geo = Geometry{p->ni, p->nb, p->rows};
   if (cudaGetDevice(&p->device) != cudaSuccess ||
       cudaDeviceGetAttribute(&p->sms, cudaDevAttrMultiProcessorCount, p->device) != cudaSuccess) {

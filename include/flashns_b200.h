@@ -35,6 +35,8 @@ typedef struct flashns_b200_plan flashns_b200_plan;
  *                   src/flashns/jet_packed.py:12-41); 1: first-order rows (psi head:
  *                   boundary targets are (u, v, p))
  *   widths          n_affine+1 entries: dim, hidden widths (1..128), outputs (3 uvp / 2 psi)
+ *   interior_points, boundary_points: the packed rows (interior x Q + boundary x (1 or dim+1))
+ *                   must not exceed 2^31 - 1
  *   viscosity, gradient_weight, boundary_weight: NSLoss (src/flashns/ns_seed.py:13-23) */
 int flashns_b200_plan_create(int dim, int head, int boundary_order, int n_affine, const int* widths,
                              int64_t interior_points, int64_t boundary_points, double viscosity,

@@ -61,6 +61,12 @@ def test_plan_rejects_invalid_arguments_without_a_gpu(library):
                                               ctypes.byref(handle))
         assert status == 1, (dim, head, order, widths, status)  # cudaErrorInvalidValue
         assert not handle.value
+    # more packed rows than 32-bit tile coordinates address: 2^28 2-D interior points are
+    # 2.7e9 rows; (2^31 - 1) / 10 points with one value point is one row too many
+    arr = (ctypes.c_int * 3)(2, 64, 2)
+    for ni, nb in ((1 << 28, 0), ((2**31 - 1) // 10, 8), (0, 2**31)):
+        status = lib.flashns_b200_plan_create(2, 1, 0, 2, arr, ni, nb, 0.05, 0.2, 5.0, ctypes.byref(handle))
+        assert status == 1 and not handle.value, (ni, nb)
 
 
 def test_no_fallback_when_library_missing(tmp_path, monkeypatch):
