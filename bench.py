@@ -332,7 +332,7 @@ def main():
     import torch.distributed as dist
     from datetime import timedelta
     from flashns_b200.costs import checkpoint_bytes, evaluation_costs
-    from flashns_b200.evaluator import PackedEvaluator, flat_parameters, xavier_normal
+    from flashns_b200.evaluator import PackedEvaluator, flat_parameters
     from flashns_b200.ns_seed import NSLoss
     from flashns_b200.problems import CONFIGS, config_options, config_parameters, config_points
 
