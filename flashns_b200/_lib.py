@@ -26,6 +26,7 @@ SIGNATURES = {
                                  _c_ptr, _c_int, ctypes.POINTER(_c_int)],
     "flashns_b200_plan_launch_kinds": [_c_ptr, ctypes.POINTER(_c_int), _c_int, ctypes.POINTER(_c_int)],
     "flashns_b200_fp64_peak_probe": [_c_int, _c_int, _c_ptr, ctypes.POINTER(_c_dbl), _c_ptr],
+    "flashns_b200_fp64_probe": [_c_int, _c_int, _c_int, _c_int, _c_ptr, ctypes.POINTER(_c_dbl), _c_ptr],
     "flashns_b200_eval_static": [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr],
     "flashns_b200_fields": [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_ptr],
     "flashns_b200_row_dots": [_c_ptr, _c_i64, _c_int, _c_ptr, _c_ptr, _c_i64, _c_ptr],

@@ -122,6 +122,21 @@ int flashns_b200_eval_static(const flashns_b200_plan* plan, const double* coordi
  * issued.  Time it with events on `stream` for the FP64 roofline denominator. */
 int flashns_b200_fp64_peak_probe(int blocks, int iters, double* sink, double* flops, cudaStream_t stream);
 
+/* The FP64 throughput of each instruction shape, for the peak table (no reference
+ * counterpart).  `blocks` CTAs of `threads` threads (a multiple of 32, at most 1024) run
+ * `iters` rounds; *flops = floating-point operations issued.  Kinds: register-only chains
+ * of 8 MMAs per warp for each f64 shape (M16N8K8 is flashns_b200_fp64_peak_probe and needs
+ * 256 threads), 16 DFMA chains per thread, or SMEM: m16n8k8 fed from shared memory in the
+ * kernels' tile shape (one m16 and five n8 tiles per warp, a 32-deep K slice per round). */
+#define FLASHNS_B200_PROBE_M16N8K8 0
+#define FLASHNS_B200_PROBE_M8N8K4 1
+#define FLASHNS_B200_PROBE_M16N8K4 2
+#define FLASHNS_B200_PROBE_M16N8K16 3
+#define FLASHNS_B200_PROBE_DFMA 4
+#define FLASHNS_B200_PROBE_SMEM 5
+int flashns_b200_fp64_probe(int kind, int blocks, int threads, int iters, double* sink, double* flops,
+                            cudaStream_t stream);
+
 /* ---------------------------------------------------------------------------------------
  * Per-stage hooks with the reference's C ABI (same names, argument order and meaning,
  * caller-provided scratch), so the reference's ctypes bindings can load this library.

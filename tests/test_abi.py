@@ -152,3 +152,19 @@ def test_hook_entry_points_check_arguments_before_any_launch(library):
     assert dg(2, True, p, q, None, None, r, 4, 8, 8, None) == 1         # fused without H, a1
     assert dg(2, False, p, q, None, None, p, 4, 8, 8, None) == 1        # output aliases D
     assert dg(2, False, None, None, None, None, None, 0, 8, 8, None) == 0
+
+
+def test_fp64_probe_rejects_bad_launch_shapes(library):
+    """The peak-table probe checks its kind and launch shape before launching."""
+    from flashns_b200 import _lib
+    from flashns_b200.peak import KINDS
+    lib = _lib.library()
+    sink, flops = ctypes.c_void_p(4096), ctypes.c_double()
+    probe = lambda kind, blocks, threads, iters, s=sink: lib.flashns_b200_fp64_probe(kind, blocks, threads, iters, s,
+                                                                                      ctypes.byref(flops), None)
+    assert sorted(KINDS.values()) == list(range(6))
+    assert probe(6, 148, 256, 10) == 1 and probe(-1, 148, 256, 10) == 1
+    assert probe(1, 148, 100, 10) == 1 and probe(1, 148, 2048, 10) == 1     # threads
+    assert probe(0, 148, 512, 10) == 1                                      # m16n8k8 runs at 256 threads
+    assert probe(2, 0, 256, 10) == 1 and probe(2, 148, 256, 0) == 1
+    assert probe(5, 148, 256, 10, None) == 1
