@@ -111,3 +111,29 @@ def test_kovasznay_and_tgv_fields_solve_the_equations():
     assert float(ru.detach().abs().max()) < 1e-12 and float(rv.detach().abs().max()) < 1e-12
     expect_u = 1 - torch.exp(lam * x[:, 0]) * torch.cos(2 * math.pi * x[:, 1])
     assert float((u - expect_u).detach().abs().max()) < 1e-13
+
+
+@pytest.mark.parametrize("dim", [2, 3])
+def test_oracle_tanh_jet_tails_vs_100_digit_reference(dim):
+    """Saturated centers up to 350: every jet coefficient of the oracle's stable tanh
+    matches 100-digit mpmath (criterion of the reference's tests/test_jet_stable.py:28-42)."""
+    from oracle import jets as J
+    from tests.tails import expected_jets, input_jets, within_tail_tolerance
+    h, a1 = J.tanh_jet(input_jets(dim), dim)
+    ok = within_tail_tolerance(h, expected_jets(dim))
+    assert ok.all(), np.argwhere(~ok)
+
+
+@pytest.mark.parametrize("center", [0.0, 5.0, 20.0, -20.0, 100.0, 350.0])
+def test_stable_tanh_nested_derivatives_vs_100_digit_reference(center):
+    """flashns_b200.jet_stable.stable_tanh: four nested autograd derivatives against mpmath
+    (the reference's tests/test_jet_stable.py:28-42 on this library's helper)."""
+    import torch
+
+    from flashns_b200.jet_stable import stable_tanh
+    from tests.tails import tanh_derivative, within_tail_tolerance
+    x = torch.tensor(center, dtype=torch.float64, requires_grad=True)
+    derivative = stable_tanh(x)
+    for order in range(1, 5):
+        (derivative,) = torch.autograd.grad(derivative, x, create_graph=True)
+        assert within_tail_tolerance(float(derivative.detach()), tanh_derivative(center, order)), (center, order)
