@@ -290,7 +290,8 @@ __global__ void __launch_bounds__(kHookThreads)
 
 // ---------------------------------------------------------------- coordinate wgrad
 // Stage 1: partials[tile][c][0..DIM-1] = sum over the tile's 8 points of
-// D[row0][c] x[a] + D[unit(a)][c] (full points), partials[tile][c][DIM] = sum D[row0][c].
+// D[row0][c] x[a] + D[unit(a)][c] (full points; every other slot enters multiplied by its
+// structural zero), partials[tile][c][DIM] = sum D[row0][c].
 // ACT first applies the jet VJP (bar_Z from H, a1, bar_H).  Stage 2 reduces the tiles of
 // each channel in a fixed order.  Layout of `partials` as the reference's binding
 // allocates it: [(points+7)/8][C][DIM+1] (experiments/pinn_v8/native.py:146).
@@ -328,13 +329,20 @@ __global__ void __launch_bounds__(kHookThreads)
           }
           vjp_full<DIM>(hv, aux[p * channels + c], hb, zb);
         } else {
-          zb[0] = dz_or_h[base];
 #pragma unroll
-          for (int a = 0; a < DIM; ++a) zb[unit_row<DIM>(a)] = dz_or_h[base + int64_t(unit_row<DIM>(a)) * channels];
+          for (int s = 0; s < Q; ++s) zb[s] = dz_or_h[base + int64_t(s) * channels];
         }
         acc[DIM] += zb[0];
+        // the dense contraction bar_Z^T X of the coordinate jets, structural zeros included:
+        // a NaN or Inf in any slot reaches dW as it does through 0 * NaN in a GEMM (the
+        // reference's experiments/pinn_v8/coordinate_wgrad.cuh:19-31 keeps the same terms)
 #pragma unroll
-        for (int a = 0; a < DIM; ++a) acc[a] += zb[0] * xp[a] + zb[unit_row<DIM>(a)];
+        for (int a = 0; a < DIM; ++a) {
+          double v = zb[0] * xp[a];
+#pragma unroll
+          for (int s = 1; s < Q; ++s) v += zb[s] * (s == unit_row<DIM>(a) ? 1.0 : 0.0);
+          acc[a] += v;
+        }
       } else {
         const int64_t r = (full * Q + (p - full)) * channels + c;
         const double z0 = ACT ? hbar[r] * aux[p * channels + c] : dz_or_h[r];
