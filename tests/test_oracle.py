@@ -137,3 +137,26 @@ def test_stable_tanh_nested_derivatives_vs_100_digit_reference(center):
     for order in range(1, 5):
         (derivative,) = torch.autograd.grad(derivative, x, create_graph=True)
         assert within_tail_tolerance(float(derivative.detach()), tanh_derivative(center, order)), (center, order)
+
+
+def test_oracle_fourth_derivative_vjp_vs_100_digit_reference():
+    """The VJP of the x^3 coefficient at z0 needs tanh'''' (the reference's
+    sources/flashns_v8_reference/tests/verify_math.py:127-139)."""
+    from oracle import jets as J
+    from tests.tails import fourth_derivative_case
+    z, seed, expected = fourth_derivative_case()
+    h, a1 = J.tanh_jet(z, 2)
+    got = J.tanh_vjp(h, a1, seed, 2)[:, 0, 0]
+    assert np.all(np.abs(got - expected) <= 1e-30 + 2e-12 * np.abs(expected)), (got, expected)
+
+
+def test_oracle_a1_tails_vs_420_digit_reference():
+    """a1 = sech^2 z0 from r = exp(-|z0|) into the subnormal range, and the information it
+    keeps where tanh rounds to 1 (verify_math.py:181-209)."""
+    from oracle import jets as J
+    from tests.tails import A1_PROBES, a1_tail_ok
+    for z in A1_PROBES:
+        for s in (1.0, -1.0):
+            assert a1_tail_ok(J.stable_a1(np.array(s * z)), s * z), s * z
+    assert np.tanh(20.0) == np.tanh(21.0) == 1.0
+    assert J.stable_a1(np.array(20.0)) != J.stable_a1(np.array(21.0))
