@@ -55,7 +55,10 @@ class PackedPINN:
             raise ValueError("boundary target shape/dtype/device mismatch")
         if not bool(torch.isfinite(x).all()) or not bool(torch.isfinite(target).all()):
             raise ValueError("finite coordinates and targets required")
-        self.x = x.detach().contiguous()
+        # the point set is fixed at construction, as the reference's packed inputs are
+        # (pinn_packed.py:60-66): a later in-place change of `x` does not reach this object;
+        # weights and targets are kept by reference, as there
+        self.x = x.detach().clone(memory_format=torch.contiguous_format)
         self.pde_weights = pde_weights.detach().contiguous()
         self.boundary_weights = boundary_weights.detach().contiguous()
         self.target = target.detach().contiguous()
