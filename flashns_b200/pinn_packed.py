@@ -7,19 +7,46 @@ evaluation (``flashns_b200_eval``) on the current CUDA stream.  Every ``layout``
 objective; all of them evaluate through the compact fused kernels.  The stage hooks
 (``activation_factory``, ``cuda_seed``, ``tail_dgrad_vjp``, ``coordinate_*``,
 ``first_*``) are accepted for compatibility -- the fused kernels already contain every
-stage they replace -- and recorded in ``metadata``.
+stage they replace -- and recorded in ``metadata``.  None of them is called; a hook that
+is not this library's own (``foreign_hooks``) draws a ``UserWarning`` so that a
+caller-defined stage or residual cannot be dropped silently.
 
 Extensions: ``head="psi"`` (stream-function net, outputs (psi, p)), 3-D coordinates
 (x, y, t) for the psi head, and ``boundary_order=1`` (first-order boundary rows with
 (u, v, p) targets).
 """
 
+import warnings
 from contextlib import nullcontext
 
 import torch
 
 from flashns_b200.evaluator import PackedEvaluator, output_width, target_width
 from flashns_b200.ns_seed import NSLoss, validate_weights
+
+HOOKS = ("activation_factory", "cuda_seed", "residual_reference", "tail_dgrad_vjp", "coordinate_affine",
+         "first_affine_activation", "coordinate_wgrad", "first_activation_wgrad")
+
+
+def foreign_hooks(**hooks):
+    """Names of the supplied stage hooks that are not this library's own.
+
+    The fused kernels contain every stage a hook replaces, so this library's hooks
+    (``TensorActivation`` and the methods of ``flashns_b200.native.NativeCUDA`` /
+    ``Native``) change nothing.  Any other callable -- the reference's own equivalent
+    hooks included -- is not called either; ``PackedPINN`` warns about those, because a
+    caller-defined stage or residual would silently not take effect."""
+    from flashns_b200.jet_packed import TensorActivation
+    from flashns_b200.native import Native, NativeCUDA
+    from flashns_b200.ns_seed import per_point_loss
+    foreign = []
+    for name, hook in hooks.items():
+        if hook is None or hook is TensorActivation or hook is per_point_loss:
+            continue
+        if isinstance(getattr(hook, "__self__", None), (NativeCUDA, Native)):
+            continue
+        foreign.append(name)
+    return foreign
 
 
 class PackedPINN:
@@ -80,6 +107,18 @@ class PackedPINN:
             "coordinate_wgrad_enabled": coordinate_wgrad is not None,
             "first_activation_wgrad_enabled": first_activation_wgrad is not None,
         }
+        # the reference calls residual_reference only for seed="autograd" and cuda_seed
+        # only for seed="cuda" (src/flashns/pinn_packed.py:136-146)
+        ignored = foreign_hooks(
+            activation_factory=activation_factory, cuda_seed=cuda_seed if seed == "cuda" else None,
+            residual_reference=residual_reference if seed == "autograd" else None, tail_dgrad_vjp=tail_dgrad_vjp,
+            coordinate_affine=coordinate_affine, first_affine_activation=first_affine_activation,
+            coordinate_wgrad=coordinate_wgrad, first_activation_wgrad=first_activation_wgrad)
+        self.metadata["hooks_not_called"] = ignored
+        if ignored:
+            warnings.warn(f"flashns_b200 PackedPINN evaluates every stage in its fused kernels; the supplied "
+                          f"{', '.join(ignored)} hook(s) are not called (the objective is NSLoss's)",
+                          stacklevel=2)
 
     def region(self, name):
         return torch.profiler.record_function("flashns_b200::" + name) if self.trace else nullcontext()

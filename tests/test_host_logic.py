@@ -167,3 +167,28 @@ def test_jet_multiply_and_manifest():
     m = jet_stable.manifest(2, "a" * 64)
     assert m["activation_aux_state"]["strategy"] == "stable_aux_a1" and m["q"] == 10
     assert jet_packed.stable_a1 is jet_stable.stable_a1
+
+
+def test_foreign_stage_hooks_are_named():
+    """PackedPINN calls no stage hook (its fused kernels contain the stages); this
+    library's own hooks are recognized, any other callable is reported so the drop-in
+    can warn instead of dropping a caller-defined stage silently."""
+    from flashns_b200.jet_packed import TensorActivation
+    from flashns_b200.native import Native, NativeCUDA
+    from flashns_b200.ns_seed import per_point_loss
+    from flashns_b200.pinn_packed import HOOKS, foreign_hooks
+    from flashns_b200 import _lib
+    if not _lib.LIBRARY.exists():
+        pytest.skip("library not built")
+    nat, dense = NativeCUDA(), Native()
+    own = dict(activation_factory=nat.activation_factory, cuda_seed=nat.seed, residual_reference=per_point_loss,
+               tail_dgrad_vjp=nat.tail_dgrad_vjp, coordinate_affine=nat.coordinate_affine,
+               first_affine_activation=nat.coordinate_affine_activation, coordinate_wgrad=nat.coordinate_wgrad,
+               first_activation_wgrad=nat.coordinate_activation_wgrad)
+    assert set(own) == set(HOOKS)
+    assert foreign_hooks(**own) == []
+    assert foreign_hooks(activation_factory=TensorActivation, coordinate_wgrad=None) == []
+    assert foreign_hooks(activation_factory=dense.forward) == []
+    mine = lambda *a, **k: None
+    assert foreign_hooks(activation_factory=TensorActivation, coordinate_affine=mine, cuda_seed=mine) == [
+        "coordinate_affine", "cuda_seed"]

@@ -29,3 +29,23 @@ def test_point_set_fixed_at_construction(cuda):
         with torch.no_grad():
             for p, g in zip(ws + bs, grads_a):
                 p.add_(g, alpha=-1e-3)
+
+
+def test_caller_defined_hooks_draw_a_warning(cuda):
+    """A stage hook that is not this library's own is not called by the fused drop-in;
+    construction says so instead of dropping it silently.  Its own hooks stay quiet."""
+    import warnings
+
+    from flashns_b200.native import NativeCUDA
+    from flashns_b200.pinn_packed import PackedPINN
+    c = random_case(5, 2, [2, 6, 3], seed=3)
+    t = lambda a: torch.tensor(np.asarray(a), dtype=torch.float64, device=cuda)
+    args = (t(c["x"]), 5, t(c["pw"]), t(c["bw"]), t(c["target"]))
+    with pytest.warns(UserWarning, match="coordinate_affine"):
+        step = PackedPINN(*args, coordinate_affine=lambda *a: None)
+    assert step.metadata["hooks_not_called"] == ["coordinate_affine"]
+    nat = NativeCUDA()
+    with warnings.catch_warnings():
+        warnings.simplefilter("error")
+        PackedPINN(*args, seed="cuda", activation_factory=nat.activation_factory, cuda_seed=nat.seed,
+                   tail_dgrad_vjp=nat.tail_dgrad_vjp)
