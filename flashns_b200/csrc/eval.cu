@@ -3252,12 +3252,20 @@ int flashns_b200_plan_launch_count(const flashns_b200_plan* plan, int* count) {
   return flashns_b200_plan_launch_kinds(plan, nullptr, 0, count);
 }
 
+// A plan's grids and buffers belong to the device that was current when it was created;
+// launching it with another device current would hand that device foreign pointers.
+static bool on_plan_device(const flashns_b200_plan* p) {
+  int device = -1;
+  return cudaGetDevice(&device) == cudaSuccess && device == p->device;
+}
+
 static int run_eval(const flashns_b200_plan* p, const double* coordinates, const double* parameters,
                     const double* pde_weights, const double* boundary_weights, const double* target,
                     double* gradient_and_loss, void* workspace, size_t workspace_bytes, cudaStream_t stream,
                     cudaEvent_t* events, int capacity, int* recorded) {
   if (!p || !parameters || !gradient_and_loss || !workspace) return int(cudaErrorInvalidValue);
   if (workspace_bytes < size_t(p->workspace_doubles) * sizeof(double)) return int(cudaErrorInvalidValue);
+  if (!on_plan_device(p)) return int(cudaErrorInvalidDevice);
   if (p->points && !coordinates) return int(cudaErrorInvalidValue);
   if (p->ni && !pde_weights) return int(cudaErrorInvalidValue);
   if (p->nb && (!boundary_weights || !target)) return int(cudaErrorInvalidValue);
@@ -3511,6 +3519,7 @@ extern "C" int flashns_b200_fields(const flashns_b200_plan* p, const double* coo
                                    double* fields, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   if (!p || !parameters || !fields || !workspace || p->ni != 0) return int(cudaErrorInvalidValue);
   if (workspace_bytes < size_t(p->workspace_doubles) * sizeof(double)) return int(cudaErrorInvalidValue);
+  if (!on_plan_device(p)) return int(cudaErrorInvalidDevice);
   if ((reinterpret_cast<uintptr_t>(workspace) & 15) != 0) return int(cudaErrorInvalidValue);
   if (p->points == 0) return int(cudaSuccess);
   if (!coordinates) return int(cudaErrorInvalidValue);

@@ -74,7 +74,8 @@ int flashns_b200_wait_selftest(unsigned spins, int* gave_up, cudaStream_t stream
 /* One complete loss + parameter-gradient evaluation.  Replaces
  * PackedPINN.__call__(weights, biases) -> (loss, [dW_0..dW_L, db_0..db_L])
  * (src/flashns/pinn_packed.py:93-191) together with the Engine's flattening
- * (experiments/pinn_v8/runtime.py:114-117).
+ * (experiments/pinn_v8/runtime.py:114-117).  The device current at the call must be the
+ * one the plan was created on (cudaErrorInvalidDevice otherwise, nothing launched).
  *   coordinates       [interior + boundary, dim]   interior points first
  *   parameters        [P]  flat [W_0 .. W_L (row-major [out, in]), b_0 .. b_L]
  *   pde_weights       [interior]                   globally normalized
