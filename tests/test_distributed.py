@@ -102,3 +102,54 @@ def test_shards_partition_points_and_weights():
         assert abs(sum(float(s.pde_weights.sum()) for s in shards) - float(pts.pde_weights.sum())) < 1e-14
         xs = torch.cat([s.x[:s.interior_count] for s in shards])
         assert torch.equal(xs, pts.x[:101])
+
+
+def _leaving_worker(rank, world, port, widths, params, queue):
+    """Rank 1 dies between evaluations without a word to the group; rank 0's next
+    evaluation must end with an error (peer gone or the group's timeout), not hang."""
+    import time
+    from datetime import timedelta
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+    from flashns_b200.distributed import DistributedEvaluator
+    from flashns_b200.problems import kovasznay
+    ev = DistributedEvaluator(kovasznay(37, 13, seed=4), widths, local_factory=_oracle_factory(widths, params))
+    ev(torch.tensor(params))  # one evaluation together
+    if rank == 1:
+        queue.put((rank, "left", 0.0))
+        queue.close()
+        queue.join_thread()
+        os._exit(3)
+    t0 = time.monotonic()
+    try:
+        ev(torch.tensor(params))
+        outcome = "no error"
+    except Exception:  # noqa: BLE001 -- any error of the broken collective is the expected outcome
+        outcome = "error"
+    queue.put((rank, outcome, time.monotonic() - t0))
+    queue.close()
+    queue.join_thread()
+    os._exit(0)  # the group is broken: skip its teardown
+
+
+def test_a_rank_that_leaves_ends_the_others_evaluation_with_an_error():
+    from flashns_b200.evaluator import flat_parameters, xavier_normal
+    widths = [2, 8, 2]
+    params = flat_parameters(*xavier_normal(widths, 0)).numpy()
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaving_worker, args=(r, 2, port, widths, params, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        results = dict((r, (kind, secs)) for r, kind, secs in (queue.get(timeout=120) for _ in procs))
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    assert results[1][0] == "left" and procs[1].exitcode == 3
+    kind, secs = results[0]
+    assert kind == "error" and secs < 60 and procs[0].exitcode == 0
