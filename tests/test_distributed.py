@@ -43,14 +43,14 @@ def _oracle_factory(widths, params, poison_rank=None):
     return factory
 
 
-def _worker(rank, world, port, widths, params, expected, poison, queue):
+def _worker(rank, world, port, widths, params, expected, poison, queue, points=(37, 13)):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         from flashns_b200.distributed import DistributedEvaluator
         from flashns_b200.problems import kovasznay
-        pts = kovasznay(37, 13, seed=4)
+        pts = kovasznay(*points, seed=4)
         ev = DistributedEvaluator(pts, widths, local_factory=_oracle_factory(widths, params, poison))
         out = ev(torch.tensor(params))
         if poison is None:
@@ -62,15 +62,19 @@ def _worker(rank, world, port, widths, params, expected, poison, queue):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("poison", [None, 1])
-def test_two_rank_reduction_matches_single_process(poison):
+@pytest.mark.parametrize("poison,world,points", [(None, 2, (37, 13)), (1, 2, (37, 13)), (None, 3, (2, 1)),
+                                                 (None, 3, (17, 5))])
+def test_rank_reduction_matches_single_process(poison, world, points):
+    """World 2, with and without a NaN injected on rank 1; world 3 with an entirely empty
+    shard on rank 0 (2 + 1 points) and with uneven shards (17 + 5 points), as the
+    reference's experiments/cuda_jet_v5/distributed.py:431-442 exercises."""
     from flashns_b200.evaluator import flat_parameters, xavier_normal
     from flashns_b200.problems import kovasznay
     from oracle.evaluate import evaluate
     widths = [2, 12, 10, 2]
     ws, bs = xavier_normal(widths, 0)
     params = flat_parameters(ws, bs).numpy()
-    pts = kovasznay(37, 13, seed=4)
+    pts = kovasznay(*points, seed=4)
     loss, grads = evaluate(pts.x.numpy(), pts.interior_count, pts.pde_weights.numpy(), pts.boundary_weights.numpy(),
                            pts.target.numpy(), [w.numpy() for w in ws], [b.numpy() for b in bs], head="psi",
                            nu=pts.viscosity, boundary_order=1)
@@ -78,7 +82,8 @@ def test_two_rank_reduction_matches_single_process(poison):
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, widths, params, expected, poison, queue)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, widths, params, expected, poison, queue, points))
+             for r in range(world)]
     for p in procs:
         p.start()
     results = [queue.get(timeout=120) for _ in procs]
