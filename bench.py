@@ -71,6 +71,15 @@ def workload(config):
 
 
 # ---------------------------------------------------------------------------- CPU side
+def host_cores():
+    """CPUs this process may run on (its affinity mask, which a container's cpuset
+    narrows), not every CPU of the host."""
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
 def cpu_port_rate(config, steps, warmup, workers):
     """Oracle port of the reference CPU path on 1/8-point chunks over a process pool;
     returns (evals/s of the full set, median s/step, sample description)."""
@@ -318,7 +327,7 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        threads = os.cpu_count() or 1
+        threads = host_cores()
         rate, med, sample = cpu_port_rate(args.config, args.steps, args.warmup, threads)
         line = {"metric": METRIC, "value": rate, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / rate, "higher_is_better": True,
@@ -458,7 +467,7 @@ def main():
         return
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        threads = os.cpu_count() or 1
+        threads = host_cores()
         rate, med, sample = cpu_port_rate(args.config, 16, 2, threads)
         cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
     step_tflops = costs["total"] / (ms_step * 1e-3) / 1e12
