@@ -151,6 +151,18 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------- GPU side
+def hbm_peak_gbs():
+    """(GB/s, source): the driver-measured copy bandwidth of MEASURED_PEAKS.json, else the
+    pool's earlier measurement of 6.65 TB/s."""
+    try:
+        value = float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["hbm_gbs"])
+        if value > 0:
+            return value, "MEASURED_PEAKS.json hbm_gbs (measured)"
+    except (OSError, ValueError, KeyError, TypeError):
+        pass
+    return 6650.0, "fallback 6.65 TB/s (no MEASURED_PEAKS.json)"
+
+
 def fp64_peak(device_stream, torch):
     from flashns_b200 import _lib
     lib = _lib.library()
@@ -340,7 +352,7 @@ def main():
     import torch
     import torch.distributed as dist
     from datetime import timedelta
-    from flashns_b200.costs import checkpoint_bytes, evaluation_costs
+    from flashns_b200.costs import checkpoint_bytes, evaluation_bytes, evaluation_costs, kernel_rooflines
     from flashns_b200.evaluator import PackedEvaluator, flat_parameters
     from flashns_b200.ns_seed import NSLoss
     from flashns_b200.problems import CONFIGS, config_options, config_parameters, config_points
@@ -452,6 +464,10 @@ def main():
     dominant = max(ktimes, key=lambda k: ktimes[k]["total_ms_per_eval"])
     dom_flops = statistics.mean(costs["per_kind"][dominant])
     achieved = dom_flops / (ktimes[dominant]["avg_ms"] * 1e-3) / 1e12
+    hbm_peak, hbm_source = hbm_peak_gbs()
+    kernels = kernel_rooflines(ktimes, costs["per_kind"],
+                               evaluation_bytes(widths, ev.ni, ev.nb, head=head, boundary_order=order), peak,
+                               hbm_peak)
     traffic = None
     tfile = ROOT / "profiles" / "traffic.json"
     if tfile.exists():
@@ -497,7 +513,10 @@ def main():
                      "flops_per_launch": dom_flops},
         "step_roofline": {"algorithmic_tflop_per_step": costs["total"] / 1e12, "achieved": step_tflops,
                           "frac": step_tflops / peak},
-        "kernels": ktimes,
+        "kernels": kernels,
+        "kernel_peaks": {"fp64_tflops": peak, "hbm_gbs": hbm_peak, "hbm_source": hbm_source,
+                         "note": "per kind: CUDA-event mean launch time, algorithmic FLOPs and compulsory "
+                                 "DRAM bytes per launch (flashns_b200/costs.py)"},
         "clocks": clocks,
     }
     if vs_baseline is not None:

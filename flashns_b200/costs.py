@@ -88,6 +88,73 @@ def evaluation_costs(widths, ni, nb, *, head, boundary_order):
     return {"per_kind": out, "total": total, "gemm": gemm, "rows": rows}
 
 
+def evaluation_bytes(widths, ni, nb, *, head, boundary_order):
+    """Dict kind -> list of per-launch compulsory DRAM bytes, in the launch order of
+    ``evaluation_costs``: every checkpoint, auxiliary and seed a launch must read or write
+    once (FP64), plus its inputs (coordinates, objective weights and targets).  Weights,
+    biases and the per-CTA partials are left out (KB against the MB-GB tensors).
+
+    * first: x in; H_1 and a1_1 out.
+    * forward l: H_l in; H_{l+1}, a1_{l+1} out.
+    * head: H_L, a1_L, objective in; D_L out (with a single hidden layer: x in instead,
+      bar_Z_1 contracted on chip).  forward_head (fused): H_{L-1} and the objective in,
+      D_L out (H_L and a1_L stay on chip).
+    * backward l: D_{l+1}, H_l, a1_l in; D_l out, except layer 1, whose bar_Z_1 is
+      contracted with the coordinate jets (x in) and never stored.
+    * wgrad l (when not fused into backward): D_{l+1} and H_l in.
+    """
+    dim = widths[0]
+    q = 10 if dim == 2 else 20
+    qb = dim + 1 if boundary_order else 1
+    rows = ni * q + nb * qb
+    points = ni + nb
+    nh = len(widths) - 2
+    f = 3 if (head == "uvp" or boundary_order) else 2
+    objective = 8 * (ni + 2 * nb * f)
+    x = 8 * points * dim
+    hbytes = lambda c: 8 * rows * c
+    abytes = lambda c: 8 * points * c
+    out = {"first": [x + hbytes(widths[1]) + abytes(widths[1])], "forward": [], "head": [], "backward": [],
+           "wgrad": []}
+    for l in range(1, nh):
+        out["forward"].append(hbytes(widths[l]) + hbytes(widths[l + 1]) + abytes(widths[l + 1]))
+    c = widths[nh]
+    # with one hidden layer the head also contracts bar_Z_1 with the coordinates (x in,
+    # no seed out)
+    out["head"].append(hbytes(c) + abytes(c) + objective + (x if nh == 1 else hbytes(c)))
+    for l in range(nh - 1, 0, -1):
+        cin, cout = widths[l], widths[l + 1]
+        seeds_and_checkpoints = hbytes(cout) + hbytes(cin) + abytes(cin)
+        # layer 1 reads the coordinates instead of writing bar_Z_1
+        out["backward"].append(seeds_and_checkpoints + (x if l == 1 else hbytes(cin)))
+        if not fused_backward(widths, l):
+            out["wgrad"].append(hbytes(cout) + hbytes(cin))
+    if fused_head(widths):
+        out["forward"].pop()
+        out["head"].pop()
+        out["forward_head"] = [hbytes(widths[nh - 1]) + objective + hbytes(c)]
+    return out
+
+
+def kernel_rooflines(times, flops, dram_bytes, fp64_peak_tflops, hbm_peak_gbs):
+    """Per kernel kind: achieved FP64 TFLOP/s and compulsory-traffic GB/s, each against its
+    peak, from the mean launch time ``times[kind]["avg_ms"]`` and the mean per-launch
+    figures of ``evaluation_costs`` / ``evaluation_bytes``.  Kinds without a model (the
+    parameter packing, the final reduction) keep only their times."""
+    out = {}
+    for kind, t in times.items():
+        row = dict(t)
+        ms = t.get("avg_ms")
+        if ms and flops.get(kind) and dram_bytes.get(kind):
+            f = sum(flops[kind]) / len(flops[kind])
+            b = sum(dram_bytes[kind]) / len(dram_bytes[kind])
+            tflops, gbs = f / (ms * 1e-3) / 1e12, b / (ms * 1e-3) / 1e9
+            row.update(tflops=tflops, fp64_frac=tflops / fp64_peak_tflops, gbs=gbs, hbm_frac=gbs / hbm_peak_gbs,
+                       flops_per_launch=f, dram_bytes_per_launch=b)
+        out[kind] = row
+    return out
+
+
 def checkpoint_bytes(widths, ni, nb, *, boundary_order):
     """Compulsory HBM bytes: each hidden checkpoint written and read once, a1 likewise,
     one seed buffer per hidden layer written and read, inputs and the gradient."""

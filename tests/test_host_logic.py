@@ -192,3 +192,24 @@ def test_foreign_stage_hooks_are_named():
     mine = lambda *a, **k: None
     assert foreign_hooks(activation_factory=TensorActivation, coordinate_affine=mine, cuda_seed=mine) == [
         "coordinate_affine", "cuda_seed"]
+
+
+def test_compulsory_bytes_per_kernel_match_the_cfg1_profile():
+    """The per-launch DRAM model reproduces the compulsory figures of the cfg1 kernels
+    (backward 281 MB, forward 191 MB, fused head 180 MB of seeds and checkpoints) and
+    lines up launch for launch with the FLOP model for every width pattern."""
+    from flashns_b200.costs import evaluation_bytes, evaluation_costs, kernel_rooflines
+    b = evaluation_bytes([2, 64, 64, 64, 64, 2], 16384, 4096, head="psi", boundary_order=1)
+    mb = lambda v: round(v / 1e6)
+    assert [mb(v) for v in b["backward"][:2]] == [281, 281] and [mb(v) for v in b["forward"]] == [191, 191]
+    assert mb(b["forward_head"][0]) == 181 and mb(b["first"][0]) == 101
+    for widths, head, order in (([2, 128, 128, 128, 2], "psi", 1), ([3] + [128] * 5 + [2], "psi", 1),
+                                ([2, 64, 64, 3], "uvp", 0), ([2, 20, 3], "uvp", 0), ([2, 30, 64, 64, 2], "psi", 0)):
+        c = evaluation_costs(widths, 100, 10, head=head, boundary_order=order)["per_kind"]
+        d = evaluation_bytes(widths, 100, 10, head=head, boundary_order=order)
+        assert {k: len(v) for k, v in c.items() if v} == {k: len(v) for k, v in d.items() if v}, widths
+    flops = evaluation_costs([2, 64, 64, 64, 64, 2], 16384, 4096, head="psi", boundary_order=1)["per_kind"]
+    times = {"backward": {"avg_ms": 0.1158, "launches_per_eval": 3}, "reduce": {"avg_ms": 0.0101}}
+    r = kernel_rooflines(times, flops, b, 37.1, 6552.6)
+    assert 25 < r["backward"]["tflops"] < 27 and abs(r["backward"]["fp64_frac"] - r["backward"]["tflops"] / 37.1) < 1e-12
+    assert 2000 < r["backward"]["gbs"] < 2500 and r["reduce"] == {"avg_ms": 0.0101}
