@@ -2,6 +2,7 @@
 
     python -m flashns_b200.build          # incremental
     python -m flashns_b200.build --force
+    python -m flashns_b200.build --stamps # instrumented variant, libflashns_b200_stamps.so
 
 Objects go to ``flashns_b200/_build/``; the shared library is written next to
 this file so that it travels with the source tree.
@@ -20,6 +21,10 @@ ROOT = HERE.parent
 CSRC = HERE / "csrc"
 BUILD = HERE / "_build"
 LIBRARY = HERE / "libflashns_b200.so"
+# instrumented variant: the two-group kernels stamp their phase boundaries (read by
+# python -m flashns_b200.stamps); the product never loads it
+STAMPS_BUILD = HERE / "_build_stamps"
+STAMPS_LIBRARY = HERE / "libflashns_b200_stamps.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC",
          "-diag-suppress", "177", f"-I{ROOT / 'include'}", f"-I{CSRC}"]
@@ -47,19 +52,21 @@ def _stale(target, inputs):
     return any(p.stat().st_mtime > t for p in inputs)
 
 
-def build(force=False, verbose=False):
-    BUILD.mkdir(exist_ok=True)
+def build(force=False, verbose=False, stamps=False):
+    out_dir, library = (STAMPS_BUILD, STAMPS_LIBRARY) if stamps else (BUILD, LIBRARY)
+    flags = FLAGS + (["-DFLASHNS_B200_STAMPS"] if stamps else [])
+    out_dir.mkdir(exist_ok=True)
     deps = dependencies()
     compiler = nvcc()
     jobs = []
     for src in sources():
-        obj = BUILD / (src.stem + ".o")
+        obj = out_dir / (src.stem + ".o")
         if force or _stale(obj, [src, *deps]):
             jobs.append((src, obj))
 
     def compile_one(job):
         src, obj = job
-        cmd = [compiler, *ARCH, *FLAGS, "-c", str(src), "-o", str(obj)]
+        cmd = [compiler, *ARCH, *flags, "-c", str(src), "-o", str(obj)]
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
         result = subprocess.run(cmd, capture_output=True, text=True)
@@ -72,23 +79,25 @@ def build(force=False, verbose=False):
     if verbose:
         for log in logs:
             sys.stderr.write(log)
-    objects = [BUILD / (s.stem + ".o") for s in sources()]
-    if force or jobs or _stale(LIBRARY, objects):
-        tmp = LIBRARY.with_suffix(".so.tmp")
+    objects = [out_dir / (s.stem + ".o") for s in sources()]
+    if force or jobs or _stale(library, objects):
+        tmp = library.with_suffix(".so.tmp")
         cmd = [compiler, *ARCH, "-shared", "-Xcompiler", "-fPIC", *map(str, objects), "-o", str(tmp)]
         result = subprocess.run(cmd, capture_output=True, text=True)
         if result.returncode:
             raise RuntimeError(f"link failed:\n{result.stderr}")
-        os.replace(tmp, LIBRARY)
-    return LIBRARY
+        os.replace(tmp, library)
+    return library
 
 
 def main():
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--force", action="store_true")
     parser.add_argument("--verbose", action="store_true")
+    parser.add_argument("--stamps", action="store_true",
+                        help="build the instrumented library (phase stamps of the two-group kernels)")
     args = parser.parse_args()
-    print(build(force=args.force, verbose=args.verbose))
+    print(build(force=args.force, verbose=args.verbose, stamps=args.stamps))
 
 
 if __name__ == "__main__":

@@ -213,3 +213,38 @@ def test_compulsory_bytes_per_kernel_match_the_cfg1_profile():
     r = kernel_rooflines(times, flops, b, 37.1, 6552.6)
     assert 25 < r["backward"]["tflops"] < 27 and abs(r["backward"]["fp64_frac"] - r["backward"]["tflops"] / 37.1) < 1e-12
     assert 2000 < r["backward"]["gbs"] < 2500 and r["reduce"] == {"avg_ms": 0.0101}
+
+
+def test_stamp_summary_of_two_groups():
+    """Phase durations and the MMA share of a CTA's span from synthetic stamps
+    (flashns_b200.stamps.summarize; %globaltimer ns)."""
+    from flashns_b200.stamps import PHASES, TILES, summarize
+    st = np.zeros((2, 1, 2, TILES, PHASES), dtype=np.int64)
+    st[0, 0, 0, 0] = (1000, 2000, 4000, 7000, 12000)     # backward: wait 1, dgrad 2, wgrad 3, epilogue 5 us
+    st[0, 0, 1, 0] = (1000, 7000, 9000, 12000, 15000)    # waits 6 us for the turn
+    st[1, 0, 0, 0, :4] = (0, 0, 0, 0)                    # a launch without stamps is skipped
+    rows = summarize(st, ["backward", "reduce"])
+    assert len(rows) == 1 and rows[0]["half_tiles"] == 2
+    us = rows[0]["us"]
+    assert us["wait"] == 3.5 and us["dgrad"] == 2.0 and us["wait H + wgrad"] == 3.0 and us["epilogue"] == 4.0
+    assert abs(rows[0]["mma_share_of_cta_span"] - (5000 + 5000) / 14000) < 1e-12
+    fw = np.zeros((1, 1, 2, TILES, PHASES), dtype=np.int64)
+    fw[0, 0, 0, 0, :4] = (0 + 5, 1005, 3005, 6005)
+    rows = summarize(fw, ["forward"])
+    assert rows[0]["us"] == {"wait": 1.0, "mainloop": 2.0, "epilogue": 3.0}
+    assert abs(rows[0]["mma_share_of_cta_span"] - 2 / 6) < 1e-12
+
+
+def test_instrumented_variant_compiles():
+    """The stamp hooks of the instrumented build (FLASHNS_B200_STAMPS) compile; in the
+    product build they expand to nothing."""
+    import subprocess
+
+    from flashns_b200 import build
+    obj = build.ROOT / "flashns_b200" / "_build_stamps" / "eval_check.o"
+    obj.parent.mkdir(exist_ok=True)
+    cmd = [build.nvcc(), *build.ARCH, *build.FLAGS, "-DFLASHNS_B200_STAMPS", "-c",
+           str(build.CSRC / "eval.cu"), "-o", str(obj)]
+    result = subprocess.run(cmd, capture_output=True, text=True)
+    assert result.returncode == 0, result.stderr[-2000:]
+    obj.unlink()
