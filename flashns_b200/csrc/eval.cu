@@ -2264,8 +2264,10 @@ __global__ void __launch_bounds__(kPPThreads, 1)
     for (int j = 0; j < T::NT; ++j)
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[j][e] = 0.0;
+    FLASHNS_STAMP(gp, k, 0, gtid == 0);  // half tile begins
     if (!dead) dead = named_sync_or(bar_group, GT, !wait_tile(tile));
     named_sync(kPPBarTurn + gp, kPPThreads);  // this group's turn on the tensor pipe
+    FLASHNS_STAMP(gp, k, 1, gtid == 0);       // turn taken: the mainloop begins
     if (!dead) {
       // Z^T[ch][rows] = W_{L-1}[ch][cin] H_{L-1}^T[cin][rows]
 #pragma unroll
@@ -2284,6 +2286,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         }
       }
     }
+    FLASHNS_STAMP(gp, k, 2, gtid == 0);                // mainloop issued: the turn passes on
     named_arrive(kPPBarTurn + (1 - gp), kPPThreads);  // the other group's turn
     named_sync(bar_group, GT);                         // this group's input planes free
     if (k + 1 < nmy && !dead) load_tile(tile_of(k + 1));
@@ -2452,6 +2455,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         }
       }
     }
+    FLASHNS_STAMP(gp, k, 3, gtid == 0);  // epilogue done (this thread's share)
   }
   // turn counts balanced as in bwd_pingpong
   if (gp == 0 && n0 == n1) named_sync(kPPBarTurn + 0, kPPThreads);

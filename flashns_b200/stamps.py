@@ -4,13 +4,15 @@
     python -m flashns_b200.stamps [--config cfg1] [--evals 5] [--json]
 
 ``libflashns_b200_stamps.so`` is this library built with ``FLASHNS_B200_STAMPS``: the
-leader thread of each 8-warp group of ``bwd_pingpong`` and ``fwd_pingpong`` writes
-``%globaltimer`` at the phase boundaries of each of its half tiles.  For every launch of
-those kernels in one evaluation this reports, per half tile and in microseconds:
+leader thread of each 8-warp group of ``bwd_pingpong``, ``fwd_pingpong`` and
+``head_pingpong`` writes ``%globaltimer`` at the phase boundaries of each of its half
+tiles.  For every launch of those kernels in one evaluation this reports, per half tile
+and in microseconds:
 
 * backward: the wait for the seed tile and the turn, dgrad, the wait for H_l plus wgrad,
   and the VJP epilogue (the leader thread's share, to the group barrier);
-* forward: the wait for the input tile and the turn, the mainloop, and the epilogue;
+* forward and the fused head: the wait for the input tile and the turn, the mainloop,
+  and the epilogue (for the head: jet, output layer, seeds, output gradient and VJP);
 
 and the share of each CTA's span during which one of its two groups held the tensor pipe
 (its MMA phases), averaged over the CTAs.  The instrumentation changes register
@@ -26,7 +28,8 @@ import statistics
 TILES, PHASES = 32, 5  # kStampTiles, kStampPhases of csrc/eval.cu
 # kernel kind -> (phase names between consecutive stamps, the stamps bounding the MMA phase)
 LAYOUT = {"backward": (("wait", "dgrad", "wait H + wgrad", "epilogue"), (1, 3)),
-          "forward": (("wait", "mainloop", "epilogue"), (1, 2))}
+          "forward": (("wait", "mainloop", "epilogue"), (1, 2)),
+          "forward_head": (("wait", "mainloop", "epilogue"), (1, 2))}
 
 
 def summarize(stamps, kinds):
