@@ -3328,7 +3328,11 @@ static int run_eval(const flashns_b200_plan* p, const double* coordinates, const
     ~ProgrammaticScope() { t_programmatic = false; }
   } programmatic_scope;
   t_programmatic = false;
+#ifdef FLASHNS_B200_STAMPS
+  const bool overlap = false;  // instrumented build: a stamp-slot copy sits between the kernels
+#else
   const bool overlap = events == nullptr;
+#endif
   if (!p->direct) {
     int64_t packed = 0;
     for (int l = 0; l < p->n_aff; ++l) packed += int64_t(tab.l[l].coutp) * tab.l[l].cinp + tab.l[l].coutp;
