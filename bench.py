@@ -3,17 +3,19 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg1]
                     [--impl ours|reference|reference-gpu] [--route F|B1|v8|v8+]
 
-Workload: the Kovasznay stream-function net
-2->64x4->2 on 16,384 interior points with full third-order Q10 jets plus 4,096
-boundary points with first-order rows, FP64, seeded synthetic points and
-Xavier-normal weights (seed 0).  One step is one complete loss + gradient
+Default workload (cfg1): the Kovasznay stream-function net 2->64x4->2 on 16,384
+interior points with full third-order Q10 jets plus 4,096 boundary points with
+first-order rows, FP64, seeded synthetic points and Xavier-normal weights (seed 0).  One step is one complete loss + gradient
 evaluation of a cfg1-sized point set per GPU.  With N GPUs (torchrun, one rank
 per GPU) the global point set is N x cfg1, each rank evaluates its shard and one
 NCCL all-reduce of the packed [gradient, loss] buffer completes the step (weak
 scaling); ``value`` counts cfg1-sized shard evaluations of all ranks per second.
 
-``--impl reference`` times the reference algorithm's CPU path (the oracle port of
-``PackedPINN``, all host threads) on the same workload; rank 0 alone prints.
+``--impl reference`` times the reference's own CPU implementation, its ``PackedPINN``
+(installed into ``baseline/_ref/`` by ``baseline/install_reference.py``, run by
+``baseline/reference_cpu.py`` with torch on all host threads), on the same point set;
+where that is not installed, or for the 3-D configuration the reference has no head for,
+the oracle port of ``PackedPINN`` is timed instead.  Rank 0 alone runs and prints.
 
 ``--impl reference-gpu --config ref16k`` times one of the reference's own GPU routes on
 this GPU (``--route``: F, its published H100 headline route; B1; the v8 packed route;
@@ -40,6 +42,8 @@ REF16K_PUBLISHED_MS = 1.832
 # (docs/cuda-h100-results.md:54-64); the v8 packed routes have none
 REFERENCE_ROUTE_PUBLISHED_MS = {"F": 1.832, "B1": 1.954}
 METRIC = "FP64 loss+param-gradient evals/sec"
+# NVIDIA's published dense FP64 tensor-core figure for B200, beside the in-run probe
+FP64_DATASHEET_TFLOPS = 40.0
 UNIT = "evals/s"
 
 
@@ -100,6 +104,42 @@ def cpu_port_rate(config, steps, warmup, workers):
               f"of the {config} set split over {workers} single-threaded NumPy processes; "
               f"evals/s = (1/{parts}) / median step time")
     return rate, med, sample
+
+
+def reference_cpu_rate(config, steps, warmup, threads, parts=1):
+    """The reference's own PackedPINN on `threads` host threads, in its own process
+    (baseline/reference_cpu.py); returns its JSON line, or None when it is not installed
+    or does not cover the configuration."""
+    from baseline.reference_cpu import available
+    from flashns_b200.problems import CONFIGS
+    if not available() or CONFIGS[config]["kind"] == "taylor_green":
+        return None
+    cmd = [sys.executable, "-m", "baseline.reference_cpu", "--config", config, "--steps", str(steps),
+           "--warmup", str(warmup), "--parts", str(parts), "--threads", str(threads)]
+    result = subprocess.run(cmd, capture_output=True, text=True, cwd=ROOT, timeout=900)
+    if result.returncode:
+        raise RuntimeError(f"reference CPU arm failed:\n{result.stderr[-2000:]}")
+    return json.loads(result.stdout.strip().splitlines()[-1])
+
+
+def reference_cpu_sample(r, config):
+    chunk = (f"one of {r['parts']} point chunks ({r['interior'] // r['parts']}+{r['boundary'] // r['parts']} "
+             f"points) per step; evals/s = (1/{r['parts']}) / median step time" if r["parts"] > 1
+             else "one complete evaluation per step; evals/s = 1 / median step time")
+    head = ("the same (u, v, p) objective as the repo arm" if config == "ref16k" else
+            "the (u, v, p) head (the reference has no stream-function head)")
+    return (f"the reference's PackedPINN(layout='compact', seed='explicit') from {r['module']}, torch CPU FP64 "
+            f"on {r['threads']} threads: {head} on the {config} point set, net {r['net']}, {r['rows']} packed "
+            f"rows; {len(r['times_s'])} timed steps, {chunk}")
+
+
+def kernel_source_sha():
+    """sha256 over the CUDA sources and the C header (the build an ncu capture belongs to)."""
+    import hashlib
+    h = hashlib.sha256()
+    for path in sorted((ROOT / "flashns_b200" / "csrc").glob("*.cu*")) + sorted((ROOT / "include").glob("*.h")):
+        h.update(path.name.encode() + b"\0" + path.read_bytes())
+    return h.hexdigest()
 
 
 # ---------------------------------------------------------------------------- clocks
@@ -312,7 +352,7 @@ def reference_gpu_arm(args, cfg, local):
         "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": value / (1e3 / published) if published else None, "dtype": "f64",
         "data": "synthetic (the reference benchmark's recipe, as in --impl ours --config ref16k)",
-        "config": dict(cfg, parallelism="single"),
+        "config": cfg, "parallelism": "single",
         "e2e": {"value": 1e3 / e2e_ms, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "kernels_from": {k: {"sources": sorted(v["sources"]), "sha256": v["sha256"][:16]} for k, v in libs.items()},
         "cutlass": kernels.build.get("cutlass"),
@@ -340,11 +380,21 @@ def main():
         if rank != 0:
             return
         threads = host_cores()
-        rate, med, sample = cpu_port_rate(args.config, args.steps, args.warmup, threads)
+        # full evaluations when the run stays within a few minutes, else point chunks
+        parts = 1 if args.steps + args.warmup <= 60 else min(64, 1 << (args.steps + args.warmup - 1).bit_length() - 5)
+        ref = reference_cpu_rate(args.config, args.steps, args.warmup, threads, parts)
+        if ref is not None:
+            rate, kind, sample = ref["value"], "reference", reference_cpu_sample(ref, args.config)
+            objective = (f"the reference's (u, v, p) head with the gradient-enhanced residual on value boundary "
+                         f"rows, net {ref['net']}, same points and weights as the repo arm")
+        else:
+            rate, _, sample = cpu_port_rate(args.config, args.steps, args.warmup, threads)
+            kind, objective = "port", "the oracle port of PackedPINN on the repo arm's exact objective"
         line = {"metric": METRIC, "value": rate, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / rate, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic", "config": cfg,
-                "cpu_baseline": {"value": rate, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+                "reference_objective": objective,
+                "cpu_baseline": {"value": rate, "unit": UNIT, "cores": threads, "kind": kind, "sample": sample},
                 "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
@@ -468,12 +518,20 @@ def main():
     kernels = kernel_rooflines(ktimes, costs["per_kind"],
                                evaluation_bytes(widths, ev.ni, ev.nb, head=head, boundary_order=order), peak,
                                hbm_peak)
-    traffic = None
+    # DRAM bytes of one launch of the dominant kernel from a committed ncu capture, used only
+    # when that capture was taken of the kernel sources built here
+    traffic, traffic_source = None, "no ncu capture of this configuration committed"
     tfile = ROOT / "profiles" / "traffic.json"
     if tfile.exists():
         try:
-            traffic = json.loads(tfile.read_text()).get(args.config, {}).get(dominant)
-        except (ValueError, AttributeError):
+            record = json.loads(tfile.read_text())
+            captured = record.get(args.config, {}).get(dominant)
+            if captured is not None and record.get("kernel_source_sha") == kernel_source_sha():
+                traffic = captured
+                traffic_source = f"ncu capture of this build (profiles/traffic.json, sources {record['kernel_source_sha'][:12]})"
+            elif captured is not None:
+                traffic_source = "dropped: the committed ncu capture is of other kernel sources"
+        except (ValueError, AttributeError, KeyError):
             traffic = None
 
     if world > 1:
@@ -481,11 +539,14 @@ def main():
         dist.destroy_process_group()
     if rank != 0:
         return
-    cpu = None
+    cpu = port = None
     if world == 1 and not args.no_cpu_baseline:
         threads = host_cores()
+        ref = reference_cpu_rate(args.config, 3, 1, threads)
         rate, med, sample = cpu_port_rate(args.config, 16, 2, threads)
-        cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
+        port = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
+        cpu = port if ref is None else {"value": ref["value"], "unit": UNIT, "cores": threads, "kind": "reference",
+                                        "sample": reference_cpu_sample(ref, args.config)}
     step_tflops = costs["total"] / (ms_step * 1e-3) / 1e12
     value = world * 1e3 / ms_step
     if args.config == "ref16k":
@@ -501,18 +562,21 @@ def main():
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": vs_baseline, "dtype": "f64", "data": data,
-        "config": dict(cfg, parallelism=f"dp{world}" if world > 1 else "single",
-                       l2="working set (checkpoints + seeds) %.2f GB > 126 MB L2; no flush needed"
-                          % (checkpoint_bytes(widths, ev.ni, ev.nb, boundary_order=order) / 1e9)),
+        "config": cfg,
+        "parallelism": f"dp{world}" if world > 1 else "single",
+        "l2": "working set (checkpoints + seeds) %.2f GB > 126 MB L2; no flush needed"
+              % (checkpoint_bytes(widths, ev.ni, ev.nb, boundary_order=order) / 1e9),
         "e2e": {"value": world * 1e3 / float(e2e_ms), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": ev.launches_per_call * args.steps,
         "roofline": {"bound": "tensor", "kernel": dominant, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": achieved / peak, "traffic": traffic,
+                     "frac": achieved / peak, "traffic": traffic, "traffic_source": traffic_source,
                      "peak_source": "in-run FP64 DMMA m16n8k8 register-only probe (no FP64 entry in MEASURED_PEAKS.json)",
+                     "frac_of_datasheet": achieved / FP64_DATASHEET_TFLOPS,
+                     "datasheet_peak": FP64_DATASHEET_TFLOPS,
                      "flops_per_launch": dom_flops},
         "step_roofline": {"algorithmic_tflop_per_step": costs["total"] / 1e12, "achieved": step_tflops,
-                          "frac": step_tflops / peak},
+                          "frac": step_tflops / peak, "frac_of_datasheet": step_tflops / FP64_DATASHEET_TFLOPS},
         "kernels": kernels,
         "kernel_peaks": {"fp64_tflops": peak, "hbm_gbs": hbm_peak, "hbm_source": hbm_source,
                          "note": "per kind: CUDA-event mean launch time, algorithmic FLOPs and compulsory "
@@ -524,6 +588,8 @@ def main():
                                  "(docs/cuda-h100-results.md:54-64), other hardware")
     if cpu:
         line["cpu_baseline"] = cpu
+    if port and cpu is not port:
+        line["cpu_baseline_port"] = port
     print(json.dumps(line), flush=True)
 
 

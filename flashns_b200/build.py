@@ -2,7 +2,6 @@
 
     python -m flashns_b200.build          # incremental
     python -m flashns_b200.build --force
-    python -m flashns_b200.build --stamps # instrumented variant, libflashns_b200_stamps.so
 
 Objects go to ``flashns_b200/_build/``; the shared library is written next to
 this file so that it travels with the source tree.
@@ -21,10 +20,6 @@ ROOT = HERE.parent
 CSRC = HERE / "csrc"
 BUILD = HERE / "_build"
 LIBRARY = HERE / "libflashns_b200.so"
-# instrumented variant: the two-group kernels stamp their phase boundaries (read by
-# python -m flashns_b200.stamps); the product never loads it
-STAMPS_BUILD = HERE / "_build_stamps"
-STAMPS_LIBRARY = HERE / "libflashns_b200_stamps.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC",
          "-diag-suppress", "177", f"-I{ROOT / 'include'}", f"-I{CSRC}"]
@@ -52,9 +47,8 @@ def _stale(target, inputs):
     return any(p.stat().st_mtime > t for p in inputs)
 
 
-def build(force=False, verbose=False, stamps=False):
-    out_dir, library = (STAMPS_BUILD, STAMPS_LIBRARY) if stamps else (BUILD, LIBRARY)
-    flags = FLAGS + (["-DFLASHNS_B200_STAMPS"] if stamps else [])
+def build(force=False, verbose=False):
+    out_dir, library, flags = BUILD, LIBRARY, FLAGS
     out_dir.mkdir(exist_ok=True)
     deps = dependencies()
     compiler = nvcc()
@@ -94,10 +88,8 @@ def main():
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--force", action="store_true")
     parser.add_argument("--verbose", action="store_true")
-    parser.add_argument("--stamps", action="store_true",
-                        help="build the instrumented library (phase stamps of the two-group kernels)")
     args = parser.parse_args()
-    print(build(force=args.force, verbose=args.verbose, stamps=args.stamps))
+    print(build(force=args.force, verbose=args.verbose))
 
 
 if __name__ == "__main__":

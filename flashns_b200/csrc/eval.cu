@@ -39,31 +39,6 @@ constexpr int kMaxAffine = 16;
 // set by a kernel whose bounded wait on a bulk copy gave up (read by flashns_b200_device_fault)
 __device__ int g_device_fault = 0;
 
-// Phase stamps of the two-group kernels, compiled only into the instrumented library
-// (python -m flashns_b200.build --stamps; read by python -m flashns_b200.stamps).  The
-// leader thread of each group writes %globaltimer at the phase boundaries of each of its
-// half tiles into g_stamps[launch][cta][group][tile][phase].  In the product library the
-// macro expands to nothing.
-constexpr int kStampTiles = 32, kStampPhases = 5;
-#ifdef FLASHNS_B200_STAMPS
-__device__ unsigned long long* g_stamps = nullptr;
-__device__ long long g_stamp_ctas = 0;  // CTAs per launch the buffer holds
-__device__ int g_stamp_launch = -1;     // launch slot of the next kernels (set by the host)
-__device__ int g_stamp_launches = 0;
-__device__ __forceinline__ void phase_stamp(int group, int64_t tile, int phase, bool leader) {
-  if (!leader || !g_stamps || g_stamp_launch < 0 || g_stamp_launch >= g_stamp_launches || tile >= kStampTiles ||
-      blockIdx.x >= g_stamp_ctas)
-    return;
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  const long long slot = (((long long)g_stamp_launch * g_stamp_ctas + blockIdx.x) * 2 + group) * kStampTiles + tile;
-  g_stamps[slot * kStampPhases + phase] = t;
-}
-#define FLASHNS_STAMP(group, tile, phase, leader) phase_stamp(group, tile, phase, leader)
-#else
-#define FLASHNS_STAMP(group, tile, phase, leader) ((void)0)
-#endif
-
 // Self-test of the bounded wait: an mbarrier that nothing arrives at.  The wait gives up
 // after `spins` polls, raises the fault word and the kernel returns normally.
 __global__ void wait_timeout_probe(unsigned spins, int* gave_up) {
@@ -1101,7 +1076,6 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   for (int64_t k = 0; k < nmy; ++k) {
     const int64_t tile = tile_of(k);
     const bool has_next = k + 1 < nmy;
-    FLASHNS_STAMP(gp, k, 0, gtid == 0);  // half tile begins (waits for its seed and the turn follow)
     if (gtid == 0 && !dead) {  // the epilogue reads this tile's a1 rows (a contiguous range): into L2
       int64_t pt0, pts;
       TL::points(geo, nint, tile, pt0, pts);
@@ -1114,7 +1088,6 @@ __global__ void __launch_bounds__(kPPThreads, 1)
       for (int e = 0; e < 4; ++e) acc[j][e] = 0.0;
     if (!dead) dead = named_sync_or(bar_group, GT, !wait_tile(tile, bar_seed, ph_seed, false));
     named_sync(kPPBarTurn + gp, kPPThreads);  // this group's turn on the tensor pipe
-    FLASHNS_STAMP(gp, k, 1, gtid == 0);       // turn taken: dgrad begins
     if (!dead) {
       // dgrad: dH[ch][rows] += W_l^T[ch][cout plane] D^T[cout plane][rows]
 #pragma unroll
@@ -1132,7 +1105,6 @@ __global__ void __launch_bounds__(kPPThreads, 1)
           for (int j = 0; j < T::NT; ++j) mma_m16n8k8(acc[j], a, cB[2 * j * LDC + kk + t], cB[2 * j * LDC + kk + t + 4]);
         }
       }
-      FLASHNS_STAMP(gp, k, 2, gtid == 0);  // dgrad issued: the wait for H_l and wgrad follow
       dead = named_sync_or(bar_group, GT, !wait_tile(tile, bar_h, ph_h, true));  // H_l landed
     }
     if (!dead) {
@@ -1154,7 +1126,6 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         }
       }
     }
-    FLASHNS_STAMP(gp, k, 3, gtid == 0);                // wgrad issued: the turn passes on
     named_arrive(kPPBarTurn + (1 - gp), kPPThreads);  // the other group's turn
     named_sync(bar_group, GT);                         // this group's seed planes free
     if (has_next && !dead) load_tile(tile_of(k + 1), sB, &tm_seed_i, &tm_seed_b, bar_seed, dnext);
@@ -1217,7 +1188,6 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         }
       }
     }
-    FLASHNS_STAMP(gp, k, 4, gtid == 0);  // epilogue done (this thread's share)
     named_sync(bar_group, GT);  // this group's H_l planes free
     if (has_next && !dead) load_tile(tile_of(k + 1), sH, &tm_h_i, &tm_h_b, bar_h, hcur);
   }
@@ -1392,10 +1362,8 @@ __global__ void __launch_bounds__(kPPThreads, 1)
     for (int j = 0; j < T::NT; ++j)
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[j][e] = 0.0;
-    FLASHNS_STAMP(gp, k, 0, gtid == 0);  // half tile begins
     if (!dead) dead = named_sync_or(bar_group, GT, !wait_tile(tile));
     named_sync(kPPBarTurn + gp, kPPThreads);  // this group's turn on the tensor pipe
-    FLASHNS_STAMP(gp, k, 1, gtid == 0);       // turn taken: the mainloop begins
     if (!dead) {
       // Z^T[ch][rows] = W_l[ch][cin] H_l^T[cin][rows]
 #pragma unroll
@@ -1414,7 +1382,6 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         }
       }
     }
-    FLASHNS_STAMP(gp, k, 2, gtid == 0);                // mainloop issued: the turn passes on
     named_arrive(kPPBarTurn + (1 - gp), kPPThreads);  // the other group's turn
     named_sync(bar_group, GT);                         // this group's input planes free
     if (k + 1 < nmy && !dead) load_tile(tile_of(k + 1));
@@ -1458,7 +1425,6 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         }
       }
     }
-    FLASHNS_STAMP(gp, k, 3, gtid == 0);  // epilogue done (this thread's share)
   }
   // turn counts balanced as in bwd_pingpong
   if (gp == 0 && n0 == n1) named_sync(kPPBarTurn + 0, kPPThreads);
@@ -2264,10 +2230,8 @@ __global__ void __launch_bounds__(kPPThreads, 1)
     for (int j = 0; j < T::NT; ++j)
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[j][e] = 0.0;
-    FLASHNS_STAMP(gp, k, 0, gtid == 0);  // half tile begins
     if (!dead) dead = named_sync_or(bar_group, GT, !wait_tile(tile));
     named_sync(kPPBarTurn + gp, kPPThreads);  // this group's turn on the tensor pipe
-    FLASHNS_STAMP(gp, k, 1, gtid == 0);       // turn taken: the mainloop begins
     if (!dead) {
       // Z^T[ch][rows] = W_{L-1}[ch][cin] H_{L-1}^T[cin][rows]
 #pragma unroll
@@ -2286,7 +2250,6 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         }
       }
     }
-    FLASHNS_STAMP(gp, k, 2, gtid == 0);                // mainloop issued: the turn passes on
     named_arrive(kPPBarTurn + (1 - gp), kPPThreads);  // the other group's turn
     named_sync(bar_group, GT);                         // this group's input planes free
     if (k + 1 < nmy && !dead) load_tile(tile_of(k + 1));
@@ -2455,7 +2418,6 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         }
       }
     }
-    FLASHNS_STAMP(gp, k, 3, gtid == 0);  // epilogue done (this thread's share)
   }
   // turn counts balanced as in bwd_pingpong
   if (gp == 0 && n0 == n1) named_sync(kPPBarTurn + 0, kPPThreads);
@@ -3312,11 +3274,6 @@ static int run_eval(const flashns_b200_plan* p, const double* coordinates, const
   int marks = 0;
   auto mark = [&]() {
     if (events && marks < capacity) cudaEventRecord(events[marks], stream);
-#ifdef FLASHNS_B200_STAMPS
-    // instrumented build: the kernels launched next stamp into launch slot `marks`
-    const int slot = marks;
-    cudaMemcpyToSymbolAsync(g_stamp_launch, &slot, sizeof(int), 0, cudaMemcpyHostToDevice, stream);
-#endif
     ++marks;
   };
   double* ws = static_cast<double*>(workspace);
@@ -3328,11 +3285,7 @@ static int run_eval(const flashns_b200_plan* p, const double* coordinates, const
     ~ProgrammaticScope() { t_programmatic = false; }
   } programmatic_scope;
   t_programmatic = false;
-#ifdef FLASHNS_B200_STAMPS
-  const bool overlap = false;  // instrumented build: a stamp-slot copy sits between the kernels
-#else
   const bool overlap = events == nullptr;
-#endif
   if (!p->direct) {
     int64_t packed = 0;
     for (int l = 0; l < p->n_aff; ++l) packed += int64_t(tab.l[l].coutp) * tab.l[l].cinp + tab.l[l].coutp;
@@ -3484,8 +3437,9 @@ int flashns_b200_plan_launch_kinds(const flashns_b200_plan* p, int* kinds, int c
 // * Every GPU that loads this library holds the array until the process exits.
 // * Host code may not use the array's name as a device pointer (it is a host-side
 //   stand-in).  The first call on a device, with that device current, looks up the
-//   array's device address with cudaGetSymbolAddress and caches it; make that first
-//   call before any stream capture.
+//   array's device address with cudaGetSymbolAddress and caches it with the device's
+//   current context; make that first call before any stream capture.  A later call that
+//   finds another context current (after cudaDeviceReset, say) looks the address up again.
 // * All calls on a device share the one array and it keeps the last call's contents.
 //   Nothing in it has to start at zero: every evaluation writes each scratch value
 //   before reading it.  Calls whose executions overlap on the GPU (other streams, or
@@ -3496,7 +3450,28 @@ namespace {
 __device__ __align__(256) double g_static_workspace[FLASHNS_B200_STATIC_WORKSPACE_BYTES / sizeof(double)];
 std::mutex g_static_mutex;
 constexpr int kMaxDevices = 64;
-void* g_static_address[kMaxDevices] = {};
+struct StaticScratch {
+  CUcontext context;  // the context the address belongs to
+  void* address;
+};
+StaticScratch g_static_scratch[kMaxDevices] = {};
+
+// cuCtxGetCurrent through the runtime's driver entry point (no link against libcuda)
+using CtxGetCurrent = CUresult (*)(CUcontext*);
+CUcontext current_context() {
+  static CtxGetCurrent fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrent>(p);
+  });
+  CUcontext ctx = nullptr;
+  if (!fn || fn(&ctx) != CUDA_SUCCESS) return nullptr;
+  return ctx;
+}
 }  // namespace
 
 extern "C" int flashns_b200_eval_static(const flashns_b200_plan* p, const double* coordinates,
@@ -3513,13 +3488,16 @@ extern "C" int flashns_b200_eval_static(const flashns_b200_plan* p, const double
   void* scratch = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_static_mutex);
-    if (!g_static_address[device]) {
+    StaticScratch& slot = g_static_scratch[device];
+    const CUcontext ctx = current_context();
+    if (!slot.address || !ctx || ctx != slot.context) {
       void* address = nullptr;
       e = cudaGetSymbolAddress(&address, g_static_workspace);
       if (e != cudaSuccess) return int(e);
-      g_static_address[device] = address;
+      slot.address = address;
+      slot.context = current_context();  // the lookup made the device's context current
     }
-    scratch = g_static_address[device];
+    scratch = slot.address;
   }
   return run_eval(p, coordinates, parameters, pde_weights, boundary_weights, target, gradient_and_loss, scratch,
                   size_t(FLASHNS_B200_STATIC_WORKSPACE_BYTES), stream, nullptr, 0, nullptr);
@@ -3604,25 +3582,3 @@ extern "C" int flashns_b200_fields(const flashns_b200_plan* p, const double* coo
   else fields_kernel<3, 0, FLASHNS_B200_HEAD_PSI><<<grid, kThreads, 0, stream>>>(h, ws + LL.w_buf, ws + LL.b_buf, cp, fields, p->points);
   return int(cudaGetLastError());
 }
-
-#ifdef FLASHNS_B200_STAMPS
-// Instrumented build only (no product entry point): attach a device buffer of
-// launches x ctas x 2 groups x kStampTiles x kStampPhases stamps (uint64, %globaltimer ns),
-// or detach with buf = nullptr.  Synchronous.
-extern "C" int flashns_b200_stamps_attach(unsigned long long* buf, long long ctas, int launches) {
-  using namespace flashns_b200;
-  if (buf && (ctas < 1 || launches < 1)) return int(cudaErrorInvalidValue);
-  const long long c = buf ? ctas : 0;
-  const int l = buf ? launches : 0, none = -1;
-  cudaError_t e = cudaMemcpyToSymbol(g_stamps, &buf, sizeof(buf));
-  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_stamp_ctas, &c, sizeof(c));
-  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_stamp_launches, &l, sizeof(l));
-  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_stamp_launch, &none, sizeof(none));
-  return int(e);
-}
-
-// stamps per launch slot for `ctas` CTAs
-extern "C" long long flashns_b200_stamps_per_launch(long long ctas) {
-  return ctas * 2 * flashns_b200::kStampTiles * flashns_b200::kStampPhases;
-}
-#endif

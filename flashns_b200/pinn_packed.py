@@ -6,17 +6,18 @@ evaluation (``flashns_b200_eval``) on the current CUDA stream.  Every ``layout``
 (dense / split / compact) and ``seed`` mode of the reference describes the same
 objective; all of them evaluate through the compact fused kernels.  The stage hooks
 (``activation_factory``, ``cuda_seed``, ``tail_dgrad_vjp``, ``coordinate_*``,
-``first_*``) are accepted for compatibility -- the fused kernels already contain every
-stage they replace -- and recorded in ``metadata``.  None of them is called; a hook that
-is not this library's own (``foreign_hooks``) draws a ``UserWarning`` so that a
-caller-defined stage or residual cannot be dropped silently.
+``first_*``) are accepted when they are this library's own (``TensorActivation``, the
+methods of ``flashns_b200.native``): the fused kernels already contain every stage they
+replace, so they are recorded in ``metadata`` and not called.  Any other hook -- a
+caller-defined stage or residual, or another library's kernels -- raises
+``NotImplementedError`` at construction, because the reference would call it
+(``src/flashns/pinn_packed.py:108-190``) and the fused kernels cannot.
 
 Extensions: ``head="psi"`` (stream-function net, outputs (psi, p)), 3-D coordinates
 (x, y, t) for the psi head, and ``boundary_order=1`` (first-order boundary rows with
 (u, v, p) targets).
 """
 
-import warnings
 from contextlib import nullcontext
 
 import torch
@@ -72,6 +73,18 @@ class PackedPINN:
                            ("coordinate_wgrad", coordinate_wgrad), ("first_activation_wgrad", first_activation_wgrad)):
             if hook is not None and not callable(hook):
                 raise ValueError(f"{name} must be callable or None")
+        # the reference calls residual_reference only for seed="autograd" and cuda_seed
+        # only for seed="cuda" (src/flashns/pinn_packed.py:136-146)
+        foreign = foreign_hooks(
+            activation_factory=activation_factory, cuda_seed=cuda_seed if seed == "cuda" else None,
+            residual_reference=residual_reference if seed == "autograd" else None, tail_dgrad_vjp=tail_dgrad_vjp,
+            coordinate_affine=coordinate_affine, first_affine_activation=first_affine_activation,
+            coordinate_wgrad=coordinate_wgrad, first_activation_wgrad=first_activation_wgrad)
+        if foreign:
+            raise NotImplementedError(
+                f"flashns_b200 PackedPINN evaluates every stage in its fused kernels and cannot call the "
+                f"supplied {', '.join(foreign)} hook(s); pass None (or this library's own hooks) to evaluate "
+                f"the NSLoss objective")
         if not x.is_cuda:
             raise ValueError("flashns_b200 evaluates on CUDA tensors (no CPU path)")
         self.ni, self.nb = interior_count, len(x) - interior_count
@@ -106,19 +119,13 @@ class PackedPINN:
             "first_affine_activation_enabled": first_affine_activation is not None,
             "coordinate_wgrad_enabled": coordinate_wgrad is not None,
             "first_activation_wgrad_enabled": first_activation_wgrad is not None,
+            "hooks_not_called": [name for name, hook in (
+                ("activation_factory", activation_factory), ("cuda_seed", cuda_seed),
+                ("residual_reference", residual_reference), ("tail_dgrad_vjp", tail_dgrad_vjp),
+                ("coordinate_affine", coordinate_affine), ("first_affine_activation", first_affine_activation),
+                ("coordinate_wgrad", coordinate_wgrad), ("first_activation_wgrad", first_activation_wgrad))
+                if hook is not None],
         }
-        # the reference calls residual_reference only for seed="autograd" and cuda_seed
-        # only for seed="cuda" (src/flashns/pinn_packed.py:136-146)
-        ignored = foreign_hooks(
-            activation_factory=activation_factory, cuda_seed=cuda_seed if seed == "cuda" else None,
-            residual_reference=residual_reference if seed == "autograd" else None, tail_dgrad_vjp=tail_dgrad_vjp,
-            coordinate_affine=coordinate_affine, first_affine_activation=first_affine_activation,
-            coordinate_wgrad=coordinate_wgrad, first_activation_wgrad=first_activation_wgrad)
-        self.metadata["hooks_not_called"] = ignored
-        if ignored:
-            warnings.warn(f"flashns_b200 PackedPINN evaluates every stage in its fused kernels; the supplied "
-                          f"{', '.join(ignored)} hook(s) are not called (the objective is NSLoss's)",
-                          stacklevel=2)
 
     def region(self, name):
         return torch.profiler.record_function("flashns_b200::" + name) if self.trace else nullcontext()

@@ -241,7 +241,7 @@ def reference_parameters(widths, seed=7510):
     return ws, bs
 
 
-# BASELINE configurations: (builder, interior, boundary, widths); ref16k is the reference's
+# benchmark configurations: (builder, interior, boundary, widths); ref16k is the reference's
 # own headline workload (its published H100 number: 1.832 ms per evaluation)
 CONFIGS = {
     "cfg0": dict(kind="kovasznay", interior=2048, boundary=512, widths=[2, 64, 64, 64, 64, 2]),

@@ -1,4 +1,4 @@
-"""Kovasznay time-to-accuracy solve.
+"""Kovasznay time-to-accuracy solve: the 2-64x4-2 stream-function net on 16,384 + 4,096 points.
 
 The reference's complete solve (experiments/pinn_solver/solve.py:77-167) replays a
 CUDA-graph-captured loss + gradient evaluation as the closure of an Adam phase and a
@@ -151,15 +151,16 @@ def solve(*, interior=16384, boundary=4096, widths=(2, 64, 64, 64, 64, 2), re=20
         metrics = accept(flat.data)
         phases["accept_s"] += time.perf_counter() - t_accept
         accepted = metrics[0] <= tol_uv and metrics[1] <= tol_uv and metrics[2] <= tol_p
-        decision.fill_(int(accepted or not all(math.isfinite(m) for m in metrics)))
+        # rank 0 decides whether to stop (accepted, diverged or out of time) and every rank
+        # follows, so all ranks leave the loop after the same closure evaluations
+        out_of_time = time_limit is not None and time.perf_counter() - start > time_limit
+        decision.fill_(int(accepted or out_of_time or not all(math.isfinite(m) for m in metrics)))
         if world > 1:
             dist.broadcast(decision, 0)
         if log and rank == 0:
             log(json.dumps({"t": round(time.perf_counter() - start, 3), "iter": iterations, "evals": evaluations[0],
                             "loss": float(loss_view), "rel_l2_uvp": metrics}))
         if int(decision):
-            break
-        if time_limit is not None and time.perf_counter() - start > time_limit:
             break
     torch.cuda.synchronize(device)
     wall = time.perf_counter() - start
@@ -212,7 +213,7 @@ def main():
                                 "sampling": args.sampling},
                     "protocol": {k: getattr(args, k) for k in ("adam_steps", "history", "check_every",
                                                                "boundary_weight", "max_iterations")},
-                    "seed": args.seed, "init_seed": args.init_seed}
+                    "seed": args.seed, "init_seed": args.init_seed, "backend": "flashns_b200"}
             result["checkpoint_sha256"] = save_checkpoint(args.output.with_suffix(".pt"), final, meta)
             args.output.with_suffix(".json").write_text(json.dumps(result, indent=1) + "\n")
         print(json.dumps(result), flush=True)

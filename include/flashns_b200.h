@@ -112,7 +112,8 @@ int flashns_b200_fields(const flashns_b200_plan* plan, const double* coordinates
  * FLASHNS_B200_STATIC_WORKSPACE_BYTES (64 MiB) that every GPU loading the library keeps
  * until exit; plans needing more workspace are rejected with cudaErrorInvalidValue.  The
  * first call on a device looks up the array's address and should come before any stream
- * capture.  All calls share the array: calls that overlap on the GPU race. */
+ * capture; a call that finds another context current (after cudaDeviceReset) looks it up
+ * again.  All calls share the array: calls that overlap on the GPU race. */
 #define FLASHNS_B200_STATIC_WORKSPACE_BYTES (64u * 1024u * 1024u)
 int flashns_b200_eval_static(const flashns_b200_plan* plan, const double* coordinates, const double* parameters,
                              const double* pde_weights, const double* boundary_weights, const double* target,

@@ -1,6 +1,6 @@
 """Timed CPU baseline: the oracle port of ``PackedPINN`` on all host cores.
 
-TEST / BASELINE INFRASTRUCTURE ONLY (see ``oracle/__init__.py``): used by the
+TEST AND CPU-BASELINE INFRASTRUCTURE ONLY (see ``oracle/__init__.py``): used by the
 ``cpu_baseline`` and ``--impl reference`` legs of ``bench.py``.  Points are
 independent, so a sample of the point set is split over a ``spawn`` process pool
 (one single-threaded NumPy worker per core); the chunk losses and gradients are

@@ -68,6 +68,7 @@ def test_against_oracle(cuda, head, order, widths, ni, nb):
     _, out = run(case, list(widths), head, order, loss, cuda)
     expected = oracle(case, head, order, loss)
     assert close_ratio(out, expected) <= 1.0, (close_ratio(out, expected), rel_norm(out, expected))
+    assert rel_norm(out, expected) <= 1e-10, rel_norm(out, expected)
 
 
 def test_empty_point_set(cuda):

@@ -5,6 +5,7 @@ import math
 
 import numpy as np
 import pytest
+import torch
 
 from flashns_b200.distributed_contract import global_normalization, parameter_count, shard_bounds
 from flashns_b200.jet_spec import JetSpec
@@ -172,7 +173,7 @@ def test_jet_multiply_and_manifest():
 def test_foreign_stage_hooks_are_named():
     """PackedPINN calls no stage hook (its fused kernels contain the stages); this
     library's own hooks are recognized, any other callable is reported so the drop-in
-    can warn instead of dropping a caller-defined stage silently."""
+    can refuse it instead of dropping a caller-defined stage silently."""
     from flashns_b200.jet_packed import TensorActivation
     from flashns_b200.native import Native, NativeCUDA
     from flashns_b200.ns_seed import per_point_loss
@@ -194,6 +195,25 @@ def test_foreign_stage_hooks_are_named():
         "coordinate_affine", "cuda_seed"]
 
 
+def test_packed_pinn_refuses_a_foreign_residual_before_any_device_work():
+    """A caller-defined residual (seed="autograd") or CUDA seed (seed="cuda") is what the
+    reference would call (src/flashns/pinn_packed.py:136-146); the drop-in raises
+    NotImplementedError at construction, on any device, rather than ignore it."""
+    from flashns_b200.pinn_packed import PackedPINN
+    x = torch.zeros(3, 2, dtype=torch.float64)
+    args = (x, 2, torch.full((2,), 0.5, dtype=torch.float64), torch.ones(1, 3, dtype=torch.float64),
+            torch.zeros(1, 3, dtype=torch.float64))
+    mine = lambda *a, **k: None
+    with pytest.raises(NotImplementedError, match="residual_reference"):
+        PackedPINN(*args, seed="autograd", residual_reference=mine)
+    with pytest.raises(NotImplementedError, match="cuda_seed"):
+        PackedPINN(*args, seed="cuda", cuda_seed=mine)
+    with pytest.raises(NotImplementedError, match="activation_factory"):
+        PackedPINN(*args, activation_factory=mine)
+    with pytest.raises(ValueError, match="CUDA tensors"):  # no foreign hook: the CPU tensors are refused
+        PackedPINN(*args, seed="autograd", residual_reference=None)
+
+
 def test_compulsory_bytes_per_kernel_match_the_cfg1_profile():
     """The per-launch DRAM model reproduces the compulsory figures of the cfg1 kernels
     (backward 281 MB, forward 191 MB, fused head 180 MB of seeds and checkpoints) and
@@ -213,38 +233,3 @@ def test_compulsory_bytes_per_kernel_match_the_cfg1_profile():
     r = kernel_rooflines(times, flops, b, 37.1, 6552.6)
     assert 25 < r["backward"]["tflops"] < 27 and abs(r["backward"]["fp64_frac"] - r["backward"]["tflops"] / 37.1) < 1e-12
     assert 2000 < r["backward"]["gbs"] < 2500 and r["reduce"] == {"avg_ms": 0.0101}
-
-
-def test_stamp_summary_of_two_groups():
-    """Phase durations and the MMA share of a CTA's span from synthetic stamps
-    (flashns_b200.stamps.summarize; %globaltimer ns)."""
-    from flashns_b200.stamps import PHASES, TILES, summarize
-    st = np.zeros((2, 1, 2, TILES, PHASES), dtype=np.int64)
-    st[0, 0, 0, 0] = (1000, 2000, 4000, 7000, 12000)     # backward: wait 1, dgrad 2, wgrad 3, epilogue 5 us
-    st[0, 0, 1, 0] = (1000, 7000, 9000, 12000, 15000)    # waits 6 us for the turn
-    st[1, 0, 0, 0, :4] = (0, 0, 0, 0)                    # a launch without stamps is skipped
-    rows = summarize(st, ["backward", "reduce"])
-    assert len(rows) == 1 and rows[0]["half_tiles"] == 2
-    us = rows[0]["us"]
-    assert us["wait"] == 3.5 and us["dgrad"] == 2.0 and us["wait H + wgrad"] == 3.0 and us["epilogue"] == 4.0
-    assert abs(rows[0]["mma_share_of_cta_span"] - (5000 + 5000) / 14000) < 1e-12
-    fw = np.zeros((1, 1, 2, TILES, PHASES), dtype=np.int64)
-    fw[0, 0, 0, 0, :4] = (0 + 5, 1005, 3005, 6005)
-    rows = summarize(fw, ["forward"])
-    assert rows[0]["us"] == {"wait": 1.0, "mainloop": 2.0, "epilogue": 3.0}
-    assert abs(rows[0]["mma_share_of_cta_span"] - 2 / 6) < 1e-12
-
-
-def test_instrumented_variant_compiles():
-    """The stamp hooks of the instrumented build (FLASHNS_B200_STAMPS) compile; in the
-    product build they expand to nothing."""
-    import subprocess
-
-    from flashns_b200 import build
-    obj = build.ROOT / "flashns_b200" / "_build_stamps" / "eval_check.o"
-    obj.parent.mkdir(exist_ok=True)
-    cmd = [build.nvcc(), *build.ARCH, *build.FLAGS, "-DFLASHNS_B200_STAMPS", "-c",
-           str(build.CSRC / "eval.cu"), "-o", str(obj)]
-    result = subprocess.run(cmd, capture_output=True, text=True)
-    assert result.returncode == 0, result.stderr[-2000:]
-    obj.unlink()

@@ -31,23 +31,22 @@ def test_point_set_fixed_at_construction(cuda):
                 p.add_(g, alpha=-1e-3)
 
 
-def test_caller_defined_hooks_draw_a_warning(cuda):
-    """A stage hook that is not this library's own is not called by the fused drop-in;
-    construction says so instead of dropping it silently.  Its own hooks stay quiet."""
-    import warnings
-
+def test_caller_defined_hooks_are_refused(cuda):
+    """A stage hook that is not this library's own cannot be called by the fused drop-in;
+    construction refuses it instead of dropping it silently.  Its own hooks are accepted
+    (the fused kernels contain their stages) and recorded as not called."""
     from flashns_b200.native import NativeCUDA
     from flashns_b200.pinn_packed import PackedPINN
     c = random_case(5, 2, [2, 6, 3], seed=3)
     t = lambda a: torch.tensor(np.asarray(a), dtype=torch.float64, device=cuda)
     args = (t(c["x"]), 5, t(c["pw"]), t(c["bw"]), t(c["target"]))
-    with pytest.warns(UserWarning, match="coordinate_affine"):
-        step = PackedPINN(*args, coordinate_affine=lambda *a: None)
-    assert step.metadata["hooks_not_called"] == ["coordinate_affine"]
+    with pytest.raises(NotImplementedError, match="coordinate_affine"):
+        PackedPINN(*args, coordinate_affine=lambda *a: None)
+    with pytest.raises(NotImplementedError, match="residual_reference"):
+        PackedPINN(*args, seed="autograd", residual_reference=lambda *a: None)
     nat = NativeCUDA()
-    with warnings.catch_warnings(record=True) as seen:
-        warnings.simplefilter("always")
-        quiet = PackedPINN(*args, seed="cuda", activation_factory=nat.activation_factory, cuda_seed=nat.seed,
-                           tail_dgrad_vjp=nat.tail_dgrad_vjp)
-    assert quiet.metadata["hooks_not_called"] == []
-    assert not [w for w in seen if "hook" in str(w.message)]
+    quiet = PackedPINN(*args, seed="cuda", activation_factory=nat.activation_factory, cuda_seed=nat.seed,
+                       tail_dgrad_vjp=nat.tail_dgrad_vjp)
+    assert quiet.metadata["hooks_not_called"] == ["activation_factory", "cuda_seed", "tail_dgrad_vjp"]
+    loss, grads = quiet([t(w) for w in c["ws"]], [t(b) for b in c["bs"]])
+    assert torch.isfinite(loss) and len(grads) == 4
