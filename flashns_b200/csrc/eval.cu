@@ -22,6 +22,7 @@
 #include <cuda.h>
 #include <mutex>
 #include <new>
+#include <type_traits>
 #include <vector>
 
 #include "common.cuh"
@@ -2107,20 +2108,72 @@ __global__ void __launch_bounds__(HeadTile<DIM>::THREADS, HeadTile<DIM>::MINB)
 // Two-group ("ping-pong") form of fwd_head for 2-D: the last hidden layer, the output
 // layer, the residual seeds, the output-layer gradients and the VJP into layer L, with the
 // CTA's 16 warps in two 8-warp groups that take turns on the tensor pipe as in
-// bwd_pingpong.  Each group has its own input planes (TMA, rows in global order), H_L
-// tile, Y and dY; W_{L-1} and W_L are shared.  A group's mainloop runs while it holds the
-// turn; its whole epilogue (jet, output contraction, seeds, output gradients, VJP and the
-// stores of D_L) overlaps the other group's mainloop.
-template <int NF>
-constexpr size_t hpp_group_doubles() {
-  return size_t(kFusedWidth / KC) * PPTile::TR * LDC + size_t(PPTile::TR) * (kFusedWidth + 4) +
-         2 * size_t(PPTile::TR) * NF;
-}
-template <int NF>
+// bwd_pingpong.  Each group has its own input planes (TMA, rows in global order); W_{L-1}
+// and W_L are shared.  A group's mainloop runs while it holds the turn; its whole epilogue
+// overlaps the other group's mainloop.
+//
+// The epilogue keeps everything of a half tile in registers.  A thread owns one thread
+// column (one interior point, or PS boundary points) and two channels, so after the jet it
+// holds H_L of its channels at every slot of its points.  The outputs Y = H_L W_L^T + b_L
+// are sums over the 64 channels: each thread forms the partial over its two channels for
+// the output values the residual seed reads (HeadOutputs), the 8 lanes of a warp that
+// share a thread column reduce them with a three-step shuffle butterfly that leaves each
+// lane a disjoint eighth (reduce-scatter), and the 4 channel warps of a row group add
+// their eighths through shared memory in fixed order, after one 128-thread barrier.
+// Every thread of a point then has its outputs, forms the seed itself (the seed formulas
+// are a few dozen flops), accumulates dW_L = dY^T H_L for its channels, contracts
+// dH_L = dY W_L and runs the jet VJP.  Per half tile that is one sub-group barrier and
+// about 70 FP64 operations per thread beyond the jet and its VJP, instead of staging
+// H_L, Y and dY in shared memory around output-layer MMAs of which 14 of 16 rows are zero.
+//
+// Output values a head's residual seed reads (and seeds), as flat indices s * NF + f (slot
+// s of a point, output f).  Interior points: the inputs of the generated seed formulas
+// (residual_generated.cuh; tests/test_codegen.py checks the lists against that file).
+// Boundary points with first-order rows (psi head): (psi_y, psi_x, p) per point, the slots
+// of u = psi_y, v = -psi_x and p; with value rows: every output of every point.
+template <int HEAD, int BO>
+struct HeadOutputs {
+  static constexpr int NF = HeadTraits<HEAD>::NF;
+  static constexpr int Q = Basis<2>::Q, QB = BO ? 3 : 1, PS = Q / QB;
+  static_assert(!(BO && HEAD == FLASHNS_B200_HEAD_UVP), "first-order boundary rows carry the psi head");
+  static constexpr int NI = HEAD == FLASHNS_B200_HEAD_PSI ? 11 : 25;
+  static constexpr int NB = BO ? 3 * PS : PS * NF;
+  static constexpr int round8(int n) { return (n + 7) / 8 * 8; }
+  static constexpr int LDP = (round8(NI) > round8(NB) ? round8(NI) : round8(NB)) + 1;  // odd: conflict-free reads
+  // The (u, v, p) seed holds 25 outputs and 25 seeds at once; with H_L as well a thread
+  // would need more than its 128 registers, so that head keeps H_L in the thread's own
+  // shared-memory slots between the jet and the VJP (no other thread reads them).
+  static constexpr bool STASH = HEAD == FLASHNS_B200_HEAD_UVP;
+  __host__ __device__ static constexpr int interior(int k) {
+    if constexpr (HEAD == FLASHNS_B200_HEAD_PSI) {
+      constexpr int v[11] = {2, 3, 4, 5, 6, 8, 10, 12, 14, 16, 18};
+      return v[k];
+    } else {
+      constexpr int v[25] = {0, 1, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15, 16, 17, 18, 19, 21, 22, 24, 25, 27, 28};
+      return v[k];
+    }
+  }
+  __host__ __device__ static constexpr int boundary(int k) {
+    if constexpr (BO) {
+      const int kq = k / 3, j = k % 3;  // j: psi_y, psi_x, p of point kq
+      return j == 0 ? (kq * QB + unit_row<2>(1)) * NF : j == 1 ? (kq * QB + unit_row<2>(0)) * NF : kq * QB * NF + 1;
+    } else {
+      return k;  // point k / NF, output k % NF
+    }
+  }
+};
+
+template <int BO, int HEAD>
 constexpr size_t hpp_smem_bytes() {
-  return sizeof(double) * (kPPGroups * hpp_group_doubles<NF>() + size_t(kFusedWidth) * (kFusedWidth + 4) +
-                           size_t(NF) * kFusedWidth + kPPGroups);
+  using HO = HeadOutputs<HEAD, BO>;
+  constexpr size_t planes = size_t(kFusedWidth / KC) * PPTile::TR * LDC;  // one group's input half tile
+  constexpr size_t parts = size_t(kPPGroups) * PPTile::WR * 4 * PPTile::WC * HO::LDP;
+  constexpr size_t lead = size_t(kPPGroups) * PPTile::WR * 4 * (HO::NF + 1);
+  constexpr size_t stash = HO::STASH ? size_t(2) * PPTile::S * kPPThreads : 0;
+  return sizeof(double) * (kPPGroups * planes + size_t(kFusedWidth) * (kFusedWidth + 4) +
+                           size_t(HO::NF) * (kFusedWidth + 1) + parts + lead + stash + kPPGroups);
 }
+enum { kPPBarRows = 5 };  // named barriers 5 + group * 2 + row group: the 4 channel warps (128 threads)
 
 template <int BO, int HEAD>
 __global__ void __launch_bounds__(kPPThreads, 1)
@@ -2132,19 +2185,22 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   constexpr int DIM = 2, CP = kFusedWidth;
   using T = PPTile;
   using TL = Tiles<DIM, BO, T::TC>;
+  using HO = HeadOutputs<HEAD, BO>;
   constexpr int S = T::S, TR = T::TR, Q = TL::Q, QB = TL::QB, PS = TL::PS;
-  constexpr int NF = HeadTraits<HEAD>::NF;
+  constexpr int NF = HO::NF;
   constexpr int NFT = (HEAD == FLASHNS_B200_HEAD_PSI && BO) ? 3 : NF;  // boundary target fields
-  constexpr int LDA = CP + 4, LDH = CP + 4;
+  constexpr int LDA = CP + 4, LDP = HO::LDP;
   constexpr int PARTIAL = NF * CP + NF + 1 + CP;  // dW_L | db_L | loss | db_{L-1}
   constexpr int NK = CP / KC;
   constexpr int BB = pp_boundary_box_rows<BO>();
   constexpr bool SPLIT = BB != TR;
   constexpr int GT = T::THREADS;
   constexpr int PLANES = NK * TR * LDC;
-  static_assert(T::NWARPS == CP / 8 && NF <= 8, "warp w of a group owns output-gradient columns 8w..8w+7");
+  constexpr bool STASH = HO::STASH;
+  static_assert(T::WC == 4 && T::WR == 2 && T::TC == 8, "4 channel warps x 2 row groups of 4 thread columns");
   static_assert(NK == 2 && KC == 32 && TR <= 256, "TMA boxes: 36 columns, at most 256 rows");
-  static_assert((hpp_group_doubles<NF>() * sizeof(double)) % 128 == 0, "group buffers on 128-byte boundaries");
+  static_assert((size_t(PLANES) * sizeof(double)) % 128 == 0, "group planes on 128-byte boundaries");
+  static_assert(PS * QB <= S && HO::NI <= Q * NF, "slots of a thread column");
   extern __shared__ __align__(128) double smem[];
   if (smem_u32(smem) & 127) {  // TMA destinations need 128-byte alignment: refuse, never fault
     if (threadIdx.x == 0) atomicExch(&g_device_fault, 2);
@@ -2153,15 +2209,17 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int gp = warp / T::NWARPS, lw = warp % T::NWARPS, gtid = tid % GT;
   const int wc = lw % T::WC, wr = lw / T::WC;
-  double* sB = smem + gp * hpp_group_doubles<NF>();  // this group's input planes [NK][TR][LDC]
-  double* sH = sB + PLANES;                          // H_L tile [TR][CP+4], rows in tile order
-  double* sY = sH + TR * LDH;                        // Y  [TR][NF]
-  double* sD = sY + TR * NF;                         // dY [TR][NF]
-  double* sA = smem + kPPGroups * hpp_group_doubles<NF>();  // W_{L-1} [CP][CP+4], shared
-  double* sW = sA + CP * LDA;                                // W_L [NF][CP], shared
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sW + NF * CP);
+  double* sB = smem + gp * PLANES;            // this group's input planes [NK][TR][LDC]
+  double* sA = smem + kPPGroups * PLANES;     // W_{L-1} [CP][CP+4], shared
+  double* sW = sA + CP * LDA;                 // W_L [NF][CP], then b_L [NF]
+  double* sP = sW + NF * CP + NF;             // output partials [group][row group][thread column][wc][LDP]
+  double* sL = sP + kPPGroups * T::WR * 4 * T::WC * LDP;  // per lead thread: loss, db_L [NF]
+  double* sHs = sL + kPPGroups * T::WR * 4 * (NF + 1);     // STASH: H_L [2][S][threads]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sHs + (STASH ? 2 * S * kPPThreads : 0));
   uint64_t* bar_in = bars + gp;
   const int bar_group = kPPBarGroup + gp;
+  const int bar_rows = kPPBarRows + gp * T::WR + wr;
+  double* part = sP + ((gp * T::WR + wr) * 4 + t) * T::WC * LDP;  // this thread column's partials
   const int64_t nint = TL::interior(geo.ni);
   const int64_t nht = nint + TL::boundary(geo.nb);
   const int64_t mine = int64_t(blockIdx.x) < nht ? (nht - 1 - blockIdx.x) / gridDim.x + 1 : 0;
@@ -2201,24 +2259,34 @@ __global__ void __launch_bounds__(kPPThreads, 1)
     ph ^= 1u;
     return ok;
   };
-  double bias_r[2];  // a thread's channels are fixed for the whole kernel
+  // a thread's channels are fixed for the whole kernel: their W_L columns
+  double wl[NF][2];
 #pragma unroll
-  for (int hh = 0; hh < 2; ++hh) bias_r[hh] = bias[wc * T::WCH + 8 * hh + g];
+  for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+    for (int o = 0; o < NF; ++o) wl[o][hh] = wL[o * CP + wc * T::WCH + 8 * hh + g];
   for (int i = tid; i < CP * (CP / 2); i += kPPThreads) {  // W_{L-1}, resident
     const int r = i / (CP / 2), p = i % (CP / 2);
     cp_async16(sA + r * LDA + 2 * p, w + int64_t(r) * CP + 2 * p, true);
   }
   cp_async_commit();
   for (int i = tid; i < NF * CP; i += kPPThreads) sW[i] = wL[i];
+  if (tid < NF) sW[NF * CP + tid] = bL[tid];
+  if (tid < kPPGroups * T::WR * 4 * (NF + 1)) sL[tid] = 0.0;
   if (tid == 0)
     for (int b = 0; b < kPPGroups; ++b) mbar_init(&bars[b], 1);
   cp_async_wait<0>();
-  __syncthreads();  // W_{L-1}, W_L and the barriers visible
+  __syncthreads();  // W_{L-1}, W_L, b_L, the loss slots and the barriers visible
   pdl_wait();  // H_{L-1} is the predecessor's output
   pdl_trigger();
   if (nmy > 0) load_tile(tile_of(0));
-  double wacc[4] = {0.0, 0.0, 0.0, 0.0};  // dW_L[g][8 lw + 2t (+1)] (rows g < NF)
-  double bacc = 0.0, lacc = 0.0, cacc[2] = {0.0, 0.0};
+  double wacc[NF][2], cacc[2] = {0.0, 0.0};
+#pragma unroll
+  for (int o = 0; o < NF; ++o) wacc[o][0] = wacc[o][1] = 0.0;
+  // the one thread of a thread column that books its points' loss and db_L, in its own
+  // shared-memory slot (no other thread touches it until the end of the kernel)
+  const bool lead = wc == 0 && g == 0;
+  double* lslot = sL + ((gp * T::WR + wr) * 4 + t) * (NF + 1);
   bool dead = false;
   // B fragments: column g of an n8 tile is slot 2j + (g & 1) of thread column wr*4 + (g >> 1)
   const int brow = (wr * 4 + (g >> 1)) * S + (g & 1);
@@ -2253,141 +2321,165 @@ __global__ void __launch_bounds__(kPPThreads, 1)
     named_arrive(kPPBarTurn + (1 - gp), kPPThreads);  // the other group's turn
     named_sync(bar_group, GT);                         // this group's input planes free
     if (k + 1 < nmy && !dead) load_tile(tile_of(k + 1));
-    if (!dead) {
-      const int tc = wr * 4 + t;
-      const bool interior = tile < nint;
-      const int64_t p0 = interior ? tile * T::TC : (tile - nint) * (int64_t(T::TC) * PS);
-      const int64_t left = interior ? geo.ni - p0 : geo.nb - p0;
-      const int npts = int(left < (interior ? T::TC : T::TC * PS) ? left : (interior ? T::TC : T::TC * PS));
-      const int step = interior ? Q : QB;
-      const int nrows = npts * step;
-      // 1. bias on the order-0 coefficient, stable tanh jet; H_L into the shared tile
-      double a1r[2][PS];
+    if (dead) continue;
+    const int tc = wr * 4 + t;
+    const bool interior = tile < nint;
+    const int64_t p0 = interior ? tile * T::TC : (tile - nint) * (int64_t(T::TC) * PS);
+    const int64_t left = interior ? geo.ni - p0 : geo.nb - p0;
+    const int cap = interior ? T::TC : T::TC * PS;
+    const int npts = int(left < cap ? left : cap);
+    // 1. bias on the order-0 coefficient and the stable tanh jet: H_L of this thread's two
+    //    channels at every slot of its points, in registers (zero at slots without a point)
+    double hv[2][S], a1r[2][PS];
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int ch = wc * T::WCH + 8 * hh + g;
-        double z[S];
+    for (int hh = 0; hh < 2; ++hh) {
+      double z[S];
 #pragma unroll
-        for (int s = 0; s < S; ++s) z[s] = acc[s >> 1][2 * hh + (s & 1)];
-        if (interior) {
-          if (tc < npts) {
-            double hv[Q];
-            z[0] += bias_r[hh];
-            Jet<DIM, 3>::fwd(z, hv, a1r[hh][0]);
-#pragma unroll
-            for (int s = 0; s < Q; ++s) sH[(tc * Q + s) * LDH + ch] = hv[s];
-          } else {  // rows of points past the segment stay finite for the row contractions
-#pragma unroll
-            for (int s = 0; s < Q; ++s) sH[(tc * Q + s) * LDH + ch] = 0.0;
-          }
-        } else {
-#pragma unroll
-          for (int kq = 0; kq < PS; ++kq) {
-            const int lp = tc * PS + kq;
-            if (lp < npts) {
-              double zz[QB], hv[QB];
-#pragma unroll
-              for (int c = 0; c < QB; ++c) zz[c] = z[kq * QB + c];
-              zz[0] += bias_r[hh];
-              Jet<DIM, BO ? 1 : 0>::fwd(zz, hv, a1r[hh][kq]);
-#pragma unroll
-              for (int c = 0; c < QB; ++c) sH[(lp * QB + c) * LDH + ch] = hv[c];
-            } else {
-#pragma unroll
-              for (int c = 0; c < QB; ++c) sH[(lp * QB + c) * LDH + ch] = 0.0;
-            }
-          }
-        }
+      for (int s = 0; s < S; ++s) {
+        z[s] = acc[s >> 1][2 * hh + (s & 1)];
+        hv[hh][s] = 0.0;
       }
-      named_sync(bar_group, GT);
-      // 2. outputs Y^T[o][r] = W_L[o] . H[r] (+ b_L on order-0 rows) as DMMA tiles:
-      //    M = outputs (rows >= NF zero), N = tile rows (n8 tile j per warp), K = channels
-      const int kend = (nrows + 7) & ~7;
-      for (int j = lw; j < kend / 8; j += T::NWARPS) {
-        double c[4] = {0.0, 0.0, 0.0, 0.0};
 #pragma unroll
-        for (int kk = 0; kk < CP; kk += 8) {
-          const double a[4] = {g < NF ? sW[g * CP + kk + t] : 0.0, 0.0, g < NF ? sW[g * CP + kk + t + 4] : 0.0, 0.0};
-          mma_m16n8k8(c, a, sH[(8 * j + g) * LDH + kk + t], sH[(8 * j + g) * LDH + kk + t + 4]);
-        }
-        if (g < NF) {
-          const int r0 = 8 * j + 2 * t;
-          if (r0 < nrows) sY[r0 * NF + g] = c[0] + (r0 % step == 0 ? bL[g] : 0.0);
-          if (r0 + 1 < nrows) sY[(r0 + 1) * NF + g] = c[1] + ((r0 + 1) % step == 0 ? bL[g] : 0.0);
-        }
-      }
-      named_sync(bar_group, GT);
-      // 3. residual seeds, one point per thread (dY rows up to the next multiple of 8 zeroed)
-      for (int i = gtid; i < (kend - nrows) * NF; i += GT) sD[nrows * NF + i] = 0.0;
+      for (int kq = 0; kq < PS; ++kq) a1r[hh][kq] = 0.0;
       if (interior) {
-        if (gtid < npts) {
-          double y[Q * NF], dy[Q * NF];
-#pragma unroll
-          for (int k = 0; k < Q * NF; ++k) y[k] = sY[gtid * Q * NF + k];
-          lacc += interior_seed<DIM, HEAD>(y, pde_w[p0 + gtid], nu, gamma, dy);
-#pragma unroll
-          for (int k = 0; k < Q * NF; ++k) sD[gtid * Q * NF + k] = dy[k];
+        if (tc < npts) {
+          z[0] += bias[wc * T::WCH + 8 * hh + g];
+          Jet<DIM, 3>::fwd(z, hv[hh], a1r[hh][0]);
         }
       } else {
-        for (int pt = gtid; pt < npts; pt += GT) {
-          const int64_t b = p0 + pt;
-          const double* yr = sY + pt * QB * NF;
-          double* dr = sD + pt * QB * NF;
 #pragma unroll
-          for (int k = 0; k < QB * NF; ++k) dr[k] = 0.0;
+        for (int kq = 0; kq < PS; ++kq) {
+          if (tc * PS + kq < npts) {
+            double zz[QB];
+#pragma unroll
+            for (int c = 0; c < QB; ++c) zz[c] = z[kq * QB + c];
+            zz[0] += bias[wc * T::WCH + 8 * hh + g];
+            Jet<DIM, BO ? 1 : 0>::fwd(zz, hv[hh] + kq * QB, a1r[hh][kq]);
+          }
+        }
+      }
+      if constexpr (STASH) {
+#pragma unroll
+        for (int s = 0; s < S; ++s) sHs[(hh * S + s) * kPPThreads + tid] = hv[hh][s];
+      }
+    }
+    // H_L of this thread: registers, or the thread's own shared-memory slots (STASH)
+    auto hval = [&](int hh, int s) {
+      if constexpr (STASH) return sHs[(hh * S + s) * kPPThreads + tid];
+      else return hv[hh][s];
+    };
+    // 2-4. outputs, seeds, output-layer gradients, dgrad through W_L, VJP: per tile kind
+    auto finish = [&](auto kind) {
+      constexpr bool INTERIOR = decltype(kind)::value;
+      constexpr int NY = INTERIOR ? HO::NI : HO::NB;
+      constexpr int NYP = (NY + 7) / 8 * 8, H1 = NYP / 2, H2 = NYP / 4, H3 = NYP / 8;
+      constexpr int STEP = INTERIOR ? Q : QB;  // rows per point: b_L on every STEP-th slot
+      auto index = [](int k) { return INTERIOR ? HO::interior(k) : HO::boundary(k); };
+      // this thread's two channels' share of output value k (zero past NY)
+      auto share = [&](int k) {
+        if (k >= NY) return 0.0;
+        const int s = index(k) / NF, o = index(k) % NF;
+        return hval(0, s) * wl[o][0] + hval(1, s) * wl[o][1];
+      };
+      // reduce-scatter over the 8 lanes of this thread column (g = lane >> 2): after the
+      // steps over lane bits 4, 3, 2 lane g holds the sums of values [g*H3, g*H3 + H3)
+      double v1[H1], v2[H2], v3[H3];
+      const bool u4 = lane & 16, u3 = lane & 8, u2 = lane & 4;
+#pragma unroll
+      for (int i = 0; i < H1; ++i) {
+        const double lo = share(i), hi = share(H1 + i);
+        const double keep = u4 ? hi : lo, send = u4 ? lo : hi;
+        v1[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+      }
+#pragma unroll
+      for (int i = 0; i < H2; ++i) {
+        const double keep = u3 ? v1[H2 + i] : v1[i], send = u3 ? v1[i] : v1[H2 + i];
+        v2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+      }
+#pragma unroll
+      for (int i = 0; i < H3; ++i) {
+        const double keep = u2 ? v2[H3 + i] : v2[i], send = u2 ? v2[i] : v2[H3 + i];
+        v3[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+      }
+#pragma unroll
+      for (int i = 0; i < H3; ++i) part[wc * LDP + g * H3 + i] = v3[i];
+      named_sync(bar_rows, 4 * 32);  // the 4 channel warps of this row group
+      double y[NY];
+#pragma unroll
+      for (int k = 0; k < NY; ++k) {
+        y[k] = ((part[k] + part[LDP + k]) + part[2 * LDP + k]) + part[3 * LDP + k];
+        if ((index(k) / NF) % STEP == 0) y[k] += sW[NF * CP + index(k) % NF];
+      }
+      // residual seeds of this thread column's points (every thread of the column forms them)
+      double dy[NY];
+      if constexpr (INTERIOR) {
+        double yv[Q * NF], dyv[Q * NF];
+#pragma unroll
+        for (int i = 0; i < Q * NF; ++i) yv[i] = 0.0;
+#pragma unroll
+        for (int kk = 0; kk < NY; ++kk) yv[index(kk)] = y[kk];
+        const bool valid = tc < npts;
+        const double l = interior_seed<DIM, HEAD>(yv, valid ? pde_w[p0 + tc] : 0.0, nu, gamma, dyv);
+        if (valid && lead) lslot[0] += l;
+#pragma unroll
+        for (int kk = 0; kk < NY; ++kk) dy[kk] = valid ? dyv[index(kk)] : 0.0;
+      } else {
+        constexpr int PER = NY / PS;  // output values per boundary point
+#pragma unroll
+        for (int kq = 0; kq < PS; ++kq) {
+          const int64_t b = p0 + tc * PS + kq;
+          const bool valid = tc * PS + kq < npts;
           double f[NFT];
           if constexpr (BO == 0) {
 #pragma unroll
-            for (int o = 0; o < NF; ++o) f[o] = yr[o];
+            for (int o = 0; o < NF; ++o) f[o] = y[kq * PER + o];
           } else {
-            f[0] = yr[unit_row<DIM>(1) * NF + 0];   // u = psi_y
-            f[1] = -yr[unit_row<DIM>(0) * NF + 0];  // v = -psi_x
-            f[2] = yr[1];                           // p
+            f[0] = y[kq * PER + 0];   // u = psi_y
+            f[1] = -y[kq * PER + 1];  // v = -psi_x
+            f[2] = y[kq * PER + 2];   // p
           }
           double gsd[NFT];
 #pragma unroll
           for (int o = 0; o < NFT; ++o) {
-            const double err = f[o] - target[b * NFT + o];
-            const double wgt = bnd_w[b * NFT + o];
-            lacc += bc * wgt * err * err;
+            const double err = valid ? f[o] - target[b * NFT + o] : 0.0;
+            const double wgt = valid ? bnd_w[b * NFT + o] : 0.0;
+            if (valid && lead) lslot[0] += bc * wgt * err * err;
             gsd[o] = 2.0 * bc * wgt * err;
           }
           if constexpr (BO == 0) {
 #pragma unroll
-            for (int o = 0; o < NF; ++o) dr[o] = gsd[o];
+            for (int o = 0; o < NF; ++o) dy[kq * PER + o] = gsd[o];
           } else {
-            dr[unit_row<DIM>(1) * NF + 0] = gsd[0];
-            dr[unit_row<DIM>(0) * NF + 0] = -gsd[1];
-            dr[1] = gsd[2];
+            dy[kq * PER + 0] = gsd[0];
+            dy[kq * PER + 1] = -gsd[1];
+            dy[kq * PER + 2] = gsd[2];
           }
         }
       }
-      named_sync(bar_group, GT);
-      // 4. output-layer gradients dW_L[o][c] += sum_r dY[r][o] H[r][c] as DMMA tiles (M =
-      //    outputs, N = channels 8 lw.., K = tile rows); db_L over order-0 rows
-      for (int k0 = 0; k0 < kend; k0 += 8) {
-        const double a[4] = {g < NF ? sD[(k0 + t) * NF + g] : 0.0, 0.0, g < NF ? sD[(k0 + t + 4) * NF + g] : 0.0, 0.0};
-        mma_m16n8k8(wacc, a, sH[(k0 + t) * LDH + 8 * lw + g], sH[(k0 + t + 4) * LDH + 8 * lw + g]);
+      // output-layer gradients: dW_L[o][ch] += dY[s][o] H_L[s][ch] over this column's
+      // slots; db_L[o] over its points' order-0 rows (once per column)
+#pragma unroll
+      for (int kk = 0; kk < NY; ++kk) {
+        const int s = index(kk) / NF, o = index(kk) % NF;
+        wacc[o][0] += dy[kk] * hval(0, s);
+        wacc[o][1] += dy[kk] * hval(1, s);
+        if (s % STEP == 0 && lead) lslot[1 + o] += dy[kk];
       }
-      if (gtid < NF)
-        for (int r = 0; r < nrows; r += step) bacc += sD[r * NF + gtid];
-      // 5. dgrad through W_L and the jet VJP of layer L on the owned (point, channel) pairs
+      // dgrad through W_L and the jet VJP of layer L on the owned (point, channel) pairs
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const int ch = wc * T::WCH + 8 * hh + g;
-        if (interior) {
+        double dh[S];
+#pragma unroll
+        for (int s = 0; s < S; ++s) dh[s] = 0.0;
+#pragma unroll
+        for (int kk = 0; kk < NY; ++kk) dh[index(kk) / NF] += dy[kk] * wl[index(kk) % NF][hh];
+        if constexpr (INTERIOR) {
           if (tc < npts) {
-            double hv[Q], dh[Q], zb[Q];
+            double zb[Q], hr[Q];
 #pragma unroll
-            for (int s = 0; s < Q; ++s) {
-              const int r = tc * Q + s;
-              double v = 0.0;
-#pragma unroll
-              for (int o = 0; o < NF; ++o) v += sD[r * NF + o] * sW[o * CP + ch];
-              dh[s] = v;
-              hv[s] = sH[r * LDH + ch];
-            }
-            Jet<DIM, 3>::vjp(hv, a1r[hh][0], dh, zb);
+            for (int s = 0; s < Q; ++s) hr[s] = hval(hh, s);
+            Jet<DIM, 3>::vjp(hr, a1r[hh][0], dh, zb);
             double* dst = dL + (p0 + tc) * Q * CP + ch;
 #pragma unroll
             for (int s = 0; s < Q; ++s) dst[int64_t(s) * CP] = zb[s];
@@ -2398,17 +2490,10 @@ __global__ void __launch_bounds__(kPPThreads, 1)
           for (int kq = 0; kq < PS; ++kq) {
             const int lp = tc * PS + kq;
             if (lp < npts) {
-              double hv[QB], dh[QB], zb[QB];
+              double zb[QB], hr[QB];
 #pragma unroll
-              for (int c = 0; c < QB; ++c) {
-                const int r = lp * QB + c;
-                double v = 0.0;
-#pragma unroll
-                for (int o = 0; o < NF; ++o) v += sD[r * NF + o] * sW[o * CP + ch];
-                dh[c] = v;
-                hv[c] = sH[r * LDH + ch];
-              }
-              Jet<DIM, BO ? 1 : 0>::vjp(hv, a1r[hh][kq], dh, zb);
+              for (int c = 0; c < QB; ++c) hr[c] = hval(hh, kq * QB + c);
+              Jet<DIM, BO ? 1 : 0>::vjp(hr, a1r[hh][kq], dh + kq * QB, zb);
               double* dst = dL + (geo.ni * Q + (p0 + lp) * QB) * CP + ch;
 #pragma unroll
               for (int c = 0; c < QB; ++c) dst[int64_t(c) * CP] = zb[c];
@@ -2417,7 +2502,9 @@ __global__ void __launch_bounds__(kPPThreads, 1)
           }
         }
       }
-    }
+    };
+    if (interior) finish(std::true_type{});
+    else finish(std::false_type{});
   }
   // turn counts balanced as in bwd_pingpong
   if (gp == 0 && n0 == n1) named_sync(kPPBarTurn + 0, kPPThreads);
@@ -2426,41 +2513,43 @@ __global__ void __launch_bounds__(kPPThreads, 1)
     if (tid == 0) atomicExch(&g_device_fault, 1);
     return;
   }
-  // per-CTA partials, fixed-order reductions over the two groups
+  // per-CTA partials, fixed-order reductions: the 4 thread columns of a warp by shuffles,
+  // then the row groups of both groups in order
+  constexpr int RG = kPPGroups * T::WR;
   double* out = head_partial + int64_t(blockIdx.x) * PARTIAL;
-  double* red = smem;                          // [512] loss partials
-  double* cred = red + kPPThreads;             // [groups * WR][CP] bias partials of layer L-1
-  double* wsh = cred + kPPGroups * T::WR * CP;  // [8 warps][32 lanes][2] group 1's dW_L
-  double* bsh = wsh + T::NWARPS * 32 * 2;       // [NF] group 1's db_L
-  if (gp == 1) {
-    wsh[(lw * 32 + lane) * 2] = wacc[0];
-    wsh[(lw * 32 + lane) * 2 + 1] = wacc[1];
-    if (gtid < NF) bsh[gtid] = bacc;
-  }
-  red[tid] = lacc;
+  double* cred = smem;                  // [RG][CP] bias partials of layer L-1
+  double* wred = cred + RG * CP;        // [RG][NF][CP] dW_L
+  const int rg = gp * T::WR + wr;
 #pragma unroll
   for (int hh = 0; hh < 2; ++hh) {
+    const int ch = wc * T::WCH + 8 * hh + g;
     double v = cacc[hh];
     v += __shfl_xor_sync(0xffffffffu, v, 1);
     v += __shfl_xor_sync(0xffffffffu, v, 2);
-    if (t == 0) cred[(gp * T::WR + wr) * CP + wc * T::WCH + 8 * hh + g] = v;
+    if (t == 0) cred[rg * CP + ch] = v;
+#pragma unroll
+    for (int o = 0; o < NF; ++o) {
+      double u = wacc[o][hh];
+      u += __shfl_xor_sync(0xffffffffu, u, 1);
+      u += __shfl_xor_sync(0xffffffffu, u, 2);
+      if (t == 0) wred[(rg * NF + o) * CP + ch] = u;
+    }
   }
   __syncthreads();
-  if (gp == 0) {
-    if (g < NF) {
-      out[g * CP + 8 * lw + 2 * t] = wacc[0] + wsh[(lw * 32 + lane) * 2];
-      out[g * CP + 8 * lw + 2 * t + 1] = wacc[1] + wsh[(lw * 32 + lane) * 2 + 1];
-    }
-    if (gtid < NF) out[NF * CP + gtid] = bacc + bsh[gtid];
-  }
-  if (tid == 0) {
+  for (int idx = tid; idx < NF * CP; idx += kPPThreads) {  // dW_L[o][c] at o * CP + c
     double sum = 0.0;
-    for (int i = 0; i < kPPThreads; ++i) sum += red[i];
-    out[NF * CP + NF] = sum;
+    for (int r = 0; r < RG; ++r) sum += wred[r * NF * CP + idx];
+    out[idx] = sum;
+  }
+  if (tid < NF + 1) {  // db_L (tid < NF), then the loss; the lead slots in fixed order
+    const int f = tid < NF ? 1 + tid : 0;
+    double sum = 0.0;
+    for (int i = 0; i < RG * 4; ++i) sum += sL[i * (NF + 1) + f];
+    out[NF * CP + tid] = sum;
   }
   for (int c = tid; c < CP; c += kPPThreads) {
     double sum = 0.0;
-    for (int r = 0; r < kPPGroups * T::WR; ++r) sum += cred[r * CP + c];
+    for (int r = 0; r < RG; ++r) sum += cred[r * CP + c];
     out[NF * CP + NF + 1 + c] = sum;
   }
   if (tid == 0)
@@ -2892,7 +2981,7 @@ struct FwdHeadOps {
   static constexpr bool kPingPong = DIM == 2;  // 2-D: the two-group kernel over 80-row half tiles
   static cudaError_t setup(int& occ) {
     if constexpr (kPingPong) {
-      constexpr size_t smem = hpp_smem_bytes<NF>();
+      constexpr size_t smem = hpp_smem_bytes<BO, HEAD>();
       static_assert(smem <= kMaxSmem, "two-group head tile exceeds shared memory");
       cudaError_t e = allow_smem(head_pingpong<BO, HEAD>, smem);
       occ = occupancy(head_pingpong<BO, HEAD>, smem, kPPThreads);
@@ -2927,7 +3016,7 @@ struct FwdHeadOps {
       if ((e = row_tensor_map(&m[0], hin, ri, kFusedWidth, LDC, TR)) != cudaSuccess ||
           (e = row_tensor_map(&m[1], hin + ri * kFusedWidth, rb, kFusedWidth, LDC, BB)) != cudaSuccess)
         return e;
-      return launch_kernel(head_pingpong<BO, HEAD>, grid, kPPThreads, hpp_smem_bytes<NF>(), st, m[0], m[1], hin, w,
+      return launch_kernel(head_pingpong<BO, HEAD>, grid, kPPThreads, hpp_smem_bytes<BO, HEAD>(), st, m[0], m[1], hin, w,
                            b, wl, bl, pw, bw, tg, nu, gm, bc, dl, hpart, g);
     } else {
       return launch_kernel(fwd_head<DIM, BO, HEAD>, grid, HeadTile<DIM>::THREADS, fwd_head_smem_bytes<DIM, NF>(), st,

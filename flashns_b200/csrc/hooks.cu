@@ -252,40 +252,174 @@ __global__ void __launch_bounds__(kHookThreads)
 }
 
 // ---------------------------------------------------------------- dense dgrad (+ VJP)
-// dH[b, q, i] = sum_o D[b, q, o] W[o, i]; a warp covers 32 consecutive i of one sample so
-// the D row is a broadcast; W columns are coalesced.  FUSED applies the jet VJP.
+// dH[b, q, i] = sum_o D[b, q, o] W[o, i] on the FP64 tensor pipe (DMMA m16n8k8), then,
+// when FUSED, the jet VJP of each (sample, channel) from the accumulators.
+//
+// The GEMM runs transposed, as in the evaluation kernels: MMA M = input channels i (a CTA
+// owns a block of 64), MMA N = rows (b, q), K = output channels o.  A tile is 8 samples
+// (TR = 8 Q rows, contiguous in D, in their global order in shared memory); each of the 8
+// warps owns 16 channels of 4 samples, and a thread's accumulators hold, for its two
+// channels, all Q rows of one sample: the VJP needs no data exchange.  Tiles are (sample
+// block, channel block) pairs, grid-strided over a persistent grid of two CTAs per SM in
+// 2-D.  K streams through a two-stage ring of 32-column chunks of D and W that runs on
+// across tiles: the first chunk of a CTA's next tile is in flight while it runs the
+// current tile's epilogue, and the other CTA on the SM keeps the tensor pipe busy
+// meanwhile.  Copies are 16-byte cp.async when the rows allow it (even cout and cin,
+// 16-byte aligned D and W), 8-byte otherwise, zero-filled past the ends, so any cout and
+// cin work.  The tile's H rows and a1 values (contiguous ranges) are prefetched into L2
+// when the tile starts; the epilogue reads them from there.
+constexpr int kDgThreads = 256, kDgKC = 32, kDgLDC = kDgKC + 4, kDgCB = 64, kDgLDW = kDgCB + 4;
+constexpr int kDgTC = 8;  // samples per tile
+
+template <int DIM>
+constexpr size_t dgrad_smem_bytes() {
+  return sizeof(double) * 2 * (size_t(kDgTC) * Q_<DIM>::v * kDgLDC + size_t(kDgKC) * kDgLDW);
+}
+
+__device__ __forceinline__ void cp_async8(void* smem, const void* gmem, bool valid) {
+  const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(sa), "l"(gmem), "r"(valid ? 8 : 0));
+}
+
 template <int DIM, bool FUSED>
-__global__ void __launch_bounds__(kHookThreads)
+__global__ void __launch_bounds__(kDgThreads, DIM == 2 ? 2 : 1)
     dense_dgrad(const double* __restrict__ d, const double* __restrict__ w, const double* __restrict__ h,
-                const double* __restrict__ aux, double* __restrict__ out, int batch, int cout, int cin) {
-  constexpr int Q = Q_<DIM>::v;
-  const int64_t total = int64_t(batch) * cin;
-  for (int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
-       idx += int64_t(gridDim.x) * blockDim.x) {
-    const int64_t b = idx / cin;
-    const int i = int(idx % cin);
-    double acc[Q];
-#pragma unroll
-    for (int s = 0; s < Q; ++s) acc[s] = 0.0;
-    const double* db = d + b * Q * cout;
-    for (int o = 0; o < cout; ++o) {
-      const double wv = w[int64_t(o) * cin + i];
-#pragma unroll
-      for (int s = 0; s < Q; ++s) acc[s] += db[int64_t(s) * cout + o] * wv;
-    }
-    double* dst = out + b * Q * cin + i;
-    if constexpr (FUSED) {
-      double hv[Q], zb[Q];
-#pragma unroll
-      for (int s = 0; s < Q; ++s) hv[s] = h[(b * Q + s) * cin + i];
-      vjp_full<DIM>(hv, aux[idx], acc, zb);
-#pragma unroll
-      for (int s = 0; s < Q; ++s) dst[int64_t(s) * cin] = zb[s];
+                const double* __restrict__ aux, double* __restrict__ out, int batch, int cout, int cin, bool vec) {
+  constexpr int Q = Q_<DIM>::v, TR = kDgTC * Q, NT = Q / 2, LDC = kDgLDC, LDW = kDgLDW, KC = kDgKC;
+  extern __shared__ __align__(16) double dsm[];
+  double* sD = dsm;                 // [2][TR][LDC]   D chunk: rows of the tile, 32 output channels
+  double* sW = dsm + 2 * TR * LDC;  // [2][KC][LDW]   W chunk: 32 output channels, 64 input channels
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  const int wc = warp % 4, wr = warp / 4;  // 16-channel slice, sample group (4 samples)
+  const int64_t sample_tiles = (int64_t(batch) + kDgTC - 1) / kDgTC;
+  const int channel_blocks = (cin + kDgCB - 1) / kDgCB;
+  const int64_t units = sample_tiles * channel_blocks;
+  const int64_t mine = int64_t(blockIdx.x) < units ? (units - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int nk = (cout + KC - 1) / KC;
+  const int64_t steps = mine * nk;  // (tile, K chunk) pairs of this CTA, in order
+  const int brow = (wr * 4 + (g >> 1)) * Q + (g & 1);  // B column g of n8 tile j: row brow + 2j
+  auto unit_of = [&](int64_t i) { return int64_t(blockIdx.x) + i * gridDim.x; };
+  auto load = [&](int64_t step, int stage) {
+    const int64_t u = unit_of(step / nk);
+    const int kc = int(step % nk);
+    const int64_t b0 = (u / channel_blocks) * kDgTC;
+    const int i0 = int(u % channel_blocks) * kDgCB;
+    const int64_t rows_left = (int64_t(batch) - b0) * Q;
+    double* dD = sD + stage * TR * LDC;
+    double* dW = sW + stage * KC * LDW;
+    if (vec) {
+      for (int e = tid; e < TR * (KC / 2); e += kDgThreads) {
+        const int r = e / (KC / 2), c = 2 * (e % (KC / 2)), o = kc * KC + c;
+        const bool ok = r < rows_left && o < cout;  // cout even: o < cout covers o + 1
+        cp_async16(dD + r * LDC + c, ok ? d + (b0 * Q + r) * cout + o : d, ok);
+      }
+      for (int e = tid; e < KC * (kDgCB / 2); e += kDgThreads) {
+        const int r = e / (kDgCB / 2), c = 2 * (e % (kDgCB / 2)), o = kc * KC + r, i = i0 + c;
+        const bool ok = o < cout && i < cin;  // cin even: i < cin covers i + 1
+        cp_async16(dW + r * LDW + c, ok ? w + int64_t(o) * cin + i : w, ok);
+      }
     } else {
+      for (int e = tid; e < TR * KC; e += kDgThreads) {
+        const int r = e / KC, c = e % KC, o = kc * KC + c;
+        const bool ok = r < rows_left && o < cout;
+        cp_async8(dD + r * LDC + c, ok ? d + (b0 * Q + r) * cout + o : d, ok);
+      }
+      for (int e = tid; e < KC * kDgCB; e += kDgThreads) {
+        const int r = e / kDgCB, c = e % kDgCB, o = kc * KC + r, i = i0 + c;
+        const bool ok = o < cout && i < cin;
+        cp_async8(dW + r * LDW + c, ok ? w + int64_t(o) * cin + i : w, ok);
+      }
+    }
+  };
+  double acc[NT][4];
+  if (steps > 0) load(0, 0);
+  cp_async_commit();
+  for (int64_t step = 0; step < steps; ++step) {
+    const int kc = int(step % nk);
+    const int64_t u = unit_of(step / nk);
+    const int64_t b0 = (u / channel_blocks) * kDgTC;
+    const int i0 = int(u % channel_blocks) * kDgCB;
+    if (kc == 0) {
 #pragma unroll
-      for (int s = 0; s < Q; ++s) dst[int64_t(s) * cin] = acc[s];
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[j][e] = 0.0;
+      if constexpr (FUSED) {
+        if (tid == 0) {  // the epilogue's H rows and a1 values into L2 (whole rows: every channel block)
+          const int64_t nb = int64_t(batch) - b0 < kDgTC ? int64_t(batch) - b0 : kDgTC;
+          const uint64_t hbytes = uint64_t(nb) * Q * cin * sizeof(double), abytes = uint64_t(nb) * cin * sizeof(double);
+          const double* hs = h + b0 * Q * cin;
+          const double* as = aux + b0 * cin;
+          if (((reinterpret_cast<uintptr_t>(hs) | hbytes) & 15) == 0 && hbytes < (1u << 31)) prefetch_l2(hs, uint32_t(hbytes));
+          if (((reinterpret_cast<uintptr_t>(as) | abytes) & 15) == 0 && abytes < (1u << 31)) prefetch_l2(as, uint32_t(abytes));
+        }
+      }
+    }
+    if (step + 1 < steps) load(step + 1, int((step + 1) & 1));  // may be the next tile's first chunk
+    cp_async_commit();
+    cp_async_wait<1>();  // chunk `step` landed (this thread's copies)
+    __syncthreads();     // ... and every other thread's
+    const double* cB = sD + (step & 1) * TR * LDC + brow * LDC;
+    const double* cA = sW + (step & 1) * KC * LDW + wc * 16;
+#pragma unroll
+    for (int kk = 0; kk < KC; kk += 8) {
+      double a[4];
+      a[0] = cA[(kk + t) * LDW + g];
+      a[1] = cA[(kk + t) * LDW + g + 8];
+      a[2] = cA[(kk + t + 4) * LDW + g];
+      a[3] = cA[(kk + t + 4) * LDW + g + 8];
+#pragma unroll
+      for (int j = 0; j < NT; ++j) mma_m16n8k8(acc[j], a, cB[2 * j * LDC + kk + t], cB[2 * j * LDC + kk + t + 4]);
+    }
+    __syncthreads();  // stage step & 1 free for chunk step + 2
+    if (kc != nk - 1) continue;
+    // epilogue of tile u: sample b0 + wr*4 + t, channels i0 + 16 wc + {g, g + 8}
+    const int64_t b = b0 + wr * 4 + t;
+    if (b >= batch) continue;
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int i = i0 + wc * 16 + 8 * hh + g;
+      if (i >= cin) continue;
+      double dh[Q];
+#pragma unroll
+      for (int s = 0; s < Q; ++s) dh[s] = acc[s >> 1][2 * hh + (s & 1)];
+      double* dst = out + b * Q * cin + i;
+      if constexpr (FUSED) {
+        double hv[Q], zb[Q];
+#pragma unroll
+        for (int s = 0; s < Q; ++s) hv[s] = h[(b * Q + s) * cin + i];
+        vjp_full<DIM>(hv, aux[b * cin + i], dh, zb);
+#pragma unroll
+        for (int s = 0; s < Q; ++s) dst[int64_t(s) * cin] = zb[s];
+      } else {
+#pragma unroll
+        for (int s = 0; s < Q; ++s) dst[int64_t(s) * cin] = dh[s];
+      }
     }
   }
+  cp_async_wait<0>();
+}
+
+template <int DIM, bool FUSED>
+cudaError_t launch_dense_dgrad(const double* d, const double* w, const double* h, const double* aux, double* out,
+                               int batch, int cout, int cin, cudaStream_t stream) {
+  constexpr size_t smem = dgrad_smem_bytes<DIM>();
+  // a per-device attribute (host-side, not a stream operation): set on every call, so that
+  // each device the caller switches to gets it
+  cudaError_t e = cudaFuncSetAttribute(dense_dgrad<DIM, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return e;
+  int device = 0, sms = 0, per_sm = 0;
+  e = cudaGetDevice(&device);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dense_dgrad<DIM, FUSED>, kDgThreads, smem);
+  if (e != cudaSuccess) return e;
+  const int64_t units = ((int64_t(batch) + kDgTC - 1) / kDgTC) * ((cin + kDgCB - 1) / kDgCB);
+  const int64_t resident = int64_t(sms) * (per_sm > 0 ? per_sm : 1);
+  const unsigned grid = unsigned(units < resident ? units : resident);
+  const bool vec = cout % 2 == 0 && cin % 2 == 0 && (reinterpret_cast<uintptr_t>(d) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(w) & 15) == 0;
+  dense_dgrad<DIM, FUSED><<<grid, kDgThreads, smem, stream>>>(d, w, h, aux, out, batch, cout, cin, vec);
+  return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------- coordinate wgrad
@@ -613,15 +747,13 @@ int flashns_stable_dgrad_vjp(int dim, bool fused, const double* d, const double*
   if (overlaps(out, no * 8, d, size_t(batch) * q * cout * 8) || overlaps(out, no * 8, w, size_t(cout) * cin * 8) ||
       (fused && (overlaps(out, no * 8, h, no * 8) || overlaps(out, no * 8, aux, size_t(batch) * cin * 8))))
     return int(cudaErrorInvalidValue);
-  const unsigned g = grid_of(int64_t(batch) * cin);
-  if (dim == 2 && fused) dense_dgrad<2, true><<<g, kHookThreads, 0, stream>>>(d, w, h, aux, out, batch, cout, cin);
-  else if (dim == 2) dense_dgrad<2, false><<<g, kHookThreads, 0, stream>>>(d, w, h, aux, out, batch, cout, cin);
-  else if (fused) dense_dgrad<3, true><<<g, kHookThreads, 0, stream>>>(d, w, h, aux, out, batch, cout, cin);
-  else dense_dgrad<3, false><<<g, kHookThreads, 0, stream>>>(d, w, h, aux, out, batch, cout, cin);
-  return int(cudaGetLastError());
+  if (dim == 2 && fused) return int(launch_dense_dgrad<2, true>(d, w, h, aux, out, batch, cout, cin, stream));
+  if (dim == 2) return int(launch_dense_dgrad<2, false>(d, w, h, aux, out, batch, cout, cin, stream));
+  if (fused) return int(launch_dense_dgrad<3, true>(d, w, h, aux, out, batch, cout, cin, stream));
+  return int(launch_dense_dgrad<3, false>(d, w, h, aux, out, batch, cout, cin, stream));
 }
 
-int flashns_stable_dgrad_shared_bytes() { return 0; }
+int flashns_stable_dgrad_shared_bytes() { return int(flashns_b200::dgrad_smem_bytes<2>()); }
 
 }  // extern "C"
 
@@ -664,7 +796,8 @@ extern "C" int flashns_b200_residuals(int head, int dim, const double* jets, dou
 // ---- plan-based dense dgrad (+ jet VJP) under the reference's Hopper names
 // (experiments/cuda_jet_hopper/hopper.cu:287-353): the same argument meaning, limits and
 // error codes, so the reference's binding (experiments/cuda_jet_hopper/hopper.py) can load
-// this library on B200.  The plan keeps D, W and the sizes; a launch runs dense_dgrad.
+// this library on B200.  The plan keeps D, W and the sizes; a launch runs the DMMA
+// dense_dgrad (+ VJP) above.
 namespace flashns_b200 {
 namespace {
 struct DgradPlan {
@@ -678,12 +811,15 @@ int dgrad_resources(long long* values) {
   cudaFuncAttributes attr;
   cudaError_t e = cudaFuncGetAttributes(&attr, dense_dgrad<DIM, FUSED>);
   if (e != cudaSuccess) return int(e);
+  constexpr size_t smem = dgrad_smem_bytes<DIM>();
+  e = cudaFuncSetAttribute(dense_dgrad<DIM, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return int(e);
   int blocks = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, dense_dgrad<DIM, FUSED>, kHookThreads, 0);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, dense_dgrad<DIM, FUSED>, kDgThreads, smem);
   if (e != cudaSuccess) return int(e);
   values[0] = attr.numRegs;
-  values[1] = kHookThreads;
-  values[2] = 0;  // no dynamic shared memory
+  values[1] = kDgThreads;
+  values[2] = int64_t(smem);  // dynamic shared memory per CTA
   values[3] = attr.sharedSizeBytes;
   values[4] = attr.localSizeBytes;
   values[5] = blocks;

@@ -187,7 +187,8 @@ int flashns_stable_activation(int dim, bool backward, const double* value, const
                               double* output, double* aux_out, size_t batch, size_t channels, cudaStream_t stream);
 int flashns_stable_tail3(int dim, bool fused, const double* d, const double* weight, const double* hidden,
                          const double* aux, double* output, size_t batch, size_t channels, cudaStream_t stream);
-/* out[B,Q,Cin] = D[B,Q,Cout] W[Cout,Cin] (fused: followed by the jet VJP with h[B,Q,Cin], aux[B,Cin]) */
+/* out[B,Q,Cin] = D[B,Q,Cout] W[Cout,Cin] (fused: followed by the jet VJP with h[B,Q,Cin], aux[B,Cin]),
+ * on the FP64 tensor pipe (DMMA) with the VJP in the epilogue; any Cout, Cin; pointers 8-byte aligned */
 int flashns_stable_dgrad_vjp(int dim, bool fused, const double* d, const double* w, const double* h, const double* aux,
                              double* out, int batch, int cout, int cin, cudaStream_t stream);
 /* Residual values at interior points: jets [n, Q, F] coefficient-major -> out [n, R]; head UVP:
@@ -263,7 +264,7 @@ int flashns_b200_philox_points(uint64_t key0, uint64_t key1, int dim, int64_t fi
 int flashns_b200_pack_coordinates(const double* x, int64_t full_points, int64_t value_points, int dim, double* out,
                                   cudaStream_t stream);
 
-/* shared memory the dense dgrad uses per block (0: this implementation stages none) */
+/* dynamic shared memory per CTA of the dense dgrad (its 2-D kernel) */
 int flashns_stable_dgrad_shared_bytes(void);
 
 /* Plan-based dense dgrad under the reference's Hopper names
