@@ -10,6 +10,9 @@ evaluation of a cfg1-sized point set per GPU.  With N GPUs (torchrun, one rank
 per GPU) the global point set is N x cfg1, each rank evaluates its shard and one
 NCCL all-reduce of the packed [gradient, loss] buffer completes the step (weak
 scaling); ``value`` counts cfg1-sized shard evaluations of all ranks per second.
+``--scaling strong`` shards the configuration's one point set over the N ranks
+(``shard_bounds`` on interior and boundary points, global weights) and ``value``
+counts complete evaluations of that set per second.
 
 ``--impl reference`` times the reference's own CPU implementation, its ``PackedPINN``
 (installed into ``baseline/_ref/`` by ``baseline/install_reference.py``, run by
@@ -56,20 +59,31 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-gpu"])
     ap.add_argument("--route", default="F", choices=["F", "B1", "v8", "v8+"],
                     help="route of --impl reference-gpu")
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
+                    help="weak: each rank evaluates a config-sized shard of an N x config set; strong: the "
+                         "config's one point set is sharded over the N ranks")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="only W warm-up and K timed steps (for ncu launch lists); prints a short line")
+    ap.add_argument("--points-divisor", type=int, default=1,
+                    help="with --profile: 1/D of the configuration's points (small ncu captures of the same kernels)")
     return ap.parse_args()
 
 
-def workload(config):
+def workload(config, scaling="weak"):
     from flashns_b200.problems import CONFIGS, config_options
     c = CONFIGS[config]
     head, order, _ = config_options(config)
     net = "-".join(str(w) for w in c["widths"][:2]) + f"x{len(c['widths']) - 2}-{c['widths'][-1]}"
     rows = "first-order boundary rows" if order else "value boundary rows"
+    jets = f"Q{10 if c['widths'][0] == 2 else 20} interior jets"
+    if scaling == "strong":
+        return {"workload": f"{config}: {c['kind']} {c['interior']}+{c['boundary']} points in total, sharded over "
+                            f"the GPUs, {head} head, {jets}, {rows}",
+                "net": net, "interior_points": c["interior"], "boundary_points": c["boundary"], "head": head,
+                "boundary_order": order}
     return {"workload": f"{config}: {c['kind']} {c['interior']}+{c['boundary']} points per GPU, {head} head, "
-                        f"Q{10 if c['widths'][0] == 2 else 20} interior jets, {rows}",
+                        f"{jets}, {rows}",
             "net": net, "interior_points_per_gpu": c["interior"], "boundary_points_per_gpu": c["boundary"],
             "head": head, "boundary_order": order}
 
@@ -369,7 +383,7 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    cfg = workload(args.config)
+    cfg = workload(args.config, args.scaling)
 
     if args.impl == "reference-gpu":
         if rank == 0:
@@ -414,7 +428,15 @@ def main():
     c = CONFIGS[args.config]
     widths = c["widths"]
     # weak scaling: the global set is `world` x the config; each rank owns one config-sized shard
-    pts = config_points(args.config, scale=world).shard(world, rank) if world > 1 else config_points(args.config)
+    if args.points_divisor != 1 and not args.profile:
+        raise SystemExit("--points-divisor only applies to --profile runs")
+    if world == 1:
+        pts = config_points(args.config, divisor=args.points_divisor)
+    elif args.scaling == "strong":  # the configuration's point set, sharded
+        pts = config_points(args.config).shard(world, rank)
+    else:  # weak: a world x config set, one config-sized shard per rank
+        pts = config_points(args.config, scale=world).shard(world, rank)
+    per_step = world if args.scaling == "weak" else 1  # configuration-sized evaluations per step
     head, order, gamma = config_options(args.config)
     loss = NSLoss(viscosity=pts.viscosity, gradient_weight=gamma, boundary_weight=5.0)
     ev = PackedEvaluator(pts.x, pts.interior_count, pts.pde_weights, pts.boundary_weights, pts.target, widths,
@@ -446,7 +468,8 @@ def main():
             dist.destroy_process_group()
         if rank == 0:
             print(json.dumps({"profile": True, "config": args.config, "launches_per_step": ev.launches_per_call,
-                              "warmup": args.warmup, "steps": args.steps}), flush=True)
+                              "interior": ev.ni, "boundary": ev.nb, "warmup": args.warmup, "steps": args.steps}),
+                  flush=True)
         return
 
     sampler = ClockSampler(local, f"/tmp/flashns_clocks_{rank}.csv")
@@ -548,7 +571,7 @@ def main():
         cpu = port if ref is None else {"value": ref["value"], "unit": UNIT, "cores": threads, "kind": "reference",
                                         "sample": reference_cpu_sample(ref, args.config)}
     step_tflops = costs["total"] / (ms_step * 1e-3) / 1e12
-    value = world * 1e3 / ms_step
+    value = per_step * 1e3 / ms_step
     if args.config == "ref16k":
         # the reference's own headline workload, published for its fused F route on H100
         # (1.832 ms per evaluation, CUDA-graph replay): the only config with a published number
@@ -560,13 +583,13 @@ def main():
         data = "synthetic (seeded uniform Kovasznay points, analytic boundary targets, Xavier-normal weights seed 0)"
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": args.scaling,
         "vs_baseline": vs_baseline, "dtype": "f64", "data": data,
         "config": cfg,
         "parallelism": f"dp{world}" if world > 1 else "single",
         "l2": "working set (checkpoints + seeds) %.2f GB > 126 MB L2; no flush needed"
               % (checkpoint_bytes(widths, ev.ni, ev.nb, boundary_order=order) / 1e9),
-        "e2e": {"value": world * 1e3 / float(e2e_ms), "unit": UNIT, "h2d_bytes_per_step": h2d,
+        "e2e": {"value": per_step * 1e3 / float(e2e_ms), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": ev.launches_per_call * args.steps,
         "roofline": {"bound": "tensor", "kernel": dominant, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",

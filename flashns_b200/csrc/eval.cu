@@ -39,6 +39,10 @@ constexpr int LDC = KC + 4;  // padded chunk row: conflict-free FP64 fragment lo
 constexpr int kMaxAffine = 16;
 // set by a kernel whose bounded wait on a bulk copy gave up (read by flashns_b200_device_fault)
 __device__ int g_device_fault = 0;
+// the dense dgrad (+ VJP) of a 2-D 64 -> 64 layer on the two-group backward kernel (defined
+// with the host launchers below; called by the reference-ABI hook in hooks.cu)
+cudaError_t dense_dgrad_64(bool fused, const double* d, const double* w, const double* h, const double* aux,
+                           double* out, int batch, cudaStream_t stream);
 
 // Self-test of the bounded wait: an mbarrier that nothing arrives at.  The wait gives up
 // after `spins` polls, raises the fault word and the kernel returns normally.
@@ -958,7 +962,12 @@ constexpr size_t pp_smem_bytes() {
   return a > red ? a : red;
 }
 
-template <int BO, bool FIRST>
+// MODE kEvalBackward: the evaluation's layer backward (dgrad, wgrad, VJP, bias and
+// coordinate partials).  kHookDgradVjp / kHookDgrad: the dense dgrad (+ jet VJP) of the
+// reference-ABI hook (flashns_stable_dgrad_vjp on a 64 -> 64 layer): no weight gradient and
+// no partials; kHookDgrad also skips H and writes dH itself.
+enum { kEvalBackward = 0, kHookDgradVjp = 1, kHookDgrad = 2 };
+template <int BO, bool FIRST, int MODE = kEvalBackward>
 __global__ void __launch_bounds__(kPPThreads, 1)
     bwd_pingpong(const __grid_constant__ CUtensorMap tm_seed_i, const __grid_constant__ CUtensorMap tm_seed_b,
                  const __grid_constant__ CUtensorMap tm_h_i, const __grid_constant__ CUtensorMap tm_h_b,
@@ -977,6 +986,8 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   constexpr bool SPLIT = BB != TR;  // boundary tiles whose points leave slots empty: cp.async
   constexpr int GT = T::THREADS;    // threads per group
   constexpr int PLANES = NK * TR * LDC;
+  constexpr bool EVAL = MODE == kEvalBackward, WITH_H = MODE != kHookDgrad;
+  static_assert(EVAL || (!FIRST && BO == 0), "the hook modes cover dense (all full-jet) rows");
   static_assert(CP / 8 == T::NWARPS && TR % 16 == 0, "wgrad: warp w of a group owns dW columns 8w..8w+7");
   static_assert(NK == 2 && KC == 32 && TR <= 256, "TMA boxes: 36 columns, at most 256 rows");
   static_assert((size_t(TR) * LDC * sizeof(double)) % 128 == 0, "every TMA destination on a 128-byte boundary");
@@ -1064,7 +1075,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   pdl_trigger();
   if (nmy > 0) {
     load_tile(tile_of(0), sB, &tm_seed_i, &tm_seed_b, bar_seed, dnext);
-    load_tile(tile_of(0), sH, &tm_h_i, &tm_h_b, bar_h, hcur);
+    if (WITH_H) load_tile(tile_of(0), sH, &tm_h_i, &tm_h_b, bar_h, hcur);
   }
   unsigned ph_seed = 0, ph_h = 0;
   bool dead = false;  // a bounded wait ran out: skip the work, keep the turn protocol
@@ -1077,7 +1088,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   for (int64_t k = 0; k < nmy; ++k) {
     const int64_t tile = tile_of(k);
     const bool has_next = k + 1 < nmy;
-    if (gtid == 0 && !dead) {  // the epilogue reads this tile's a1 rows (a contiguous range): into L2
+    if (WITH_H && gtid == 0 && !dead) {  // the epilogue reads this tile's a1 rows (a contiguous range): into L2
       int64_t pt0, pts;
       TL::points(geo, nint, tile, pt0, pts);
       prefetch_l2(a1cur + pt0 * CP, uint32_t(pts * CP * sizeof(double)));
@@ -1106,9 +1117,9 @@ __global__ void __launch_bounds__(kPPThreads, 1)
           for (int j = 0; j < T::NT; ++j) mma_m16n8k8(acc[j], a, cB[2 * j * LDC + kk + t], cB[2 * j * LDC + kk + t + 4]);
         }
       }
-      dead = named_sync_or(bar_group, GT, !wait_tile(tile, bar_h, ph_h, true));  // H_l landed
+      if (WITH_H) dead = named_sync_or(bar_group, GT, !wait_tile(tile, bar_h, ph_h, true));  // H_l landed
     }
-    if (!dead) {
+    if (EVAL && !dead) {
       // wgrad: dW[cout][8*lw..+8] += D^T[cout][rows] H[rows][cin] over the half tile's rows
       // (each row step feeds all NM accumulators from one B fragment: NM MMAs in flight)
 #pragma unroll 2
@@ -1134,6 +1145,31 @@ __global__ void __launch_bounds__(kPPThreads, 1)
       // epilogue: jet VJP of this half tile; H_l from the shared planes (slot s of thread
       // column wr*4+t is row (wr*4+t)*S + s)
       const int tc = wr * 4 + t;
+      if constexpr (!EVAL) {  // the hook: dense rows, dH (+ VJP) straight to the output
+        const int64_t p = tile * T::TC + tc;
+        if (p < geo.ni) {
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const int ch = wc * T::WCH + 8 * hh + g;
+            double dh[S], zb[Q];
+#pragma unroll
+            for (int s = 0; s < S; ++s) dh[s] = acc[s >> 1][2 * hh + (s & 1)];
+            if constexpr (MODE == kHookDgradVjp) {
+              double hv[Q];
+              const double* hrow = sH + (tc * S) * LDC;
+#pragma unroll
+              for (int s = 0; s < Q; ++s) hv[s] = hrow[(ch >> 5) * TR * LDC + s * LDC + (ch & (KC - 1))];
+              Jet<DIM, 3>::vjp(hv, a1cur[p * CP + ch], dh, zb);
+            } else {
+#pragma unroll
+              for (int s = 0; s < Q; ++s) zb[s] = dh[s];
+            }
+            double* dst = dcur + p * Q * CP + ch;
+#pragma unroll
+            for (int s = 0; s < Q; ++s) dst[int64_t(s) * CP] = zb[s];
+          }
+        }
+      } else {
       const double* hrow = sH + (tc * S) * LDC;
       auto hslot = [&](int s, int ch) { return hrow[(ch >> 5) * TR * LDC + s * LDC + (ch & (KC - 1))]; };
       const bool interior = tile < nint;
@@ -1188,9 +1224,10 @@ __global__ void __launch_bounds__(kPPThreads, 1)
           }
         }
       }
+      }  // EVAL epilogue
     }
     named_sync(bar_group, GT);  // this group's H_l planes free
-    if (has_next && !dead) load_tile(tile_of(k + 1), sH, &tm_h_i, &tm_h_b, bar_h, hcur);
+    if (WITH_H && has_next && !dead) load_tile(tile_of(k + 1), sH, &tm_h_i, &tm_h_b, bar_h, hcur);
   }
   // Turn counts.  Barrier "turn 0" gets n0 syncs from group 0 and 1 + n1 arrivals from
   // group 1; "turn 1" gets n1 syncs from group 1 and n0 arrivals from group 0.  With
@@ -1202,6 +1239,11 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   // set `dead`; the whole CTA then leaves together with the fault word set.
   if (__syncthreads_or(dead)) {
     if (tid == 0) atomicExch(&g_device_fault, 1);
+    return;
+  }
+  if constexpr (!EVAL) {  // the hook writes no partials
+    if (tid == 0)
+      for (int b = 0; b < 2 * kPPGroups; ++b) mbar_inval(&bars[b]);
     return;
   }
   // weight-gradient partial of this CTA: the two groups' row shares combined in fixed order
@@ -2105,6 +2147,372 @@ __global__ void __launch_bounds__(HeadTile<DIM>::THREADS, HeadTile<DIM>::MINB)
   }
 }
 
+// Two-group ("ping-pong") form of fwd_head for 2-D, staged through shared memory: the last
+// hidden layer, the output layer, the residual seeds, the output-layer gradients and the
+// VJP into layer L, with the CTA's 16 warps in two 8-warp groups that take turns on the
+// tensor pipe as in bwd_pingpong.  Each group has its own input planes (TMA, rows in global
+// order), H_L tile, Y and dY; W_{L-1} and W_L are shared.  A group's mainloop runs while it
+// holds the turn; its whole epilogue (jet, output contraction, seeds, output gradients,
+// VJP and the stores of D_L) overlaps the other group's mainloop.  This form serves the
+// (u, v, p) head, whose seed reads 25 outputs (one thread per point forms it from the
+// staged outputs), and value boundary rows, where a thread column holds ten points; the
+// stream-function head with first-order rows runs head_pingpong below.
+template <int NF>
+constexpr size_t hpp_staged_group_doubles() {
+  return size_t(kFusedWidth / KC) * PPTile::TR * LDC + size_t(PPTile::TR) * (kFusedWidth + 4) +
+         2 * size_t(PPTile::TR) * NF;
+}
+template <int NF>
+constexpr size_t hpp_staged_smem_bytes() {
+  return sizeof(double) * (kPPGroups * hpp_staged_group_doubles<NF>() + size_t(kFusedWidth) * (kFusedWidth + 4) +
+                           size_t(NF) * kFusedWidth + kPPGroups);
+}
+
+template <int BO, int HEAD>
+__global__ void __launch_bounds__(kPPThreads, 1)
+    head_pingpong_staged(const __grid_constant__ CUtensorMap tm_in_i, const __grid_constant__ CUtensorMap tm_in_b,
+                  const double* __restrict__ hin, const double* __restrict__ w, const double* __restrict__ bias,
+                  const double* __restrict__ wL, const double* __restrict__ bL, const double* __restrict__ pde_w,
+                  const double* __restrict__ bnd_w, const double* __restrict__ target, double nu, double gamma,
+                  double bc, double* __restrict__ dL, double* __restrict__ head_partial, Geometry geo) {
+  constexpr int DIM = 2, CP = kFusedWidth;
+  using T = PPTile;
+  using TL = Tiles<DIM, BO, T::TC>;
+  constexpr int S = T::S, TR = T::TR, Q = TL::Q, QB = TL::QB, PS = TL::PS;
+  constexpr int NF = HeadTraits<HEAD>::NF;
+  constexpr int NFT = (HEAD == FLASHNS_B200_HEAD_PSI && BO) ? 3 : NF;  // boundary target fields
+  constexpr int LDA = CP + 4, LDH = CP + 4;
+  constexpr int PARTIAL = NF * CP + NF + 1 + CP;  // dW_L | db_L | loss | db_{L-1}
+  constexpr int NK = CP / KC;
+  constexpr int BB = pp_boundary_box_rows<BO>();
+  constexpr bool SPLIT = BB != TR;
+  constexpr int GT = T::THREADS;
+  constexpr int PLANES = NK * TR * LDC;
+  static_assert(T::NWARPS == CP / 8 && NF <= 8, "warp w of a group owns output-gradient columns 8w..8w+7");
+  static_assert(NK == 2 && KC == 32 && TR <= 256, "TMA boxes: 36 columns, at most 256 rows");
+  static_assert((hpp_staged_group_doubles<NF>() * sizeof(double)) % 128 == 0, "group buffers on 128-byte boundaries");
+  extern __shared__ __align__(128) double smem[];
+  if (smem_u32(smem) & 127) {  // TMA destinations need 128-byte alignment: refuse, never fault
+    if (threadIdx.x == 0) atomicExch(&g_device_fault, 2);
+    return;
+  }
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  const int gp = warp / T::NWARPS, lw = warp % T::NWARPS, gtid = tid % GT;
+  const int wc = lw % T::WC, wr = lw / T::WC;
+  double* sB = smem + gp * hpp_staged_group_doubles<NF>();  // this group's input planes [NK][TR][LDC]
+  double* sH = sB + PLANES;                          // H_L tile [TR][CP+4], rows in tile order
+  double* sY = sH + TR * LDH;                        // Y  [TR][NF]
+  double* sD = sY + TR * NF;                         // dY [TR][NF]
+  double* sA = smem + kPPGroups * hpp_staged_group_doubles<NF>();  // W_{L-1} [CP][CP+4], shared
+  double* sW = sA + CP * LDA;                                // W_L [NF][CP], shared
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sW + NF * CP);
+  uint64_t* bar_in = bars + gp;
+  const int bar_group = kPPBarGroup + gp;
+  const int64_t nint = TL::interior(geo.ni);
+  const int64_t nht = nint + TL::boundary(geo.nb);
+  const int64_t mine = int64_t(blockIdx.x) < nht ? (nht - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int64_t n0 = (mine + 1) / 2, n1 = mine / 2;
+  const int64_t nmy = gp == 0 ? n0 : n1;
+  auto tile_of = [&](int64_t k) { return int64_t(blockIdx.x) + (2 * k + gp) * int64_t(gridDim.x); };
+  auto load_tile = [&](int64_t tile) {
+    const bool interior = tile < nint;
+    if (SPLIT && !interior) {
+      const int64_t b0 = (tile - nint) * (int64_t(T::TC) * PS);
+      for (int i = gtid; i < NK * TR * (KC / 2); i += GT) {
+        const int kc = i / (TR * (KC / 2)), rem = i % (TR * (KC / 2));
+        const int r = rem / (KC / 2), q = rem % (KC / 2);
+        const int tc = r / S, sl = r % S;
+        const int64_t b = b0 + int64_t(tc) * PS + sl / QB;
+        const bool ok = sl < PS * QB && b < geo.nb;
+        const int64_t gr = ok ? geo.ni * Q + b * QB + sl % QB : 0;
+        cp_async16(sB + kc * TR * LDC + r * LDC + 2 * q, hin + gr * CP + kc * KC + 2 * q, ok);
+      }
+      cp_async_commit();
+      return;
+    }
+    if (gtid != 0) return;
+    fence_proxy_async();  // the planes' last readers finished before the barrier that led here
+    const int y = interior ? int(tile * T::TC * Q) : int((tile - nint) * (int64_t(T::TC) * PS) * QB);
+    mbar_arrive_expect_tx(bar_in, NK * TR * LDC * sizeof(double));
+#pragma unroll
+    for (int kc = 0; kc < NK; ++kc) tma_load_2d(sB + kc * TR * LDC, interior ? &tm_in_i : &tm_in_b, kc * KC, y, bar_in);
+  };
+  unsigned ph = 0;
+  auto wait_tile = [&](int64_t tile) {
+    if (SPLIT && tile >= nint) {
+      cp_async_wait<0>();
+      return true;
+    }
+    const bool ok = mbar_wait(bar_in, ph);
+    ph ^= 1u;
+    return ok;
+  };
+  double bias_r[2];  // a thread's channels are fixed for the whole kernel
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) bias_r[hh] = bias[wc * T::WCH + 8 * hh + g];
+  for (int i = tid; i < CP * (CP / 2); i += kPPThreads) {  // W_{L-1}, resident
+    const int r = i / (CP / 2), p = i % (CP / 2);
+    cp_async16(sA + r * LDA + 2 * p, w + int64_t(r) * CP + 2 * p, true);
+  }
+  cp_async_commit();
+  for (int i = tid; i < NF * CP; i += kPPThreads) sW[i] = wL[i];
+  if (tid == 0)
+    for (int b = 0; b < kPPGroups; ++b) mbar_init(&bars[b], 1);
+  cp_async_wait<0>();
+  __syncthreads();  // W_{L-1}, W_L and the barriers visible
+  pdl_wait();  // H_{L-1} is the predecessor's output
+  pdl_trigger();
+  if (nmy > 0) load_tile(tile_of(0));
+  double wacc[4] = {0.0, 0.0, 0.0, 0.0};  // dW_L[g][8 lw + 2t (+1)] (rows g < NF)
+  double bacc = 0.0, lacc = 0.0, cacc[2] = {0.0, 0.0};
+  bool dead = false;
+  // B fragments: column g of an n8 tile is slot 2j + (g & 1) of thread column wr*4 + (g >> 1)
+  const int brow = (wr * 4 + (g >> 1)) * S + (g & 1);
+  if (gp == 1) named_arrive(kPPBarTurn + 0, kPPThreads);  // group 0 takes the first turn
+  for (int64_t k = 0; k < nmy; ++k) {
+    const int64_t tile = tile_of(k);
+    double acc[T::NT][4];
+#pragma unroll
+    for (int j = 0; j < T::NT; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[j][e] = 0.0;
+    if (!dead) dead = named_sync_or(bar_group, GT, !wait_tile(tile));
+    named_sync(kPPBarTurn + gp, kPPThreads);  // this group's turn on the tensor pipe
+    if (!dead) {
+      // Z^T[ch][rows] = W_{L-1}[ch][cin] H_{L-1}^T[cin][rows]
+#pragma unroll
+      for (int kc = 0; kc < NK; ++kc) {
+        const double* cB = sB + kc * TR * LDC + brow * LDC;
+        const double* cA = sA + wc * T::WCH * LDA + kc * KC;
+#pragma unroll
+        for (int kk = 0; kk < KC; kk += 8) {
+          double a[4];
+          a[0] = cA[g * LDA + kk + t];
+          a[1] = cA[(g + 8) * LDA + kk + t];
+          a[2] = cA[g * LDA + kk + t + 4];
+          a[3] = cA[(g + 8) * LDA + kk + t + 4];
+#pragma unroll
+          for (int j = 0; j < T::NT; ++j) mma_m16n8k8(acc[j], a, cB[2 * j * LDC + kk + t], cB[2 * j * LDC + kk + t + 4]);
+        }
+      }
+    }
+    named_arrive(kPPBarTurn + (1 - gp), kPPThreads);  // the other group's turn
+    named_sync(bar_group, GT);                         // this group's input planes free
+    if (k + 1 < nmy && !dead) load_tile(tile_of(k + 1));
+    if (!dead) {
+      const int tc = wr * 4 + t;
+      const bool interior = tile < nint;
+      const int64_t p0 = interior ? tile * T::TC : (tile - nint) * (int64_t(T::TC) * PS);
+      const int64_t left = interior ? geo.ni - p0 : geo.nb - p0;
+      const int npts = int(left < (interior ? T::TC : T::TC * PS) ? left : (interior ? T::TC : T::TC * PS));
+      const int step = interior ? Q : QB;
+      const int nrows = npts * step;
+      // 1. bias on the order-0 coefficient, stable tanh jet; H_L into the shared tile
+      double a1r[2][PS];
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int ch = wc * T::WCH + 8 * hh + g;
+        double z[S];
+#pragma unroll
+        for (int s = 0; s < S; ++s) z[s] = acc[s >> 1][2 * hh + (s & 1)];
+        if (interior) {
+          if (tc < npts) {
+            double hv[Q];
+            z[0] += bias_r[hh];
+            Jet<DIM, 3>::fwd(z, hv, a1r[hh][0]);
+#pragma unroll
+            for (int s = 0; s < Q; ++s) sH[(tc * Q + s) * LDH + ch] = hv[s];
+          } else {  // rows of points past the segment stay finite for the row contractions
+#pragma unroll
+            for (int s = 0; s < Q; ++s) sH[(tc * Q + s) * LDH + ch] = 0.0;
+          }
+        } else {
+#pragma unroll
+          for (int kq = 0; kq < PS; ++kq) {
+            const int lp = tc * PS + kq;
+            if (lp < npts) {
+              double zz[QB], hv[QB];
+#pragma unroll
+              for (int c = 0; c < QB; ++c) zz[c] = z[kq * QB + c];
+              zz[0] += bias_r[hh];
+              Jet<DIM, BO ? 1 : 0>::fwd(zz, hv, a1r[hh][kq]);
+#pragma unroll
+              for (int c = 0; c < QB; ++c) sH[(lp * QB + c) * LDH + ch] = hv[c];
+            } else {
+#pragma unroll
+              for (int c = 0; c < QB; ++c) sH[(lp * QB + c) * LDH + ch] = 0.0;
+            }
+          }
+        }
+      }
+      named_sync(bar_group, GT);
+      // 2. outputs Y^T[o][r] = W_L[o] . H[r] (+ b_L on order-0 rows) as DMMA tiles:
+      //    M = outputs (rows >= NF zero), N = tile rows (n8 tile j per warp), K = channels
+      const int kend = (nrows + 7) & ~7;
+      for (int j = lw; j < kend / 8; j += T::NWARPS) {
+        double c[4] = {0.0, 0.0, 0.0, 0.0};
+#pragma unroll
+        for (int kk = 0; kk < CP; kk += 8) {
+          const double a[4] = {g < NF ? sW[g * CP + kk + t] : 0.0, 0.0, g < NF ? sW[g * CP + kk + t + 4] : 0.0, 0.0};
+          mma_m16n8k8(c, a, sH[(8 * j + g) * LDH + kk + t], sH[(8 * j + g) * LDH + kk + t + 4]);
+        }
+        if (g < NF) {
+          const int r0 = 8 * j + 2 * t;
+          if (r0 < nrows) sY[r0 * NF + g] = c[0] + (r0 % step == 0 ? bL[g] : 0.0);
+          if (r0 + 1 < nrows) sY[(r0 + 1) * NF + g] = c[1] + ((r0 + 1) % step == 0 ? bL[g] : 0.0);
+        }
+      }
+      named_sync(bar_group, GT);
+      // 3. residual seeds, one point per thread (dY rows up to the next multiple of 8 zeroed)
+      for (int i = gtid; i < (kend - nrows) * NF; i += GT) sD[nrows * NF + i] = 0.0;
+      if (interior) {
+        if (gtid < npts) {
+          double y[Q * NF], dy[Q * NF];
+#pragma unroll
+          for (int k = 0; k < Q * NF; ++k) y[k] = sY[gtid * Q * NF + k];
+          lacc += interior_seed<DIM, HEAD>(y, pde_w[p0 + gtid], nu, gamma, dy);
+#pragma unroll
+          for (int k = 0; k < Q * NF; ++k) sD[gtid * Q * NF + k] = dy[k];
+        }
+      } else {
+        for (int pt = gtid; pt < npts; pt += GT) {
+          const int64_t b = p0 + pt;
+          const double* yr = sY + pt * QB * NF;
+          double* dr = sD + pt * QB * NF;
+#pragma unroll
+          for (int k = 0; k < QB * NF; ++k) dr[k] = 0.0;
+          double f[NFT];
+          if constexpr (BO == 0) {
+#pragma unroll
+            for (int o = 0; o < NF; ++o) f[o] = yr[o];
+          } else {
+            f[0] = yr[unit_row<DIM>(1) * NF + 0];   // u = psi_y
+            f[1] = -yr[unit_row<DIM>(0) * NF + 0];  // v = -psi_x
+            f[2] = yr[1];                           // p
+          }
+          double gsd[NFT];
+#pragma unroll
+          for (int o = 0; o < NFT; ++o) {
+            const double err = f[o] - target[b * NFT + o];
+            const double wgt = bnd_w[b * NFT + o];
+            lacc += bc * wgt * err * err;
+            gsd[o] = 2.0 * bc * wgt * err;
+          }
+          if constexpr (BO == 0) {
+#pragma unroll
+            for (int o = 0; o < NF; ++o) dr[o] = gsd[o];
+          } else {
+            dr[unit_row<DIM>(1) * NF + 0] = gsd[0];
+            dr[unit_row<DIM>(0) * NF + 0] = -gsd[1];
+            dr[1] = gsd[2];
+          }
+        }
+      }
+      named_sync(bar_group, GT);
+      // 4. output-layer gradients dW_L[o][c] += sum_r dY[r][o] H[r][c] as DMMA tiles (M =
+      //    outputs, N = channels 8 lw.., K = tile rows); db_L over order-0 rows
+      for (int k0 = 0; k0 < kend; k0 += 8) {
+        const double a[4] = {g < NF ? sD[(k0 + t) * NF + g] : 0.0, 0.0, g < NF ? sD[(k0 + t + 4) * NF + g] : 0.0, 0.0};
+        mma_m16n8k8(wacc, a, sH[(k0 + t) * LDH + 8 * lw + g], sH[(k0 + t + 4) * LDH + 8 * lw + g]);
+      }
+      if (gtid < NF)
+        for (int r = 0; r < nrows; r += step) bacc += sD[r * NF + gtid];
+      // 5. dgrad through W_L and the jet VJP of layer L on the owned (point, channel) pairs
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int ch = wc * T::WCH + 8 * hh + g;
+        if (interior) {
+          if (tc < npts) {
+            double hv[Q], dh[Q], zb[Q];
+#pragma unroll
+            for (int s = 0; s < Q; ++s) {
+              const int r = tc * Q + s;
+              double v = 0.0;
+#pragma unroll
+              for (int o = 0; o < NF; ++o) v += sD[r * NF + o] * sW[o * CP + ch];
+              dh[s] = v;
+              hv[s] = sH[r * LDH + ch];
+            }
+            Jet<DIM, 3>::vjp(hv, a1r[hh][0], dh, zb);
+            double* dst = dL + (p0 + tc) * Q * CP + ch;
+#pragma unroll
+            for (int s = 0; s < Q; ++s) dst[int64_t(s) * CP] = zb[s];
+            cacc[hh] += zb[0];
+          }
+        } else {
+#pragma unroll
+          for (int kq = 0; kq < PS; ++kq) {
+            const int lp = tc * PS + kq;
+            if (lp < npts) {
+              double hv[QB], dh[QB], zb[QB];
+#pragma unroll
+              for (int c = 0; c < QB; ++c) {
+                const int r = lp * QB + c;
+                double v = 0.0;
+#pragma unroll
+                for (int o = 0; o < NF; ++o) v += sD[r * NF + o] * sW[o * CP + ch];
+                dh[c] = v;
+                hv[c] = sH[r * LDH + ch];
+              }
+              Jet<DIM, BO ? 1 : 0>::vjp(hv, a1r[hh][kq], dh, zb);
+              double* dst = dL + (geo.ni * Q + (p0 + lp) * QB) * CP + ch;
+#pragma unroll
+              for (int c = 0; c < QB; ++c) dst[int64_t(c) * CP] = zb[c];
+              cacc[hh] += zb[0];
+            }
+          }
+        }
+      }
+    }
+  }
+  // turn counts balanced as in bwd_pingpong
+  if (gp == 0 && n0 == n1) named_sync(kPPBarTurn + 0, kPPThreads);
+  if (gp == 1 && n0 == n1 + 1) named_sync(kPPBarTurn + 1, kPPThreads);
+  if (__syncthreads_or(dead)) {
+    if (tid == 0) atomicExch(&g_device_fault, 1);
+    return;
+  }
+  // per-CTA partials, fixed-order reductions over the two groups
+  double* out = head_partial + int64_t(blockIdx.x) * PARTIAL;
+  double* red = smem;                          // [512] loss partials
+  double* cred = red + kPPThreads;             // [groups * WR][CP] bias partials of layer L-1
+  double* wsh = cred + kPPGroups * T::WR * CP;  // [8 warps][32 lanes][2] group 1's dW_L
+  double* bsh = wsh + T::NWARPS * 32 * 2;       // [NF] group 1's db_L
+  if (gp == 1) {
+    wsh[(lw * 32 + lane) * 2] = wacc[0];
+    wsh[(lw * 32 + lane) * 2 + 1] = wacc[1];
+    if (gtid < NF) bsh[gtid] = bacc;
+  }
+  red[tid] = lacc;
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    double v = cacc[hh];
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    if (t == 0) cred[(gp * T::WR + wr) * CP + wc * T::WCH + 8 * hh + g] = v;
+  }
+  __syncthreads();
+  if (gp == 0) {
+    if (g < NF) {
+      out[g * CP + 8 * lw + 2 * t] = wacc[0] + wsh[(lw * 32 + lane) * 2];
+      out[g * CP + 8 * lw + 2 * t + 1] = wacc[1] + wsh[(lw * 32 + lane) * 2 + 1];
+    }
+    if (gtid < NF) out[NF * CP + gtid] = bacc + bsh[gtid];
+  }
+  if (tid == 0) {
+    double sum = 0.0;
+    for (int i = 0; i < kPPThreads; ++i) sum += red[i];
+    out[NF * CP + NF] = sum;
+  }
+  for (int c = tid; c < CP; c += kPPThreads) {
+    double sum = 0.0;
+    for (int r = 0; r < kPPGroups * T::WR; ++r) sum += cred[r * CP + c];
+    out[NF * CP + NF + 1 + c] = sum;
+  }
+  if (tid == 0)
+    for (int b = 0; b < kPPGroups; ++b) mbar_inval(&bars[b]);
+}
+
 // Two-group ("ping-pong") form of fwd_head for 2-D: the last hidden layer, the output
 // layer, the residual seeds, the output-layer gradients and the VJP into layer L, with the
 // CTA's 16 warps in two 8-warp groups that take turns on the tensor pipe as in
@@ -2126,56 +2534,35 @@ __global__ void __launch_bounds__(HeadTile<DIM>::THREADS, HeadTile<DIM>::MINB)
 // about 70 FP64 operations per thread beyond the jet and its VJP, instead of staging
 // H_L, Y and dY in shared memory around output-layer MMAs of which 14 of 16 rows are zero.
 //
-// Output values a head's residual seed reads (and seeds), as flat indices s * NF + f (slot
-// s of a point, output f).  Interior points: the inputs of the generated seed formulas
-// (residual_generated.cuh; tests/test_codegen.py checks the lists against that file).
-// Boundary points with first-order rows (psi head): (psi_y, psi_x, p) per point, the slots
-// of u = psi_y, v = -psi_x and p; with value rows: every output of every point.
-template <int HEAD, int BO>
+// Output values the stream-function seed reads (and seeds), as flat indices s * NF + f
+// (slot s of a point, output f).  Interior points: the inputs of the generated seed formulas
+// (seed_psi_2d in residual_generated.cuh; tests/test_codegen.py checks the list against
+// that file).  Boundary points (first-order rows): (psi_y, psi_x, p) of each of a thread
+// column's PS points, the slots of u = psi_y, v = -psi_x and p.
 struct HeadOutputs {
-  static constexpr int NF = HeadTraits<HEAD>::NF;
-  static constexpr int Q = Basis<2>::Q, QB = BO ? 3 : 1, PS = Q / QB;
-  static_assert(!(BO && HEAD == FLASHNS_B200_HEAD_UVP), "first-order boundary rows carry the psi head");
-  static constexpr int NI = HEAD == FLASHNS_B200_HEAD_PSI ? 11 : 25;
-  static constexpr int NB = BO ? 3 * PS : PS * NF;
-  static constexpr int round8(int n) { return (n + 7) / 8 * 8; }
-  static constexpr int LDP = (round8(NI) > round8(NB) ? round8(NI) : round8(NB)) + 1;  // odd: conflict-free reads
-  // The (u, v, p) seed holds 25 outputs and 25 seeds at once; with H_L as well a thread
-  // would need more than its 128 registers, so that head keeps H_L in the thread's own
-  // shared-memory slots between the jet and the VJP (no other thread reads them).
-  static constexpr bool STASH = HEAD == FLASHNS_B200_HEAD_UVP;
+  static constexpr int NF = 2, Q = Basis<2>::Q, QB = 3, PS = Q / QB;
+  static constexpr int NI = 11, NB = 3 * PS;
+  static constexpr int LDP = 16 + 1;  // both lists padded to 8 lanes x 2; odd: conflict-free reads
   __host__ __device__ static constexpr int interior(int k) {
-    if constexpr (HEAD == FLASHNS_B200_HEAD_PSI) {
-      constexpr int v[11] = {2, 3, 4, 5, 6, 8, 10, 12, 14, 16, 18};
-      return v[k];
-    } else {
-      constexpr int v[25] = {0, 1, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15, 16, 17, 18, 19, 21, 22, 24, 25, 27, 28};
-      return v[k];
-    }
+    constexpr int v[NI] = {2, 3, 4, 5, 6, 8, 10, 12, 14, 16, 18};
+    return v[k];
   }
   __host__ __device__ static constexpr int boundary(int k) {
-    if constexpr (BO) {
-      const int kq = k / 3, j = k % 3;  // j: psi_y, psi_x, p of point kq
-      return j == 0 ? (kq * QB + unit_row<2>(1)) * NF : j == 1 ? (kq * QB + unit_row<2>(0)) * NF : kq * QB * NF + 1;
-    } else {
-      return k;  // point k / NF, output k % NF
-    }
+    const int kq = k / 3, j = k % 3;  // j: psi_y, psi_x, p of point kq
+    return j == 0 ? (kq * QB + unit_row<2>(1)) * NF : j == 1 ? (kq * QB + unit_row<2>(0)) * NF : kq * QB * NF + 1;
   }
 };
 
-template <int BO, int HEAD>
 constexpr size_t hpp_smem_bytes() {
-  using HO = HeadOutputs<HEAD, BO>;
+  using HO = HeadOutputs;
   constexpr size_t planes = size_t(kFusedWidth / KC) * PPTile::TR * LDC;  // one group's input half tile
   constexpr size_t parts = size_t(kPPGroups) * PPTile::WR * 4 * PPTile::WC * HO::LDP;
   constexpr size_t lead = size_t(kPPGroups) * PPTile::WR * 4 * (HO::NF + 1);
-  constexpr size_t stash = HO::STASH ? size_t(2) * PPTile::S * kPPThreads : 0;
   return sizeof(double) * (kPPGroups * planes + size_t(kFusedWidth) * (kFusedWidth + 4) +
-                           size_t(HO::NF) * (kFusedWidth + 1) + parts + lead + stash + kPPGroups);
+                           size_t(HO::NF) * (kFusedWidth + 1) + parts + lead + kPPGroups);
 }
 enum { kPPBarRows = 5 };  // named barriers 5 + group * 2 + row group: the 4 channel warps (128 threads)
 
-template <int BO, int HEAD>
 __global__ void __launch_bounds__(kPPThreads, 1)
     head_pingpong(const __grid_constant__ CUtensorMap tm_in_i, const __grid_constant__ CUtensorMap tm_in_b,
                   const double* __restrict__ hin, const double* __restrict__ w, const double* __restrict__ bias,
@@ -2184,8 +2571,9 @@ __global__ void __launch_bounds__(kPPThreads, 1)
                   double bc, double* __restrict__ dL, double* __restrict__ head_partial, Geometry geo) {
   constexpr int DIM = 2, CP = kFusedWidth;
   using T = PPTile;
+  constexpr int BO = 1, HEAD = FLASHNS_B200_HEAD_PSI;
   using TL = Tiles<DIM, BO, T::TC>;
-  using HO = HeadOutputs<HEAD, BO>;
+  using HO = HeadOutputs;
   constexpr int S = T::S, TR = T::TR, Q = TL::Q, QB = TL::QB, PS = TL::PS;
   constexpr int NF = HO::NF;
   constexpr int NFT = (HEAD == FLASHNS_B200_HEAD_PSI && BO) ? 3 : NF;  // boundary target fields
@@ -2196,7 +2584,6 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   constexpr bool SPLIT = BB != TR;
   constexpr int GT = T::THREADS;
   constexpr int PLANES = NK * TR * LDC;
-  constexpr bool STASH = HO::STASH;
   static_assert(T::WC == 4 && T::WR == 2 && T::TC == 8, "4 channel warps x 2 row groups of 4 thread columns");
   static_assert(NK == 2 && KC == 32 && TR <= 256, "TMA boxes: 36 columns, at most 256 rows");
   static_assert((size_t(PLANES) * sizeof(double)) % 128 == 0, "group planes on 128-byte boundaries");
@@ -2214,8 +2601,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   double* sW = sA + CP * LDA;                 // W_L [NF][CP], then b_L [NF]
   double* sP = sW + NF * CP + NF;             // output partials [group][row group][thread column][wc][LDP]
   double* sL = sP + kPPGroups * T::WR * 4 * T::WC * LDP;  // per lead thread: loss, db_L [NF]
-  double* sHs = sL + kPPGroups * T::WR * 4 * (NF + 1);     // STASH: H_L [2][S][threads]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sHs + (STASH ? 2 * S * kPPThreads : 0));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sL + kPPGroups * T::WR * 4 * (NF + 1));
   uint64_t* bar_in = bars + gp;
   const int bar_group = kPPBarGroup + gp;
   const int bar_rows = kPPBarRows + gp * T::WR + wr;
@@ -2354,20 +2740,11 @@ __global__ void __launch_bounds__(kPPThreads, 1)
 #pragma unroll
             for (int c = 0; c < QB; ++c) zz[c] = z[kq * QB + c];
             zz[0] += bias[wc * T::WCH + 8 * hh + g];
-            Jet<DIM, BO ? 1 : 0>::fwd(zz, hv[hh] + kq * QB, a1r[hh][kq]);
+            Jet<DIM, 1>::fwd(zz, hv[hh] + kq * QB, a1r[hh][kq]);
           }
         }
       }
-      if constexpr (STASH) {
-#pragma unroll
-        for (int s = 0; s < S; ++s) sHs[(hh * S + s) * kPPThreads + tid] = hv[hh][s];
-      }
     }
-    // H_L of this thread: registers, or the thread's own shared-memory slots (STASH)
-    auto hval = [&](int hh, int s) {
-      if constexpr (STASH) return sHs[(hh * S + s) * kPPThreads + tid];
-      else return hv[hh][s];
-    };
     // 2-4. outputs, seeds, output-layer gradients, dgrad through W_L, VJP: per tile kind
     auto finish = [&](auto kind) {
       constexpr bool INTERIOR = decltype(kind)::value;
@@ -2379,7 +2756,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
       auto share = [&](int k) {
         if (k >= NY) return 0.0;
         const int s = index(k) / NF, o = index(k) % NF;
-        return hval(0, s) * wl[o][0] + hval(1, s) * wl[o][1];
+        return hv[0][s] * wl[o][0] + hv[1][s] * wl[o][1];
       };
       // reduce-scatter over the 8 lanes of this thread column (g = lane >> 2): after the
       // steps over lane bits 4, 3, 2 lane g holds the sums of values [g*H3, g*H3 + H3)
@@ -2430,14 +2807,9 @@ __global__ void __launch_bounds__(kPPThreads, 1)
           const int64_t b = p0 + tc * PS + kq;
           const bool valid = tc * PS + kq < npts;
           double f[NFT];
-          if constexpr (BO == 0) {
-#pragma unroll
-            for (int o = 0; o < NF; ++o) f[o] = y[kq * PER + o];
-          } else {
-            f[0] = y[kq * PER + 0];   // u = psi_y
-            f[1] = -y[kq * PER + 1];  // v = -psi_x
-            f[2] = y[kq * PER + 2];   // p
-          }
+          f[0] = y[kq * PER + 0];   // u = psi_y
+          f[1] = -y[kq * PER + 1];  // v = -psi_x
+          f[2] = y[kq * PER + 2];   // p
           double gsd[NFT];
 #pragma unroll
           for (int o = 0; o < NFT; ++o) {
@@ -2446,14 +2818,9 @@ __global__ void __launch_bounds__(kPPThreads, 1)
             if (valid && lead) lslot[0] += bc * wgt * err * err;
             gsd[o] = 2.0 * bc * wgt * err;
           }
-          if constexpr (BO == 0) {
-#pragma unroll
-            for (int o = 0; o < NF; ++o) dy[kq * PER + o] = gsd[o];
-          } else {
-            dy[kq * PER + 0] = gsd[0];
-            dy[kq * PER + 1] = -gsd[1];
-            dy[kq * PER + 2] = gsd[2];
-          }
+          dy[kq * PER + 0] = gsd[0];
+          dy[kq * PER + 1] = -gsd[1];
+          dy[kq * PER + 2] = gsd[2];
         }
       }
       // output-layer gradients: dW_L[o][ch] += dY[s][o] H_L[s][ch] over this column's
@@ -2461,8 +2828,8 @@ __global__ void __launch_bounds__(kPPThreads, 1)
 #pragma unroll
       for (int kk = 0; kk < NY; ++kk) {
         const int s = index(kk) / NF, o = index(kk) % NF;
-        wacc[o][0] += dy[kk] * hval(0, s);
-        wacc[o][1] += dy[kk] * hval(1, s);
+        wacc[o][0] += dy[kk] * hv[0][s];
+        wacc[o][1] += dy[kk] * hv[1][s];
         if (s % STEP == 0 && lead) lslot[1 + o] += dy[kk];
       }
       // dgrad through W_L and the jet VJP of layer L on the owned (point, channel) pairs
@@ -2476,10 +2843,8 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         for (int kk = 0; kk < NY; ++kk) dh[index(kk) / NF] += dy[kk] * wl[index(kk) % NF][hh];
         if constexpr (INTERIOR) {
           if (tc < npts) {
-            double zb[Q], hr[Q];
-#pragma unroll
-            for (int s = 0; s < Q; ++s) hr[s] = hval(hh, s);
-            Jet<DIM, 3>::vjp(hr, a1r[hh][0], dh, zb);
+            double zb[Q];
+            Jet<DIM, 3>::vjp(hv[hh], a1r[hh][0], dh, zb);
             double* dst = dL + (p0 + tc) * Q * CP + ch;
 #pragma unroll
             for (int s = 0; s < Q; ++s) dst[int64_t(s) * CP] = zb[s];
@@ -2490,10 +2855,8 @@ __global__ void __launch_bounds__(kPPThreads, 1)
           for (int kq = 0; kq < PS; ++kq) {
             const int lp = tc * PS + kq;
             if (lp < npts) {
-              double zb[QB], hr[QB];
-#pragma unroll
-              for (int c = 0; c < QB; ++c) hr[c] = hval(hh, kq * QB + c);
-              Jet<DIM, BO ? 1 : 0>::vjp(hr, a1r[hh][kq], dh + kq * QB, zb);
+              double zb[QB];
+              Jet<DIM, 1>::vjp(hv[hh] + kq * QB, a1r[hh][kq], dh + kq * QB, zb);
               double* dst = dL + (geo.ni * Q + (p0 + lp) * QB) * CP + ch;
 #pragma unroll
               for (int c = 0; c < QB; ++c) dst[int64_t(c) * CP] = zb[c];
@@ -2944,6 +3307,39 @@ struct FusedOps {
   }
 };
 
+// Dense dgrad (+ jet VJP) of a 2-D 64 -> 64 layer for the reference-ABI hook
+// (flashns_stable_dgrad_vjp, hooks.cu): the two-group backward kernel without its weight
+// gradient, over dense rows [batch * Q][64] (all points full jets).  d and h must be 16-byte
+// aligned (TMA); rows are counted in int32 by the tensor maps.
+template <int MODE>
+cudaError_t launch_dense_dgrad_pingpong(const double* d, const double* w, const double* h, const double* aux,
+                                        double* out, int batch, cudaStream_t stream) {
+  using TL = Tiles<2, 0, PPTile::TC>;
+  constexpr int TR = PPTile::TR;
+  const int64_t rows = int64_t(batch) * TL::Q;
+  if (rows > INT32_MAX - TR) return cudaErrorInvalidValue;
+  const Geometry g{batch, 0, rows};
+  cudaError_t e = allow_smem(bwd_pingpong<0, false, MODE>, pp_smem_bytes());
+  if (e != cudaSuccess) return e;
+  int device = 0, sms = 0;
+  if ((e = cudaGetDevice(&device)) != cudaSuccess ||
+      (e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess)
+    return e;
+  const int64_t pairs = (TL::interior(batch) + 1) / 2;
+  const int grid = int(pairs < sms ? pairs : sms);
+  CUtensorMap m[4];
+  const double* hm = MODE == kHookDgradVjp ? h : d;  // dgrad only: H is never read
+  if ((e = row_tensor_map(&m[0], d, rows, kFusedWidth, LDC, TR)) != cudaSuccess ||
+      (e = row_tensor_map(&m[1], d, 0, kFusedWidth, LDC, TR)) != cudaSuccess ||
+      (e = row_tensor_map(&m[2], hm, rows, kFusedWidth, LDC, TR)) != cudaSuccess ||
+      (e = row_tensor_map(&m[3], hm, 0, kFusedWidth, LDC, TR)) != cudaSuccess)
+    return e;
+  t_programmatic = false;
+  return launch_kernel(bwd_pingpong<0, false, MODE>, grid, kPPThreads, pp_smem_bytes(), stream, m[0], m[1], m[2],
+                       m[3], d, hm, w, aux, out, static_cast<const double*>(nullptr), static_cast<double*>(nullptr),
+                       static_cast<double*>(nullptr), g);
+}
+
 template <bool FIRST, typename F>
 bool with_fused(int dim, int bo, F&& f) {
   if (dim == 2 && bo == 0) { f(FusedOps<2, 0, FIRST>{}); return true; }
@@ -2979,12 +3375,20 @@ template <int DIM, int BO, int HEAD>
 struct FwdHeadOps {
   static constexpr int NF = HeadTraits<HEAD>::NF;
   static constexpr bool kPingPong = DIM == 2;  // 2-D: the two-group kernel over 80-row half tiles
+  // the stream-function head with first-order boundary rows keeps its epilogue in registers
+  static constexpr bool kRegisters = BO == 1 && HEAD == FLASHNS_B200_HEAD_PSI;
   static cudaError_t setup(int& occ) {
-    if constexpr (kPingPong) {
-      constexpr size_t smem = hpp_smem_bytes<BO, HEAD>();
+    if constexpr (kPingPong && kRegisters) {
+      constexpr size_t smem = hpp_smem_bytes();
       static_assert(smem <= kMaxSmem, "two-group head tile exceeds shared memory");
-      cudaError_t e = allow_smem(head_pingpong<BO, HEAD>, smem);
-      occ = occupancy(head_pingpong<BO, HEAD>, smem, kPPThreads);
+      cudaError_t e = allow_smem(head_pingpong, smem);
+      occ = occupancy(head_pingpong, smem, kPPThreads);
+      return e;
+    } else if constexpr (kPingPong) {
+      constexpr size_t smem = hpp_staged_smem_bytes<NF>();
+      static_assert(smem <= kMaxSmem, "two-group head tile exceeds shared memory");
+      cudaError_t e = allow_smem(head_pingpong_staged<BO, HEAD>, smem);
+      occ = occupancy(head_pingpong_staged<BO, HEAD>, smem, kPPThreads);
       return e;
     } else {
       constexpr size_t smem = fwd_head_smem_bytes<DIM, NF>();
@@ -3016,8 +3420,12 @@ struct FwdHeadOps {
       if ((e = row_tensor_map(&m[0], hin, ri, kFusedWidth, LDC, TR)) != cudaSuccess ||
           (e = row_tensor_map(&m[1], hin + ri * kFusedWidth, rb, kFusedWidth, LDC, BB)) != cudaSuccess)
         return e;
-      return launch_kernel(head_pingpong<BO, HEAD>, grid, kPPThreads, hpp_smem_bytes<BO, HEAD>(), st, m[0], m[1], hin, w,
-                           b, wl, bl, pw, bw, tg, nu, gm, bc, dl, hpart, g);
+      if constexpr (kRegisters)
+        return launch_kernel(head_pingpong, grid, kPPThreads, hpp_smem_bytes(), st, m[0], m[1], hin, w, b, wl, bl, pw,
+                             bw, tg, nu, gm, bc, dl, hpart, g);
+      else
+        return launch_kernel(head_pingpong_staged<BO, HEAD>, grid, kPPThreads, hpp_staged_smem_bytes<NF>(), st, m[0],
+                             m[1], hin, w, b, wl, bl, pw, bw, tg, nu, gm, bc, dl, hpart, g);
     } else {
       return launch_kernel(fwd_head<DIM, BO, HEAD>, grid, HeadTile<DIM>::THREADS, fwd_head_smem_bytes<DIM, NF>(), st,
                            hin, w, b, wl, bl, pw, bw, tg, nu, gm, bc, dl, hpart, g);
@@ -3102,6 +3510,13 @@ int first_launch(int dim, int bo, int grid, cudaStream_t st, const double* x, co
 }
 
 }  // namespace
+
+// The dense 64 -> 64 dgrad (+ VJP) for the reference-ABI hook in hooks.cu
+cudaError_t flashns_b200::dense_dgrad_64(bool fused, const double* d, const double* w, const double* h,
+                                         const double* aux, double* out, int batch, cudaStream_t stream) {
+  return fused ? launch_dense_dgrad_pingpong<kHookDgradVjp>(d, w, h, aux, out, batch, stream)
+               : launch_dense_dgrad_pingpong<kHookDgrad>(d, w, h, aux, out, batch, stream);
+}
 
 // ======================================================================================
 extern "C" {

@@ -25,6 +25,10 @@
 #include "residual_generated.cuh"
 
 namespace flashns_b200 {
+// eval.cu: the dense dgrad (+ VJP) of a 2-D 64 -> 64 layer on the evaluation's two-group
+// backward kernel without its weight gradient
+cudaError_t dense_dgrad_64(bool fused, const double* d, const double* w, const double* h, const double* aux,
+                           double* out, int batch, cudaStream_t stream);
 namespace {
 
 constexpr int kHookThreads = 128;
@@ -261,19 +265,29 @@ __global__ void __launch_bounds__(kHookThreads)
 // warps owns 16 channels of 4 samples, and a thread's accumulators hold, for its two
 // channels, all Q rows of one sample: the VJP needs no data exchange.  Tiles are (sample
 // block, channel block) pairs, grid-strided over a persistent grid of two CTAs per SM in
-// 2-D.  K streams through a two-stage ring of 32-column chunks of D and W that runs on
-// across tiles: the first chunk of a CTA's next tile is in flight while it runs the
-// current tile's epilogue, and the other CTA on the SM keeps the tensor pipe busy
-// meanwhile.  Copies are 16-byte cp.async when the rows allow it (even cout and cin,
-// 16-byte aligned D and W), 8-byte otherwise, zero-filled past the ends, so any cout and
-// cin work.  The tile's H rows and a1 values (contiguous ranges) are prefetched into L2
-// when the tile starts; the epilogue reads them from there.
+// 2-D.  K streams through a two-stage ring of 32-column chunks of D that runs on across
+// tiles: the first chunk of a CTA's next tile is in flight while it runs the current
+// tile's epilogue, and the other CTA on the SM keeps the tensor pipe busy meanwhile.  W
+// stays resident in shared memory when one channel block covers cin (cin <= 64) and
+// cout <= 128 (the layers of the reference's nets); otherwise its chunks stream beside
+// D's.  Copies are 16-byte cp.async when the rows allow it (even cout and cin, 16-byte
+// aligned D and W), 8-byte otherwise, zero-filled past the ends, so any cout and cin work.
+// The tile's H rows and a1 values (contiguous ranges) are prefetched into L2 when the
+// tile starts; the epilogue reads them from there.
 constexpr int kDgThreads = 256, kDgKC = 32, kDgLDC = kDgKC + 4, kDgCB = 64, kDgLDW = kDgCB + 4;
-constexpr int kDgTC = 8;  // samples per tile
+constexpr int kDgTC = 8;             // samples per tile
+constexpr int kDgResidentRows = 128;  // largest cout (rounded up to KC) kept resident
 
+// W resident: one channel block and cout within the resident rows
+inline bool dgrad_resident(int cout, int cin) { return cin <= kDgCB && cout <= kDgResidentRows; }
 template <int DIM>
-constexpr size_t dgrad_smem_bytes() {
-  return sizeof(double) * 2 * (size_t(kDgTC) * Q_<DIM>::v * kDgLDC + size_t(kDgKC) * kDgLDW);
+constexpr size_t dgrad_smem_bytes(int w_rows) {
+  return sizeof(double) * (2 * size_t(kDgTC) * Q_<DIM>::v * kDgLDC + size_t(w_rows) * kDgLDW);
+}
+template <int DIM>
+size_t dgrad_smem_bytes_for(int cout, int cin) {
+  const int nk = (cout + kDgKC - 1) / kDgKC;
+  return dgrad_smem_bytes<DIM>(dgrad_resident(cout, cin) ? nk * kDgKC : 2 * kDgKC);
 }
 
 __device__ __forceinline__ void cp_async8(void* smem, const void* gmem, bool valid) {
@@ -284,11 +298,12 @@ __device__ __forceinline__ void cp_async8(void* smem, const void* gmem, bool val
 template <int DIM, bool FUSED>
 __global__ void __launch_bounds__(kDgThreads, DIM == 2 ? 2 : 1)
     dense_dgrad(const double* __restrict__ d, const double* __restrict__ w, const double* __restrict__ h,
-                const double* __restrict__ aux, double* __restrict__ out, int batch, int cout, int cin, bool vec) {
+                const double* __restrict__ aux, double* __restrict__ out, int batch, int cout, int cin, bool vec,
+                bool resident) {
   constexpr int Q = Q_<DIM>::v, TR = kDgTC * Q, NT = Q / 2, LDC = kDgLDC, LDW = kDgLDW, KC = kDgKC;
   extern __shared__ __align__(16) double dsm[];
   double* sD = dsm;                 // [2][TR][LDC]   D chunk: rows of the tile, 32 output channels
-  double* sW = dsm + 2 * TR * LDC;  // [2][KC][LDW]   W chunk: 32 output channels, 64 input channels
+  double* sW = dsm + 2 * TR * LDC;  // W: [nk*KC][LDW] resident, or [2][KC][LDW] chunks
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int wc = warp % 4, wr = warp / 4;  // 16-channel slice, sample group (4 samples)
   const int64_t sample_tiles = (int64_t(batch) + kDgTC - 1) / kDgTC;
@@ -313,6 +328,7 @@ __global__ void __launch_bounds__(kDgThreads, DIM == 2 ? 2 : 1)
         const bool ok = r < rows_left && o < cout;  // cout even: o < cout covers o + 1
         cp_async16(dD + r * LDC + c, ok ? d + (b0 * Q + r) * cout + o : d, ok);
       }
+      if (resident) return;
       for (int e = tid; e < KC * (kDgCB / 2); e += kDgThreads) {
         const int r = e / (kDgCB / 2), c = 2 * (e % (kDgCB / 2)), o = kc * KC + r, i = i0 + c;
         const bool ok = o < cout && i < cin;  // cin even: i < cin covers i + 1
@@ -324,6 +340,7 @@ __global__ void __launch_bounds__(kDgThreads, DIM == 2 ? 2 : 1)
         const bool ok = r < rows_left && o < cout;
         cp_async8(dD + r * LDC + c, ok ? d + (b0 * Q + r) * cout + o : d, ok);
       }
+      if (resident) return;
       for (int e = tid; e < KC * kDgCB; e += kDgThreads) {
         const int r = e / kDgCB, c = e % kDgCB, o = kc * KC + r, i = i0 + c;
         const bool ok = o < cout && i < cin;
@@ -332,6 +349,13 @@ __global__ void __launch_bounds__(kDgThreads, DIM == 2 ? 2 : 1)
     }
   };
   double acc[NT][4];
+  if (resident && steps > 0) {  // W [nk*KC][64], zero past cout and cin; joins the first chunk's group
+    for (int e = tid; e < nk * KC * kDgCB; e += kDgThreads) {
+      const int o = e / kDgCB, i = e % kDgCB;
+      const bool ok = o < cout && i < cin;
+      cp_async8(sW + o * LDW + i, ok ? w + int64_t(o) * cin + i : w, ok);
+    }
+  }
   if (steps > 0) load(0, 0);
   cp_async_commit();
   for (int64_t step = 0; step < steps; ++step) {
@@ -360,7 +384,7 @@ __global__ void __launch_bounds__(kDgThreads, DIM == 2 ? 2 : 1)
     cp_async_wait<1>();  // chunk `step` landed (this thread's copies)
     __syncthreads();     // ... and every other thread's
     const double* cB = sD + (step & 1) * TR * LDC + brow * LDC;
-    const double* cA = sW + (step & 1) * KC * LDW + wc * 16;
+    const double* cA = sW + (resident ? kc : int(step & 1)) * KC * LDW + wc * 16;
 #pragma unroll
     for (int kk = 0; kk < KC; kk += 8) {
       double a[4];
@@ -403,10 +427,12 @@ __global__ void __launch_bounds__(kDgThreads, DIM == 2 ? 2 : 1)
 template <int DIM, bool FUSED>
 cudaError_t launch_dense_dgrad(const double* d, const double* w, const double* h, const double* aux, double* out,
                                int batch, int cout, int cin, cudaStream_t stream) {
-  constexpr size_t smem = dgrad_smem_bytes<DIM>();
+  const bool resident = dgrad_resident(cout, cin);
+  const size_t smem = dgrad_smem_bytes_for<DIM>(cout, cin);
   // a per-device attribute (host-side, not a stream operation): set on every call, so that
   // each device the caller switches to gets it
-  cudaError_t e = cudaFuncSetAttribute(dense_dgrad<DIM, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  cudaError_t e = cudaFuncSetAttribute(dense_dgrad<DIM, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(dgrad_smem_bytes<DIM>(kDgResidentRows)));
   if (e != cudaSuccess) return e;
   int device = 0, sms = 0, per_sm = 0;
   e = cudaGetDevice(&device);
@@ -414,11 +440,11 @@ cudaError_t launch_dense_dgrad(const double* d, const double* w, const double* h
   if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dense_dgrad<DIM, FUSED>, kDgThreads, smem);
   if (e != cudaSuccess) return e;
   const int64_t units = ((int64_t(batch) + kDgTC - 1) / kDgTC) * ((cin + kDgCB - 1) / kDgCB);
-  const int64_t resident = int64_t(sms) * (per_sm > 0 ? per_sm : 1);
-  const unsigned grid = unsigned(units < resident ? units : resident);
+  const int64_t slots = int64_t(sms) * (per_sm > 0 ? per_sm : 1);
+  const unsigned grid = unsigned(units < slots ? units : slots);
   const bool vec = cout % 2 == 0 && cin % 2 == 0 && (reinterpret_cast<uintptr_t>(d) & 15) == 0 &&
                    (reinterpret_cast<uintptr_t>(w) & 15) == 0;
-  dense_dgrad<DIM, FUSED><<<grid, kDgThreads, smem, stream>>>(d, w, h, aux, out, batch, cout, cin, vec);
+  dense_dgrad<DIM, FUSED><<<grid, kDgThreads, smem, stream>>>(d, w, h, aux, out, batch, cout, cin, vec, resident);
   return cudaGetLastError();
 }
 
@@ -747,13 +773,19 @@ int flashns_stable_dgrad_vjp(int dim, bool fused, const double* d, const double*
   if (overlaps(out, no * 8, d, size_t(batch) * q * cout * 8) || overlaps(out, no * 8, w, size_t(cout) * cin * 8) ||
       (fused && (overlaps(out, no * 8, h, no * 8) || overlaps(out, no * 8, aux, size_t(batch) * cin * 8))))
     return int(cudaErrorInvalidValue);
+  // 2-D 64 -> 64 (the reference's nets): the two-group backward kernel of the evaluation,
+  // TMA-fed, without its weight gradient; other shapes: the general kernel above
+  const auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (dim == 2 && cout == 64 && cin == 64 && aligned(d) && aligned(w) && (!fused || aligned(h)) &&
+      int64_t(batch) * 10 <= INT32_MAX / 2)
+    return int(flashns_b200::dense_dgrad_64(fused, d, w, h, aux, out, batch, stream));
   if (dim == 2 && fused) return int(launch_dense_dgrad<2, true>(d, w, h, aux, out, batch, cout, cin, stream));
   if (dim == 2) return int(launch_dense_dgrad<2, false>(d, w, h, aux, out, batch, cout, cin, stream));
   if (fused) return int(launch_dense_dgrad<3, true>(d, w, h, aux, out, batch, cout, cin, stream));
   return int(launch_dense_dgrad<3, false>(d, w, h, aux, out, batch, cout, cin, stream));
 }
 
-int flashns_stable_dgrad_shared_bytes() { return int(flashns_b200::dgrad_smem_bytes<2>()); }
+int flashns_stable_dgrad_shared_bytes() { return int(flashns_b200::dgrad_smem_bytes_for<2>(64, 64)); }
 
 }  // extern "C"
 
@@ -811,8 +843,9 @@ int dgrad_resources(long long* values) {
   cudaFuncAttributes attr;
   cudaError_t e = cudaFuncGetAttributes(&attr, dense_dgrad<DIM, FUSED>);
   if (e != cudaSuccess) return int(e);
-  constexpr size_t smem = dgrad_smem_bytes<DIM>();
-  e = cudaFuncSetAttribute(dense_dgrad<DIM, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  const size_t smem = dgrad_smem_bytes_for<DIM>(64, 64);  // the shape of the reference's plans
+  e = cudaFuncSetAttribute(dense_dgrad<DIM, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           int(dgrad_smem_bytes<DIM>(kDgResidentRows)));
   if (e != cudaSuccess) return int(e);
   int blocks = 0;
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, dense_dgrad<DIM, FUSED>, kDgThreads, smem);

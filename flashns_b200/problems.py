@@ -265,10 +265,13 @@ def config_parameters(name, seed=0):
     return reference_parameters(c["widths"]) if c.get("init") == "reference" else xavier_normal(c["widths"], seed)
 
 
-def config_points(name, *, scale=1, seed=1, boundary_order=None):
+def config_points(name, *, scale=1, seed=1, boundary_order=None, divisor=1):
+    """The configuration's point set, `scale` times as many points (weak scaling), or
+    1/`divisor` of them (small profiling cases of the same kernels)."""
     c = CONFIGS[name]
+    ni, nb = c["interior"] * scale // divisor, c["boundary"] * scale // divisor
     if c["kind"] == "reference_case":
-        return reference_case(c["interior"] * scale)
+        return reference_case(ni)
     build = kovasznay if c["kind"] == "kovasznay" else taylor_green
     order = c.get("boundary_order", 1) if boundary_order is None else boundary_order
-    return build(c["interior"] * scale, c["boundary"] * scale, seed=seed, boundary_order=order)
+    return build(ni, nb, seed=seed, boundary_order=order)

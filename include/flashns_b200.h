@@ -264,7 +264,7 @@ int flashns_b200_philox_points(uint64_t key0, uint64_t key1, int dim, int64_t fi
 int flashns_b200_pack_coordinates(const double* x, int64_t full_points, int64_t value_points, int dim, double* out,
                                   cudaStream_t stream);
 
-/* dynamic shared memory per CTA of the dense dgrad (its 2-D kernel) */
+/* dynamic shared memory per CTA of the dense dgrad (its 2-D kernel, 64 -> 64) */
 int flashns_stable_dgrad_shared_bytes(void);
 
 /* Plan-based dense dgrad under the reference's Hopper names

@@ -35,18 +35,19 @@ def test_uvp_polynomials_match_reference_residual_table():
 
 
 def test_head_output_lists_match_the_generated_seeds():
-    """The two-group head forms only the output values its residual seed reads
-    (HeadOutputs in eval.cu); those lists must be exactly the y[...] inputs (and dy[...]
-    outputs) of the generated seed formulas, or a seed would read a value never formed."""
+    """The register form of the two-group head forms only the output values the
+    stream-function seed reads (HeadOutputs in eval.cu); that list must be exactly the
+    y[...] inputs (and dy[...] outputs) of the generated seed formula, or the seed would
+    read a value never formed."""
     import re
     from pathlib import Path
     csrc = Path(codegen.__file__).resolve().parent / "csrc"
     seeds = (csrc / "residual_generated.cuh").read_text()
     source = (csrc / "eval.cu").read_text()
     block = source[source.index("struct HeadOutputs"):source.index("hpp_smem_bytes")]
-    lists = [[int(v) for v in m.split(",")] for m in re.findall(r"constexpr int v\[\d+\] = \{([^}]*)\}", block)]
-    assert len(lists) == 2
-    for name, listed in (("seed_psi_2d", lists[0]), ("seed_uvp_2d", lists[1])):
+    lists = [[int(v) for v in m.split(",")] for m in re.findall(r"constexpr int v\[\w+\] = \{([^}]*)\}", block)]
+    assert len(lists) == 1
+    for name, listed in (("seed_psi_2d", lists[0]),):
         body = seeds[seeds.index(name + "("):]
         body = body[:body.index("\n}\n")]
         used = sorted({int(i) for i in re.findall(r"\by\[(\d+)\]", body)})
