@@ -157,11 +157,12 @@ def test_hook_entry_points_check_arguments_before_any_launch(library):
 def test_fp64_probe_rejects_bad_launch_shapes(library):
     """The peak-table probe checks its kind and launch shape before launching."""
     from flashns_b200 import _lib
+    from baseline.fp64_peak import KINDS
     lib = _lib.library()
     sink, flops = ctypes.c_void_p(4096), ctypes.c_double()
     probe = lambda kind, blocks, threads, iters, s=sink: lib.flashns_b200_fp64_probe(kind, blocks, threads, iters, s,
                                                                                       ctypes.byref(flops), None)
-    # kinds 0..5: m16n8k8, m8n8k4, m16n8k4, m16n8k16, dfma, shared-memory-fed m16n8k8
+    assert sorted(KINDS.values()) == list(range(6))
     assert probe(6, 148, 256, 10) == 1 and probe(-1, 148, 256, 10) == 1
     assert probe(1, 148, 100, 10) == 1 and probe(1, 148, 2048, 10) == 1     # threads
     assert probe(0, 148, 512, 10) == 1                                      # m16n8k8 runs at 256 threads

@@ -1,5 +1,7 @@
 """GPU (NCCL, 2 ranks on 2 GPUs; skipped with fewer): the sharded evaluation with one
-all-reduce equals the single-GPU evaluation of the whole point set."""
+all-reduce equals the single-GPU evaluation of the whole point set and the oracle.  The
+shards split 4,099 interior and 1,031 boundary points 2,049 / 2,050 and 515 / 516, so both
+shard boundaries cut through a tile of the kernels."""
 
 import os
 import socket
@@ -67,3 +69,11 @@ def test_two_gpu_allreduce_matches_single_gpu():
     assert np.array_equal(outs[0], outs[1])  # identical bytes on every rank
     rel = np.linalg.norm(outs[0] - expected) / np.linalg.norm(expected)
     assert rel <= 1e-12
+    from oracle.evaluate import evaluate
+    from tests.cases import close_ratio, rel_norm
+    loss, grads = evaluate(pts.x.numpy(), pts.interior_count, pts.pde_weights.numpy(), pts.boundary_weights.numpy(),
+                           pts.target.numpy(), [w.numpy() for w in ws], [b.numpy() for b in bs], head="psi",
+                           nu=pts.viscosity, boundary_order=1)
+    reference = np.concatenate([g.reshape(-1) for g in grads] + [[loss]])
+    assert close_ratio(outs[0], reference) <= 1.0
+    assert rel_norm(outs[0], reference) <= 1e-10
