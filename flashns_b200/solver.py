@@ -40,14 +40,17 @@ def acceptance_grid(n=201):
 
 
 class Acceptance:
-    """Relative L2 errors of (u, v, p) on the grid against the analytic solution."""
+    """Relative L2 errors of (u, v, p) on the grid against the analytic solution.  The
+    stream-function head gives (u, v, p) = (psi_y, -psi_x, p) from first-order rows, the
+    (u, v, p) head its raw outputs from value rows."""
 
-    def __init__(self, widths, re, device, n=201):
+    def __init__(self, widths, re, device, n=201, head="psi"):
         grid = acceptance_grid(n)
         u, v, p, _ = kovasznay_exact(grid, re)
         self.exact = torch.stack((u, v, p), 1).to(device)
         self.norm = self.exact.square().sum(0).sqrt()
-        self.fields = FieldEvaluator(grid, widths, head="psi", boundary_order=1, device=device)
+        self.fields = FieldEvaluator(grid, widths, head=head, boundary_order=1 if head == "psi" else 0,
+                                     device=device)
 
     def __call__(self, flat):
         f = self.fields(flat)
@@ -68,24 +71,39 @@ def load_checkpoint(path):
     return torch.load(Path(path), map_location="cpu", weights_only=True)
 
 
-def solve(*, interior=16384, boundary=4096, widths=(2, 64, 64, 64, 64, 2), re=20.0, seed=1, init_seed=0,
+def solve(*, interior=16384, boundary=4096, widths=None, re=20.0, seed=1, init_seed=0,
           boundary_weight=5.0, tol_uv=1e-3, tol_p=1e-2, max_iterations=50000, check_every=100, history=50,
           adam_steps=3000, adam_lr=1e-3, grid=201, device=None, log=None, time_limit=None, optimizer="device",
-          sampling="uniform", initial=None, return_parameters=False):
+          sampling="uniform", initial=None, return_parameters=False, head="psi", make_evaluator=None):
+    """Solve to acceptance; returns the result dict (and the final parameters).
+
+    ``head`` "psi": the stream-function net (psi, p), first-order boundary rows with (u, v, p)
+    targets (the benchmark configuration); "uvp": the reference's (u, v, p) net with the
+    gradient-enhanced residual (gradient weight 0.2) and (u, v, p) targets on value rows.
+    ``make_evaluator(points, widths, head, boundary_order, loss, device)`` replaces the
+    evaluation: an object with ``parameters`` (P) whose ``__call__(flat, out)`` writes
+    ``[grad(P), loss]`` into ``out`` on the current stream, capturable in a CUDA graph."""
     start = time.perf_counter()
     world = dist.get_world_size() if dist.is_initialized() else 1
     rank = dist.get_rank() if dist.is_initialized() else 0
     device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-    widths = list(widths)
+    if head not in ("psi", "uvp"):
+        raise ValueError("head must be 'psi' or 'uvp'")
+    widths = list(widths) if widths is not None else [2, 64, 64, 64, 64, 2 if head == "psi" else 3]
+    order = 1 if head == "psi" else 0
+    # the first-order-row point set carries (u, v, p) targets and weights per boundary point,
+    # which the (u, v, p) head's value rows use as they are
     pts = kovasznay(interior, boundary, re=re, seed=seed, boundary_order=1, sampling=sampling, device=device)
     loss = NSLoss(viscosity=1.0 / re, boundary_weight=boundary_weight)
-    if world > 1:
+    if make_evaluator is not None:
+        ev = make_evaluator(pts, widths, head, order, loss, device)
+    elif world > 1:
         from flashns_b200.distributed import DistributedEvaluator
-        ev = DistributedEvaluator(pts, widths, head="psi", boundary_order=1, loss=loss, device=device)
+        ev = DistributedEvaluator(pts, widths, head=head, boundary_order=order, loss=loss, device=device)
     else:
         ev = PackedEvaluator(pts.x, pts.interior_count, pts.pde_weights, pts.boundary_weights, pts.target, widths,
-                             head="psi", boundary_order=1, loss=loss, device=device)
-    accept = Acceptance(widths, re, device, grid)
+                             head=head, boundary_order=order, loss=loss, device=device)
+    accept = Acceptance(widths, re, device, grid, head)
     ws, bs = xavier_normal(widths, init_seed)
     start_params = flat_parameters(ws, bs) if initial is None else initial.detach().to(torch.float64).reshape(-1)
     flat = torch.nn.Parameter(start_params.to(device).contiguous())
@@ -169,7 +187,7 @@ def solve(*, interior=16384, boundary=4096, widths=(2, 64, 64, 64, 64, 2), re=20
               "iterations": iterations,
               "evaluations": evaluations[0], "rel_l2_u": metrics[0], "rel_l2_v": metrics[1], "rel_l2_p": metrics[2],
               "final_loss": float(loss_view), "n_gpus": world, "interior": interior, "boundary": boundary,
-              "widths": widths, "re": re, "seed": seed, "init_seed": init_seed, "sampling": sampling}
+              "widths": widths, "head": head, "re": re, "seed": seed, "init_seed": init_seed, "sampling": sampling}
     return (result, flat.detach().cpu()) if return_parameters else result
 
 
@@ -187,6 +205,8 @@ def main():
     ap.add_argument("--sampling", choices=list(SAMPLINGS), default="uniform",
                     help="uniform: torch CPU generator; sobol / philox: drawn on the device")
     ap.add_argument("--initial", type=Path, default=None, help="start from a checkpoint's flat parameters")
+    ap.add_argument("--head", choices=["psi", "uvp"], default="psi",
+                    help="psi: stream-function net (the benchmark); uvp: the reference's (u, v, p) net")
     ap.add_argument("--output", type=Path, default=None,
                     help="write OUTPUT.pt (final parameters + run description) and OUTPUT.json (result)")
     ap.add_argument("--quiet", action="store_true")
@@ -201,7 +221,7 @@ def main():
     result, final = solve(seed=args.seed, init_seed=args.init_seed, max_iterations=args.max_iterations,
                           check_every=args.check_every, boundary_weight=args.boundary_weight,
                           adam_steps=args.adam_steps, history=args.history, time_limit=args.time_limit,
-                          optimizer=args.optimizer, sampling=args.sampling, initial=initial,
+                          optimizer=args.optimizer, sampling=args.sampling, initial=initial, head=args.head,
                           log=None if args.quiet else lambda s: print(s, flush=True), return_parameters=True)
     if world > 1:
         dist.barrier()
@@ -210,7 +230,7 @@ def main():
         if args.output is not None:
             meta = {"problem": {"name": "kovasznay", "re": result["re"], "interior": result["interior"],
                                 "boundary": result["boundary"], "widths": result["widths"],
-                                "sampling": args.sampling},
+                                "head": args.head, "sampling": args.sampling},
                     "protocol": {k: getattr(args, k) for k in ("adam_steps", "history", "check_every",
                                                                "boundary_weight", "max_iterations")},
                     "seed": args.seed, "init_seed": args.init_seed, "backend": "flashns_b200"}

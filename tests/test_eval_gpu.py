@@ -169,6 +169,18 @@ def test_solver_runs_and_reduces_loss(cuda):
     assert r["final_loss"] < first
 
 
+def test_solver_uvp_head_runs_and_reduces_loss(cuda):
+    """The (u, v, p) head of the solver (the reference's objective, value boundary rows):
+    the captured closure, L-BFGS and the acceptance fields run and the loss decreases."""
+    from flashns_b200.solver import solve
+    log = []
+    r = solve(interior=512, boundary=128, widths=(2, 32, 32, 3), max_iterations=40, check_every=20, grid=21,
+              adam_steps=50, device=cuda, log=log.append, head="uvp")
+    assert r["head"] == "uvp" and r["iterations"] >= 20
+    first = __import__("json").loads(log[0])["loss"]
+    assert r["final_loss"] < first
+
+
 @pytest.mark.gpu
 def test_bounded_wait_reports_instead_of_hanging(cuda):
     """An mbarrier that nothing arrives at: the kernel's bounded wait gives up, raises the

@@ -52,3 +52,25 @@ def test_reference_route_follows_new_inputs(cuda):
     loss, grads = captured.replay()
     got = torch.cat([g.reshape(-1) for g in grads] + [loss.reshape(1)]).cpu()
     assert close_ratio(got.numpy(), ours2.numpy()) <= 1
+
+
+def test_reference_route_evaluator_for_the_solve(cuda):
+    """The closure of the same-machine reference solve (baseline/reference_solve.py): the
+    v8+ route with parameters as views of one flat vector writes the same [grad, loss] as
+    this library's (u, v, p) evaluation of the Kovasznay point set."""
+    from baseline.reference_solve import ReferenceRouteEvaluator
+    from flashns_b200.evaluator import PackedEvaluator, flat_parameters, xavier_normal
+    from flashns_b200.ns_seed import NSLoss
+    from flashns_b200.problems import kovasznay
+    pts = kovasznay(301, 77, seed=4, boundary_order=1)
+    widths = [2, 64, 64, 3]
+    loss = NSLoss(viscosity=pts.viscosity, gradient_weight=0.2, boundary_weight=5.0)
+    ref = ReferenceRouteEvaluator(pts, widths, "uvp", 0, loss, cuda)
+    ours = PackedEvaluator(pts.x, pts.interior_count, pts.pde_weights, pts.boundary_weights, pts.target, widths,
+                           head="uvp", boundary_order=0, loss=loss, device=cuda)
+    flat = flat_parameters(*xavier_normal(widths, 0)).to(cuda)
+    out = torch.empty(ref.parameters + 1, dtype=torch.float64, device=cuda)
+    ref(flat, out)
+    expected = ours(flat)
+    torch.cuda.synchronize()
+    assert close_ratio(out.cpu().numpy(), expected.cpu().numpy()) <= 1
