@@ -39,10 +39,10 @@ constexpr int LDC = KC + 4;  // padded chunk row: conflict-free FP64 fragment lo
 constexpr int kMaxAffine = 16;
 // set by a kernel whose bounded wait on a bulk copy gave up (read by flashns_b200_device_fault)
 __device__ int g_device_fault = 0;
-// the dense dgrad (+ VJP) of a 2-D 64 -> 64 layer on the two-group backward kernel (defined
+// the dense dgrad (+ VJP) of a 64 -> 64 layer on the evaluation's backward kernels (defined
 // with the host launchers below; called by the reference-ABI hook in hooks.cu)
-cudaError_t dense_dgrad_64(bool fused, const double* d, const double* w, const double* h, const double* aux,
-                           double* out, int batch, cudaStream_t stream);
+cudaError_t dense_dgrad_64(int dim, bool fused, const double* d, const double* w, const double* h,
+                           const double* aux, double* out, int batch, cudaStream_t stream);
 
 // Self-test of the bounded wait: an mbarrier that nothing arrives at.  The wait gives up
 // after `spins` polls, raises the fault word and the kernel returns normally.
@@ -620,7 +620,12 @@ constexpr size_t fused_smem_bytes() {
   return a > red ? a : red;
 }
 
-template <int DIM, int BO, bool FIRST>
+// MODE kEvalBackward: the evaluation's layer backward (dgrad, wgrad, VJP, bias and
+// coordinate partials).  kHookDgradVjp / kHookDgrad: the dense dgrad (+ jet VJP) of the
+// reference-ABI hook (flashns_stable_dgrad_vjp on a 64 -> 64 layer: bwd_pingpong in 2-D, bwd_fused in 3-D): no weight gradient and
+// no partials; kHookDgrad also skips H and writes dH itself.
+enum { kEvalBackward = 0, kHookDgradVjp = 1, kHookDgrad = 2 };
+template <int DIM, int BO, bool FIRST, int MODE = kEvalBackward>
 __global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
     bwd_fused(const __grid_constant__ CUtensorMap tm_seed_i, const __grid_constant__ CUtensorMap tm_seed_b,
               const __grid_constant__ CUtensorMap tm_h_i, const __grid_constant__ CUtensorMap tm_h_b,
@@ -641,6 +646,8 @@ __global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
   constexpr int RS = T::NWARPS / 8, RROWS = TR / RS;
   static_assert(CP / 8 == 8 && T::NWARPS % 8 == 0 && RROWS % 16 == 0, "wgrad warp split");
   static_assert(NK == 2 && KC == 32 && TR <= 256, "TMA boxes: 36 columns, at most 256 rows");
+  constexpr bool EVAL = MODE == kEvalBackward, WITH_H = MODE != kHookDgrad;
+  static_assert(EVAL || (!FIRST && BO == 0), "the hook modes cover dense (all full-jet) rows");
   static_assert((size_t(TR) * LDC * sizeof(double)) % 128 == 0, "every TMA destination on a 128-byte boundary");
   extern __shared__ __align__(128) double smem[];
   double* sB = smem;                // seed planes [NK][TR][LDC]
@@ -732,7 +739,7 @@ __global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
   pdl_trigger();
   if (int64_t(blockIdx.x) < ntiles) {
     load_tile(blockIdx.x, sB, &tm_seed_i, &tm_seed_b, &bars[0], dnext);
-    load_tile(blockIdx.x, sH, &tm_h_i, &tm_h_b, &bars[1], hcur);
+    if (WITH_H) load_tile(blockIdx.x, sH, &tm_h_i, &tm_h_b, &bars[1], hcur);
   }
   unsigned ph_seed = 0, ph_h = 0;
   // B fragments of the dgrad: column g of an n8 tile is slot 2j + (g & 1) of thread
@@ -742,7 +749,7 @@ __global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
   const double* hcol = sH + (wn >> 2) * TR * LDC + ((8 * wn) & (KC - 1)) + g;
   for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     const bool has_next = tile + gridDim.x < ntiles;
-    if (tid == 0) {  // the epilogue reads this tile's a1 rows (a contiguous range): bring them into L2
+    if (WITH_H && tid == 0) {  // the epilogue reads this tile's a1 rows (a contiguous range): bring them into L2
       int64_t pt0, pts;
       TL::points(geo, nint, tile, pt0, pts);
       prefetch_l2(a1cur + pt0 * CP, uint32_t(pts * CP * sizeof(double)));
@@ -782,13 +789,13 @@ __global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
         }
       }
     }
-    if (__syncthreads_or(!wait_tile(tile, &bars[1], ph_h, true))) {  // H_l tile landed
+    if (WITH_H && __syncthreads_or(!wait_tile(tile, &bars[1], ph_h, true))) {  // H_l tile landed
       if (tid == 0) atomicExch(&g_device_fault, 1);
       return;
     }
     // wgrad: dW[cout][8*wn..+8] += D^T[cout][rows] H[rows][cin], rows of share wrs
 #pragma unroll
-    for (int kc = 0; kc < NK; ++kc) {
+    for (int kc = 0; kc < (EVAL ? NK : 0); ++kc) {
       const double* cD = sB + kc * TR * LDC;
 #pragma unroll 4
       for (int r = wrs * RROWS; r < (wrs + 1) * RROWS; r += 8) {
@@ -813,8 +820,34 @@ __global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
     const double* hrow = sH + (tc * S) * LDC;
     auto hslot = [&](int s, int ch) { return hrow[(ch >> 5) * TR * LDC + s * LDC + (ch & (KC - 1))]; };
     const bool interior = tile < nint;
+    if constexpr (!EVAL) {  // the hook: dense rows, dH (+ VJP) straight to the output
+      const int64_t p = tile * T::TC + tc;
+      if (p < geo.ni) {
 #pragma unroll
-    for (int i = 0; i < T::MT; ++i) {
+        for (int i = 0; i < T::MT; ++i)
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const int ch = wc * T::WCH + 16 * i + 8 * hh + g;
+            double dh[S], zb[Q];
+#pragma unroll
+            for (int s = 0; s < S; ++s) dh[s] = acc[i][s >> 1][2 * hh + (s & 1)];
+            if constexpr (MODE == kHookDgradVjp) {
+              double hv[Q];
+#pragma unroll
+              for (int s = 0; s < Q; ++s) hv[s] = hslot(s, ch);
+              Jet<DIM, 3>::vjp(hv, a1cur[p * CP + ch], dh, zb);
+            } else {
+#pragma unroll
+              for (int s = 0; s < Q; ++s) zb[s] = dh[s];
+            }
+            double* dst = dcur + p * Q * CP + ch;
+#pragma unroll
+            for (int s = 0; s < Q; ++s) dst[int64_t(s) * CP] = zb[s];
+          }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < (EVAL ? T::MT : 0); ++i) {
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const int ch = wc * T::WCH + 16 * i + 8 * hh + g;
@@ -868,7 +901,14 @@ __global__ void __launch_bounds__(FusedTile<DIM>::THREADS, 1)
       }
     }
     __syncthreads();  // H_l planes free
-    if (has_next) load_tile(tile + gridDim.x, sH, &tm_h_i, &tm_h_b, &bars[1], hcur);
+    if (WITH_H && has_next) load_tile(tile + gridDim.x, sH, &tm_h_i, &tm_h_b, &bars[1], hcur);
+  }
+  if constexpr (!EVAL) {  // the hook writes no partials
+    if (tid == 0) {  // every phase completed before the last barrier
+      mbar_inval(&bars[0]);
+      mbar_inval(&bars[1]);
+    }
+    return;
   }
   // weight-gradient partial of this CTA: row shares combined in fixed order through smem
   __syncthreads();
@@ -962,11 +1002,6 @@ constexpr size_t pp_smem_bytes() {
   return a > red ? a : red;
 }
 
-// MODE kEvalBackward: the evaluation's layer backward (dgrad, wgrad, VJP, bias and
-// coordinate partials).  kHookDgradVjp / kHookDgrad: the dense dgrad (+ jet VJP) of the
-// reference-ABI hook (flashns_stable_dgrad_vjp on a 64 -> 64 layer): no weight gradient and
-// no partials; kHookDgrad also skips H and writes dH itself.
-enum { kEvalBackward = 0, kHookDgradVjp = 1, kHookDgrad = 2 };
 template <int BO, bool FIRST, int MODE = kEvalBackward>
 __global__ void __launch_bounds__(kPPThreads, 1)
     bwd_pingpong(const __grid_constant__ CUtensorMap tm_seed_i, const __grid_constant__ CUtensorMap tm_seed_b,
@@ -3511,9 +3546,42 @@ int first_launch(int dim, int bo, int grid, cudaStream_t st, const double* x, co
 
 }  // namespace
 
-// The dense 64 -> 64 dgrad (+ VJP) for the reference-ABI hook in hooks.cu
-cudaError_t flashns_b200::dense_dgrad_64(bool fused, const double* d, const double* w, const double* h,
+// The dense 64 -> 64 dgrad (+ VJP) for the reference-ABI hook in hooks.cu: the two-group
+// backward kernel in 2-D, the one-group fused backward kernel (160-row tiles) in 3-D
+template <int MODE>
+cudaError_t launch_dense_dgrad_fused3(const double* d, const double* w, const double* h, const double* aux,
+                                      double* out, int batch, cudaStream_t stream) {
+  using T = FusedTile<3>;
+  using TL = Tiles<3, 0, T::TC>;
+  const int64_t rows = int64_t(batch) * TL::Q;
+  if (rows > INT32_MAX - T::TR) return cudaErrorInvalidValue;
+  const Geometry g{batch, 0, rows};
+  cudaError_t e = allow_smem(bwd_fused<3, 0, false, MODE>, fused_smem_bytes<3>());
+  if (e != cudaSuccess) return e;
+  int device = 0, sms = 0;
+  if ((e = cudaGetDevice(&device)) != cudaSuccess ||
+      (e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess)
+    return e;
+  const int64_t tiles = TL::interior(batch);
+  const int grid = int(tiles < sms ? tiles : sms);
+  CUtensorMap m[4];
+  const double* hm = MODE == kHookDgradVjp ? h : d;  // dgrad only: H is never read
+  if ((e = row_tensor_map(&m[0], d, rows, kFusedWidth, LDC, T::TR)) != cudaSuccess ||
+      (e = row_tensor_map(&m[1], d, 0, kFusedWidth, LDC, T::TR)) != cudaSuccess ||
+      (e = row_tensor_map(&m[2], hm, rows, kFusedWidth, LDC, T::TR)) != cudaSuccess ||
+      (e = row_tensor_map(&m[3], hm, 0, kFusedWidth, LDC, T::TR)) != cudaSuccess)
+    return e;
+  t_programmatic = false;
+  return launch_kernel(bwd_fused<3, 0, false, MODE>, grid, T::THREADS, fused_smem_bytes<3>(), stream, m[0], m[1],
+                       m[2], m[3], d, hm, w, aux, out, static_cast<const double*>(nullptr),
+                       static_cast<double*>(nullptr), static_cast<double*>(nullptr), g);
+}
+
+cudaError_t flashns_b200::dense_dgrad_64(int dim, bool fused, const double* d, const double* w, const double* h,
                                          const double* aux, double* out, int batch, cudaStream_t stream) {
+  if (dim == 3)
+    return fused ? launch_dense_dgrad_fused3<kHookDgradVjp>(d, w, h, aux, out, batch, stream)
+                 : launch_dense_dgrad_fused3<kHookDgrad>(d, w, h, aux, out, batch, stream);
   return fused ? launch_dense_dgrad_pingpong<kHookDgradVjp>(d, w, h, aux, out, batch, stream)
                : launch_dense_dgrad_pingpong<kHookDgrad>(d, w, h, aux, out, batch, stream);
 }

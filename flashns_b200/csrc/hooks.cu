@@ -25,10 +25,10 @@
 #include "residual_generated.cuh"
 
 namespace flashns_b200 {
-// eval.cu: the dense dgrad (+ VJP) of a 2-D 64 -> 64 layer on the evaluation's two-group
-// backward kernel without its weight gradient
-cudaError_t dense_dgrad_64(bool fused, const double* d, const double* w, const double* h, const double* aux,
-                           double* out, int batch, cudaStream_t stream);
+// eval.cu: the dense dgrad (+ VJP) of a 64 -> 64 layer on the evaluation's backward kernels
+// (two-group in 2-D, one-group 160-row tiles in 3-D) without their weight gradient
+cudaError_t dense_dgrad_64(int dim, bool fused, const double* d, const double* w, const double* h,
+                           const double* aux, double* out, int batch, cudaStream_t stream);
 namespace {
 
 constexpr int kHookThreads = 128;
@@ -773,12 +773,12 @@ int flashns_stable_dgrad_vjp(int dim, bool fused, const double* d, const double*
   if (overlaps(out, no * 8, d, size_t(batch) * q * cout * 8) || overlaps(out, no * 8, w, size_t(cout) * cin * 8) ||
       (fused && (overlaps(out, no * 8, h, no * 8) || overlaps(out, no * 8, aux, size_t(batch) * cin * 8))))
     return int(cudaErrorInvalidValue);
-  // 2-D 64 -> 64 (the reference's nets): the two-group backward kernel of the evaluation,
-  // TMA-fed, without its weight gradient; other shapes: the general kernel above
+  // 64 -> 64 (the reference's nets): the evaluation's TMA-fed backward kernels without
+  // their weight gradient; other shapes: the general kernel above
   const auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-  if (dim == 2 && cout == 64 && cin == 64 && aligned(d) && aligned(w) && (!fused || aligned(h)) &&
-      int64_t(batch) * 10 <= INT32_MAX / 2)
-    return int(flashns_b200::dense_dgrad_64(fused, d, w, h, aux, out, batch, stream));
+  if (cout == 64 && cin == 64 && aligned(d) && aligned(w) && (!fused || aligned(h)) &&
+      int64_t(batch) * (dim == 2 ? 10 : 20) <= INT32_MAX / 2)
+    return int(flashns_b200::dense_dgrad_64(dim, fused, d, w, h, aux, out, batch, stream));
   if (dim == 2 && fused) return int(launch_dense_dgrad<2, true>(d, w, h, aux, out, batch, cout, cin, stream));
   if (dim == 2) return int(launch_dense_dgrad<2, false>(d, w, h, aux, out, batch, cout, cin, stream));
   if (fused) return int(launch_dense_dgrad<3, true>(d, w, h, aux, out, batch, cout, cin, stream));
