@@ -12,7 +12,8 @@ driver reports under load.
   SMs x {1, 2, 4} CTAs of {128, 256, 512} threads (m16n8k8 runs at 256 threads, the
   in-run probe's shape);
 * ``smem``: m16n8k8 fed from shared memory in the kernels' tile shape at 16 warps per SM
-  (one 512-thread CTA, or two 256-thread CTAs) and at 8 warps per SM (one 256-thread CTA).
+  (one 512-thread CTA, or two 256-thread CTAs), at 8 warps per SM (one 256-thread CTA) and
+  at 4 warps per SM (one 128-thread CTA).
 """
 
 import argparse
@@ -32,7 +33,7 @@ KINDS = {"m16n8k8": 0, "m8n8k4": 1, "m16n8k4": 2, "m16n8k16": 3, "dfma": 4, "sme
 def launch_shapes(kind, sms):
     if kind == "smem":
         return [(sms, 512, "16 warps/SM, one 512-thread CTA"), (2 * sms, 256, "16 warps/SM, two 256-thread CTAs"),
-                (sms, 256, "8 warps/SM, one 256-thread CTA")]
+                (sms, 256, "8 warps/SM, one 256-thread CTA"), (sms, 128, "4 warps/SM, one 128-thread CTA")]
     threads = (256,) if kind == "m16n8k8" else (128, 256, 512)
     return [(m * sms, t, f"{m} x {t}-thread CTAs per SM") for m in (1, 2, 4) for t in threads]
 
