@@ -993,6 +993,38 @@ constexpr int pp_boundary_box_rows() {
   return TL::PS * TL::QB == PPTile::S ? PPTile::TR : TL::PS * TL::QB;
 }
 
+// The turn ring of NG groups of 16 / NG warps (the CTA's 512 threads).  Group g holds the
+// tensor pipe after group g - 1 (group 0 after group NG - 1, which opens the ring with one
+// arrival); turn barrier g counts group g's threads syncing and group g - 1's arriving.
+// A CTA's tiles are blockIdx.x + k * gridDim.x; group g takes k = g, g + NG, ..., so the
+// groups' counts differ by at most one, and a group whose predecessor arrived once more
+// than it synced closes with one more sync.
+template <int NG>
+struct Ring {
+  using T = MmaTile<2, kFusedWidth, 16 / NG>;
+  static constexpr int GT = T::THREADS;
+  static_assert(NG * GT == kPPThreads && 2 * NG + 1 <= 16, "512 threads; named barriers 1..2NG");
+  __device__ static int group_bar(int g) { return 1 + g; }      // the group's own threads
+  __device__ static int turn_bar(int g) { return 1 + NG + g; }  // group g syncs, g - 1 arrives
+  __device__ static int64_t count(int64_t mine, int g) { return mine > g ? (mine - 1 - g) / NG + 1 : 0; }
+  __device__ static void open(int gp) {
+    if (gp == NG - 1) named_arrive(turn_bar(0), 2 * GT);
+  }
+  __device__ static void take(int gp) { named_sync(turn_bar(gp), 2 * GT); }
+  __device__ static void pass(int gp) { named_arrive(turn_bar((gp + 1) % NG), 2 * GT); }
+  __device__ static void close(int gp, int64_t mine) {
+    const int64_t in = gp == 0 ? count(mine, NG - 1) + 1 : count(mine, gp - 1);
+    if (in > count(mine, gp)) named_sync(turn_bar(gp), 2 * GT);
+  }
+};
+
+template <int BO, int NG>
+constexpr int ring_boundary_box_rows() {
+  using T = typename Ring<NG>::T;
+  using TL = Tiles<2, BO, T::TC>;
+  return TL::PS * TL::QB == T::S ? T::TR : TL::PS * TL::QB;
+}
+
 constexpr size_t pp_smem_bytes() {
   using T = PPTile;
   constexpr size_t planes = size_t(kFusedWidth / KC) * size_t(T::TR) * LDC;  // one tensor's half tile
@@ -2192,18 +2224,18 @@ __global__ void __launch_bounds__(HeadTile<DIM>::THREADS, HeadTile<DIM>::MINB)
 // (u, v, p) head, whose seed reads 25 outputs (one thread per point forms it from the
 // staged outputs), and value boundary rows, where a thread column holds ten points; the
 // stream-function head with first-order rows runs head_pingpong below.
-template <int NF>
+template <int NF, int NG>
 constexpr size_t hpp_staged_group_doubles() {
-  return size_t(kFusedWidth / KC) * PPTile::TR * LDC + size_t(PPTile::TR) * (kFusedWidth + 4) +
-         2 * size_t(PPTile::TR) * NF;
+  using T = typename Ring<NG>::T;
+  return size_t(kFusedWidth / KC) * T::TR * LDC + size_t(T::TR) * (kFusedWidth + 4) + 2 * size_t(T::TR) * NF;
 }
-template <int NF>
+template <int NF, int NG>
 constexpr size_t hpp_staged_smem_bytes() {
-  return sizeof(double) * (kPPGroups * hpp_staged_group_doubles<NF>() + size_t(kFusedWidth) * (kFusedWidth + 4) +
-                           size_t(NF) * kFusedWidth + kPPGroups);
+  return sizeof(double) * (NG * hpp_staged_group_doubles<NF, NG>() + size_t(kFusedWidth) * (kFusedWidth + 4) +
+                           size_t(NF) * kFusedWidth + NG);
 }
 
-template <int BO, int HEAD>
+template <int BO, int HEAD, int NG>
 __global__ void __launch_bounds__(kPPThreads, 1)
     head_pingpong_staged(const __grid_constant__ CUtensorMap tm_in_i, const __grid_constant__ CUtensorMap tm_in_b,
                   const double* __restrict__ hin, const double* __restrict__ w, const double* __restrict__ bias,
@@ -2211,7 +2243,8 @@ __global__ void __launch_bounds__(kPPThreads, 1)
                   const double* __restrict__ bnd_w, const double* __restrict__ target, double nu, double gamma,
                   double bc, double* __restrict__ dL, double* __restrict__ head_partial, Geometry geo) {
   constexpr int DIM = 2, CP = kFusedWidth;
-  using T = PPTile;
+  using R = Ring<NG>;
+  using T = typename R::T;
   using TL = Tiles<DIM, BO, T::TC>;
   constexpr int S = T::S, TR = T::TR, Q = TL::Q, QB = TL::QB, PS = TL::PS;
   constexpr int NF = HeadTraits<HEAD>::NF;
@@ -2219,13 +2252,14 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   constexpr int LDA = CP + 4, LDH = CP + 4;
   constexpr int PARTIAL = NF * CP + NF + 1 + CP;  // dW_L | db_L | loss | db_{L-1}
   constexpr int NK = CP / KC;
-  constexpr int BB = pp_boundary_box_rows<BO>();
+  constexpr int BB = ring_boundary_box_rows<BO, NG>();
   constexpr bool SPLIT = BB != TR;
   constexpr int GT = T::THREADS;
   constexpr int PLANES = NK * TR * LDC;
-  static_assert(T::NWARPS == CP / 8 && NF <= 8, "warp w of a group owns output-gradient columns 8w..8w+7");
+  constexpr int CB = CP / 8 / T::NWARPS;  // output-gradient column blocks of 8 per warp
+  static_assert(CB * T::NWARPS * 8 == CP && NF <= 8, "warp w of a group owns output-gradient columns 8 CB w..");
   static_assert(NK == 2 && KC == 32 && TR <= 256, "TMA boxes: 36 columns, at most 256 rows");
-  static_assert((hpp_staged_group_doubles<NF>() * sizeof(double)) % 128 == 0, "group buffers on 128-byte boundaries");
+  static_assert((hpp_staged_group_doubles<NF, NG>() * sizeof(double)) % 128 == 0, "group buffers on 128-byte boundaries");
   extern __shared__ __align__(128) double smem[];
   if (smem_u32(smem) & 127) {  // TMA destinations need 128-byte alignment: refuse, never fault
     if (threadIdx.x == 0) atomicExch(&g_device_fault, 2);
@@ -2234,21 +2268,20 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int gp = warp / T::NWARPS, lw = warp % T::NWARPS, gtid = tid % GT;
   const int wc = lw % T::WC, wr = lw / T::WC;
-  double* sB = smem + gp * hpp_staged_group_doubles<NF>();  // this group's input planes [NK][TR][LDC]
+  double* sB = smem + gp * hpp_staged_group_doubles<NF, NG>();  // this group's input planes [NK][TR][LDC]
   double* sH = sB + PLANES;                          // H_L tile [TR][CP+4], rows in tile order
   double* sY = sH + TR * LDH;                        // Y  [TR][NF]
   double* sD = sY + TR * NF;                         // dY [TR][NF]
-  double* sA = smem + kPPGroups * hpp_staged_group_doubles<NF>();  // W_{L-1} [CP][CP+4], shared
+  double* sA = smem + NG * hpp_staged_group_doubles<NF, NG>();  // W_{L-1} [CP][CP+4], shared
   double* sW = sA + CP * LDA;                                // W_L [NF][CP], shared
   uint64_t* bars = reinterpret_cast<uint64_t*>(sW + NF * CP);
   uint64_t* bar_in = bars + gp;
-  const int bar_group = kPPBarGroup + gp;
+  const int bar_group = R::group_bar(gp);
   const int64_t nint = TL::interior(geo.ni);
   const int64_t nht = nint + TL::boundary(geo.nb);
   const int64_t mine = int64_t(blockIdx.x) < nht ? (nht - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-  const int64_t n0 = (mine + 1) / 2, n1 = mine / 2;
-  const int64_t nmy = gp == 0 ? n0 : n1;
-  auto tile_of = [&](int64_t k) { return int64_t(blockIdx.x) + (2 * k + gp) * int64_t(gridDim.x); };
+  const int64_t nmy = R::count(mine, gp);
+  auto tile_of = [&](int64_t k) { return int64_t(blockIdx.x) + (NG * k + gp) * int64_t(gridDim.x); };
   auto load_tile = [&](int64_t tile) {
     const bool interior = tile < nint;
     if (SPLIT && !interior) {
@@ -2292,18 +2325,20 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   cp_async_commit();
   for (int i = tid; i < NF * CP; i += kPPThreads) sW[i] = wL[i];
   if (tid == 0)
-    for (int b = 0; b < kPPGroups; ++b) mbar_init(&bars[b], 1);
+    for (int b = 0; b < NG; ++b) mbar_init(&bars[b], 1);
   cp_async_wait<0>();
   __syncthreads();  // W_{L-1}, W_L and the barriers visible
   pdl_wait();  // H_{L-1} is the predecessor's output
   pdl_trigger();
   if (nmy > 0) load_tile(tile_of(0));
-  double wacc[4] = {0.0, 0.0, 0.0, 0.0};  // dW_L[g][8 lw + 2t (+1)] (rows g < NF)
+  double wacc[CB][4];  // dW_L[g][8 (CB lw + cb) + 2t (+1)] (rows g < NF)
+#pragma unroll
+  for (int cb = 0; cb < CB; ++cb) wacc[cb][0] = wacc[cb][1] = wacc[cb][2] = wacc[cb][3] = 0.0;
   double bacc = 0.0, lacc = 0.0, cacc[2] = {0.0, 0.0};
   bool dead = false;
   // B fragments: column g of an n8 tile is slot 2j + (g & 1) of thread column wr*4 + (g >> 1)
   const int brow = (wr * 4 + (g >> 1)) * S + (g & 1);
-  if (gp == 1) named_arrive(kPPBarTurn + 0, kPPThreads);  // group 0 takes the first turn
+  R::open(gp);  // group 0 takes the first turn
   for (int64_t k = 0; k < nmy; ++k) {
     const int64_t tile = tile_of(k);
     double acc[T::NT][4];
@@ -2312,7 +2347,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[j][e] = 0.0;
     if (!dead) dead = named_sync_or(bar_group, GT, !wait_tile(tile));
-    named_sync(kPPBarTurn + gp, kPPThreads);  // this group's turn on the tensor pipe
+    R::take(gp);  // this group's turn on the tensor pipe
     if (!dead) {
       // Z^T[ch][rows] = W_{L-1}[ch][cin] H_{L-1}^T[cin][rows]
 #pragma unroll
@@ -2331,7 +2366,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         }
       }
     }
-    named_arrive(kPPBarTurn + (1 - gp), kPPThreads);  // the other group's turn
+    R::pass(gp);                // the next group's turn
     named_sync(bar_group, GT);                         // this group's input planes free
     if (k + 1 < nmy && !dead) load_tile(tile_of(k + 1));
     if (!dead) {
@@ -2445,10 +2480,14 @@ __global__ void __launch_bounds__(kPPThreads, 1)
       }
       named_sync(bar_group, GT);
       // 4. output-layer gradients dW_L[o][c] += sum_r dY[r][o] H[r][c] as DMMA tiles (M =
-      //    outputs, N = channels 8 lw.., K = tile rows); db_L over order-0 rows
+      //    outputs, N = channels 8 (CB lw + cb).., K = tile rows); db_L over order-0 rows
       for (int k0 = 0; k0 < kend; k0 += 8) {
         const double a[4] = {g < NF ? sD[(k0 + t) * NF + g] : 0.0, 0.0, g < NF ? sD[(k0 + t + 4) * NF + g] : 0.0, 0.0};
-        mma_m16n8k8(wacc, a, sH[(k0 + t) * LDH + 8 * lw + g], sH[(k0 + t + 4) * LDH + 8 * lw + g]);
+#pragma unroll
+        for (int cb = 0; cb < CB; ++cb) {
+          const int c8 = 8 * (CB * lw + cb) + g;
+          mma_m16n8k8(wacc[cb], a, sH[(k0 + t) * LDH + c8], sH[(k0 + t + 4) * LDH + c8]);
+        }
       }
       if (gtid < NF)
         for (int r = 0; r < nrows; r += step) bacc += sD[r * NF + gtid];
@@ -2500,24 +2539,23 @@ __global__ void __launch_bounds__(kPPThreads, 1)
       }
     }
   }
-  // turn counts balanced as in bwd_pingpong
-  if (gp == 0 && n0 == n1) named_sync(kPPBarTurn + 0, kPPThreads);
-  if (gp == 1 && n0 == n1 + 1) named_sync(kPPBarTurn + 1, kPPThreads);
+  R::close(gp, mine);  // turn counts balanced
   if (__syncthreads_or(dead)) {
     if (tid == 0) atomicExch(&g_device_fault, 1);
     return;
   }
-  // per-CTA partials, fixed-order reductions over the two groups
+  // per-CTA partials, fixed-order reductions over the groups
   double* out = head_partial + int64_t(blockIdx.x) * PARTIAL;
-  double* red = smem;                          // [512] loss partials
-  double* cred = red + kPPThreads;             // [groups * WR][CP] bias partials of layer L-1
-  double* wsh = cred + kPPGroups * T::WR * CP;  // [8 warps][32 lanes][2] group 1's dW_L
-  double* bsh = wsh + T::NWARPS * 32 * 2;       // [NF] group 1's db_L
-  if (gp == 1) {
-    wsh[(lw * 32 + lane) * 2] = wacc[0];
-    wsh[(lw * 32 + lane) * 2 + 1] = wacc[1];
-    if (gtid < NF) bsh[gtid] = bacc;
+  double* red = smem;                      // [512] loss partials
+  double* cred = red + kPPThreads;         // [groups * WR][CP] bias partials of layer L-1
+  double* wsh = cred + NG * T::WR * CP;    // [groups][warps][CB][32 lanes][2] dW_L
+  double* bsh = wsh + NG * T::NWARPS * CB * 32 * 2;  // [groups][NF] db_L
+#pragma unroll
+  for (int cb = 0; cb < CB; ++cb) {
+    wsh[(((gp * T::NWARPS + lw) * CB + cb) * 32 + lane) * 2] = wacc[cb][0];
+    wsh[(((gp * T::NWARPS + lw) * CB + cb) * 32 + lane) * 2 + 1] = wacc[cb][1];
   }
+  if (gtid < NF) bsh[gp * NF + gtid] = bacc;
   red[tid] = lacc;
 #pragma unroll
   for (int hh = 0; hh < 2; ++hh) {
@@ -2529,10 +2567,22 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   __syncthreads();
   if (gp == 0) {
     if (g < NF) {
-      out[g * CP + 8 * lw + 2 * t] = wacc[0] + wsh[(lw * 32 + lane) * 2];
-      out[g * CP + 8 * lw + 2 * t + 1] = wacc[1] + wsh[(lw * 32 + lane) * 2 + 1];
+#pragma unroll
+      for (int cb = 0; cb < CB; ++cb) {
+        double v0 = 0.0, v1 = 0.0;
+        for (int q = 0; q < NG; ++q) {
+          v0 += wsh[(((q * T::NWARPS + lw) * CB + cb) * 32 + lane) * 2];
+          v1 += wsh[(((q * T::NWARPS + lw) * CB + cb) * 32 + lane) * 2 + 1];
+        }
+        out[g * CP + 8 * (CB * lw + cb) + 2 * t] = v0;
+        out[g * CP + 8 * (CB * lw + cb) + 2 * t + 1] = v1;
+      }
     }
-    if (gtid < NF) out[NF * CP + gtid] = bacc + bsh[gtid];
+    if (gtid < NF) {
+      double v = 0.0;
+      for (int q = 0; q < NG; ++q) v += bsh[q * NF + gtid];
+      out[NF * CP + gtid] = v;
+    }
   }
   if (tid == 0) {
     double sum = 0.0;
@@ -2541,21 +2591,24 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   }
   for (int c = tid; c < CP; c += kPPThreads) {
     double sum = 0.0;
-    for (int r = 0; r < kPPGroups * T::WR; ++r) sum += cred[r * CP + c];
+    for (int r = 0; r < NG * T::WR; ++r) sum += cred[r * CP + c];
     out[NF * CP + NF + 1 + c] = sum;
   }
   if (tid == 0)
-    for (int b = 0; b < kPPGroups; ++b) mbar_inval(&bars[b]);
+    for (int b = 0; b < NG; ++b) mbar_inval(&bars[b]);
 }
 
-// Two-group ("ping-pong") form of fwd_head for 2-D: the last hidden layer, the output
-// layer, the residual seeds, the output-layer gradients and the VJP into layer L, with the
-// CTA's 16 warps in two 8-warp groups that take turns on the tensor pipe as in
-// bwd_pingpong.  Each group has its own input planes (TMA, rows in global order); W_{L-1}
-// and W_L are shared.  A group's mainloop runs while it holds the turn; its whole epilogue
-// overlaps the other group's mainloop.
+// Turn-taking form of fwd_head for 2-D: the last hidden layer, the output layer, the
+// residual seeds, the output-layer gradients and the VJP into layer L, with the CTA's 16
+// warps in NG groups (Ring<NG>; kHeadGroups = 4 groups of 4 warps, 40-row tiles) that take
+// turns on the tensor pipe.  Each group has its own input planes (TMA, rows in global
+// order); W_{L-1} and W_L are shared.  A group's mainloop runs while it holds the turn; its
+// epilogue overlaps the other groups' mainloops.  DMMA issue has priority over the
+// epilogue's FP64 instructions, so an epilogue advances mostly between other groups'
+// turns: with four groups it has three turns to finish in, which outweighs the lower DMMA
+// rate of a 4-warp turn (81 % of the 8-warp rate).
 //
-// The epilogue keeps everything of a half tile in registers.  A thread owns one thread
+// The epilogue keeps everything of a tile in registers.  A thread owns one thread
 // column (one interior point, or PS boundary points) and two channels, so after the jet it
 // holds H_L of its channels at every slot of its points.  The outputs Y = H_L W_L^T + b_L
 // are sums over the 64 channels: each thread forms the partial over its two channels for
@@ -2565,7 +2618,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
 // their eighths through shared memory in fixed order, after one 128-thread barrier.
 // Every thread of a point then has its outputs, forms the seed itself (the seed formulas
 // are a few dozen flops), accumulates dW_L = dY^T H_L for its channels, contracts
-// dH_L = dY W_L and runs the jet VJP.  Per half tile that is one sub-group barrier and
+// dH_L = dY W_L and runs the jet VJP.  Per tile that is one row-group barrier and
 // about 70 FP64 operations per thread beyond the jet and its VJP, instead of staging
 // H_L, Y and dY in shared memory around output-layer MMAs of which 14 of 16 rows are zero.
 //
@@ -2588,16 +2641,20 @@ struct HeadOutputs {
   }
 };
 
+constexpr int kHeadGroups = 4;  // groups of the register head's turn ring
+
+template <int NG>
 constexpr size_t hpp_smem_bytes() {
   using HO = HeadOutputs;
-  constexpr size_t planes = size_t(kFusedWidth / KC) * PPTile::TR * LDC;  // one group's input half tile
-  constexpr size_t parts = size_t(kPPGroups) * PPTile::WR * 4 * PPTile::WC * HO::LDP;
-  constexpr size_t lead = size_t(kPPGroups) * PPTile::WR * 4 * (HO::NF + 1);
-  return sizeof(double) * (kPPGroups * planes + size_t(kFusedWidth) * (kFusedWidth + 4) +
-                           size_t(HO::NF) * (kFusedWidth + 1) + parts + lead + kPPGroups);
+  using T = typename Ring<NG>::T;
+  constexpr size_t planes = size_t(kFusedWidth / KC) * T::TR * LDC;  // one group's input tile
+  constexpr size_t parts = size_t(NG) * T::WR * 4 * T::WC * HO::LDP;
+  constexpr size_t lead = size_t(NG) * T::WR * 4 * (HO::NF + 1);
+  return sizeof(double) * (NG * planes + size_t(kFusedWidth) * (kFusedWidth + 4) +
+                           size_t(HO::NF) * (kFusedWidth + 1) + parts + lead + NG);
 }
-enum { kPPBarRows = 5 };  // named barriers 5 + group * 2 + row group: the 4 channel warps (128 threads)
 
+template <int NG>
 __global__ void __launch_bounds__(kPPThreads, 1)
     head_pingpong(const __grid_constant__ CUtensorMap tm_in_i, const __grid_constant__ CUtensorMap tm_in_b,
                   const double* __restrict__ hin, const double* __restrict__ w, const double* __restrict__ bias,
@@ -2605,7 +2662,8 @@ __global__ void __launch_bounds__(kPPThreads, 1)
                   const double* __restrict__ bnd_w, const double* __restrict__ target, double nu, double gamma,
                   double bc, double* __restrict__ dL, double* __restrict__ head_partial, Geometry geo) {
   constexpr int DIM = 2, CP = kFusedWidth;
-  using T = PPTile;
+  using R = Ring<NG>;
+  using T = typename R::T;
   constexpr int BO = 1, HEAD = FLASHNS_B200_HEAD_PSI;
   using TL = Tiles<DIM, BO, T::TC>;
   using HO = HeadOutputs;
@@ -2615,11 +2673,11 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   constexpr int LDA = CP + 4, LDP = HO::LDP;
   constexpr int PARTIAL = NF * CP + NF + 1 + CP;  // dW_L | db_L | loss | db_{L-1}
   constexpr int NK = CP / KC;
-  constexpr int BB = pp_boundary_box_rows<BO>();
+  constexpr int BB = ring_boundary_box_rows<BO, NG>();
   constexpr bool SPLIT = BB != TR;
   constexpr int GT = T::THREADS;
   constexpr int PLANES = NK * TR * LDC;
-  static_assert(T::WC == 4 && T::WR == 2 && T::TC == 8, "4 channel warps x 2 row groups of 4 thread columns");
+  static_assert(T::WC == 4 && T::TC == 4 * T::WR, "4 channel warps x row groups of 4 thread columns");
   static_assert(NK == 2 && KC == 32 && TR <= 256, "TMA boxes: 36 columns, at most 256 rows");
   static_assert((size_t(PLANES) * sizeof(double)) % 128 == 0, "group planes on 128-byte boundaries");
   static_assert(PS * QB <= S && HO::NI <= Q * NF, "slots of a thread column");
@@ -2632,21 +2690,21 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   const int gp = warp / T::NWARPS, lw = warp % T::NWARPS, gtid = tid % GT;
   const int wc = lw % T::WC, wr = lw / T::WC;
   double* sB = smem + gp * PLANES;            // this group's input planes [NK][TR][LDC]
-  double* sA = smem + kPPGroups * PLANES;     // W_{L-1} [CP][CP+4], shared
+  double* sA = smem + NG * PLANES;            // W_{L-1} [CP][CP+4], shared
   double* sW = sA + CP * LDA;                 // W_L [NF][CP], then b_L [NF]
   double* sP = sW + NF * CP + NF;             // output partials [group][row group][thread column][wc][LDP]
-  double* sL = sP + kPPGroups * T::WR * 4 * T::WC * LDP;  // per lead thread: loss, db_L [NF]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sL + kPPGroups * T::WR * 4 * (NF + 1));
+  double* sL = sP + NG * T::WR * 4 * T::WC * LDP;  // per lead thread: loss, db_L [NF]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sL + NG * T::WR * 4 * (NF + 1));
   uint64_t* bar_in = bars + gp;
-  const int bar_group = kPPBarGroup + gp;
-  const int bar_rows = kPPBarRows + gp * T::WR + wr;
+  const int bar_group = R::group_bar(gp);
+  // the 4 channel warps of a row group: the group itself, or barriers 2NG + 1 + ...
+  const int bar_rows = T::WR == 1 ? bar_group : 2 * NG + 1 + gp * T::WR + wr;
   double* part = sP + ((gp * T::WR + wr) * 4 + t) * T::WC * LDP;  // this thread column's partials
   const int64_t nint = TL::interior(geo.ni);
   const int64_t nht = nint + TL::boundary(geo.nb);
   const int64_t mine = int64_t(blockIdx.x) < nht ? (nht - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-  const int64_t n0 = (mine + 1) / 2, n1 = mine / 2;
-  const int64_t nmy = gp == 0 ? n0 : n1;
-  auto tile_of = [&](int64_t k) { return int64_t(blockIdx.x) + (2 * k + gp) * int64_t(gridDim.x); };
+  const int64_t nmy = R::count(mine, gp);
+  auto tile_of = [&](int64_t k) { return int64_t(blockIdx.x) + (NG * k + gp) * int64_t(gridDim.x); };
   auto load_tile = [&](int64_t tile) {
     const bool interior = tile < nint;
     if (SPLIT && !interior) {
@@ -2693,9 +2751,9 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   cp_async_commit();
   for (int i = tid; i < NF * CP; i += kPPThreads) sW[i] = wL[i];
   if (tid < NF) sW[NF * CP + tid] = bL[tid];
-  if (tid < kPPGroups * T::WR * 4 * (NF + 1)) sL[tid] = 0.0;
+  if (tid < NG * T::WR * 4 * (NF + 1)) sL[tid] = 0.0;
   if (tid == 0)
-    for (int b = 0; b < kPPGroups; ++b) mbar_init(&bars[b], 1);
+    for (int b = 0; b < NG; ++b) mbar_init(&bars[b], 1);
   cp_async_wait<0>();
   __syncthreads();  // W_{L-1}, W_L, b_L, the loss slots and the barriers visible
   pdl_wait();  // H_{L-1} is the predecessor's output
@@ -2711,7 +2769,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   bool dead = false;
   // B fragments: column g of an n8 tile is slot 2j + (g & 1) of thread column wr*4 + (g >> 1)
   const int brow = (wr * 4 + (g >> 1)) * S + (g & 1);
-  if (gp == 1) named_arrive(kPPBarTurn + 0, kPPThreads);  // group 0 takes the first turn
+  R::open(gp);  // group 0 takes the first turn
   for (int64_t k = 0; k < nmy; ++k) {
     const int64_t tile = tile_of(k);
     double acc[T::NT][4];
@@ -2720,7 +2778,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[j][e] = 0.0;
     if (!dead) dead = named_sync_or(bar_group, GT, !wait_tile(tile));
-    named_sync(kPPBarTurn + gp, kPPThreads);  // this group's turn on the tensor pipe
+    R::take(gp);  // this group's turn on the tensor pipe
     if (!dead) {
       // Z^T[ch][rows] = W_{L-1}[ch][cin] H_{L-1}^T[cin][rows]
 #pragma unroll
@@ -2739,7 +2797,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         }
       }
     }
-    named_arrive(kPPBarTurn + (1 - gp), kPPThreads);  // the other group's turn
+    R::pass(gp);                // the next group's turn
     named_sync(bar_group, GT);                         // this group's input planes free
     if (k + 1 < nmy && !dead) load_tile(tile_of(k + 1));
     if (dead) continue;
@@ -2904,16 +2962,14 @@ __global__ void __launch_bounds__(kPPThreads, 1)
     if (interior) finish(std::true_type{});
     else finish(std::false_type{});
   }
-  // turn counts balanced as in bwd_pingpong
-  if (gp == 0 && n0 == n1) named_sync(kPPBarTurn + 0, kPPThreads);
-  if (gp == 1 && n0 == n1 + 1) named_sync(kPPBarTurn + 1, kPPThreads);
+  R::close(gp, mine);  // turn counts balanced
   if (__syncthreads_or(dead)) {
     if (tid == 0) atomicExch(&g_device_fault, 1);
     return;
   }
   // per-CTA partials, fixed-order reductions: the 4 thread columns of a warp by shuffles,
-  // then the row groups of both groups in order
-  constexpr int RG = kPPGroups * T::WR;
+  // then the row groups of all groups in order
+  constexpr int RG = NG * T::WR;
   double* out = head_partial + int64_t(blockIdx.x) * PARTIAL;
   double* cred = smem;                  // [RG][CP] bias partials of layer L-1
   double* wred = cred + RG * CP;        // [RG][NF][CP] dW_L
@@ -2951,7 +3007,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
     out[NF * CP + NF + 1 + c] = sum;
   }
   if (tid == 0)
-    for (int b = 0; b < kPPGroups; ++b) mbar_inval(&bars[b]);
+    for (int b = 0; b < NG; ++b) mbar_inval(&bars[b]);
 }
 
 
@@ -3412,18 +3468,19 @@ struct FwdHeadOps {
   static constexpr bool kPingPong = DIM == 2;  // 2-D: the two-group kernel over 80-row half tiles
   // the stream-function head with first-order boundary rows keeps its epilogue in registers
   static constexpr bool kRegisters = BO == 1 && HEAD == FLASHNS_B200_HEAD_PSI;
+  static constexpr int kGroups = kHeadGroups;  // turn-taking groups of the 2-D kernels
   static cudaError_t setup(int& occ) {
     if constexpr (kPingPong && kRegisters) {
-      constexpr size_t smem = hpp_smem_bytes();
-      static_assert(smem <= kMaxSmem, "two-group head tile exceeds shared memory");
-      cudaError_t e = allow_smem(head_pingpong, smem);
-      occ = occupancy(head_pingpong, smem, kPPThreads);
+      constexpr size_t smem = hpp_smem_bytes<kHeadGroups>();
+      static_assert(smem <= kMaxSmem, "turn-taking head tiles exceed shared memory");
+      cudaError_t e = allow_smem(head_pingpong<kHeadGroups>, smem);
+      occ = occupancy(head_pingpong<kHeadGroups>, smem, kPPThreads);
       return e;
     } else if constexpr (kPingPong) {
-      constexpr size_t smem = hpp_staged_smem_bytes<NF>();
-      static_assert(smem <= kMaxSmem, "two-group head tile exceeds shared memory");
-      cudaError_t e = allow_smem(head_pingpong_staged<BO, HEAD>, smem);
-      occ = occupancy(head_pingpong_staged<BO, HEAD>, smem, kPPThreads);
+      constexpr size_t smem = hpp_staged_smem_bytes<NF, kHeadGroups>();
+      static_assert(smem <= kMaxSmem, "turn-taking head tiles exceed shared memory");
+      cudaError_t e = allow_smem(head_pingpong_staged<BO, HEAD, kHeadGroups>, smem);
+      occ = occupancy(head_pingpong_staged<BO, HEAD, kHeadGroups>, smem, kPPThreads);
       return e;
     } else {
       constexpr size_t smem = fwd_head_smem_bytes<DIM, NF>();
@@ -3435,8 +3492,8 @@ struct FwdHeadOps {
   }
   static int64_t tiles(const Geometry& g) {
     if constexpr (kPingPong) {
-      using TL = Tiles<2, BO, PPTile::TC>;
-      return (TL::interior(g.ni) + TL::boundary(g.nb) + 1) / 2;
+      using TL = Tiles<2, BO, Ring<kGroups>::T::TC>;
+      return (TL::interior(g.ni) + TL::boundary(g.nb) + kGroups - 1) / kGroups;
     } else {
       using TL = Tiles<DIM, BO, HeadTile<DIM>::TC>;
       return TL::interior(g.ni) + TL::boundary(g.nb);
@@ -3446,8 +3503,9 @@ struct FwdHeadOps {
                             const double* wl, const double* bl, const double* pw, const double* bw, const double* tg,
                             double nu, double gm, double bc, double* dl, double* hpart, Geometry g) {
     if constexpr (kPingPong) {
-      using TL = Tiles<2, BO, PPTile::TC>;
-      constexpr int TR = PPTile::TR, BB = pp_boundary_box_rows<BO>();
+      using TT = typename Ring<kGroups>::T;
+      using TL = Tiles<2, BO, TT::TC>;
+      constexpr int TR = TT::TR, BB = ring_boundary_box_rows<BO, kGroups>();
       const int64_t ri = g.ni * TL::Q, rb = g.nb * TL::QB;  // interior / boundary segment rows
       if (ri > INT32_MAX - TR || rb > INT32_MAX - TR) return cudaErrorInvalidValue;  // TMA rows are int32
       CUtensorMap m[2];
@@ -3456,11 +3514,12 @@ struct FwdHeadOps {
           (e = row_tensor_map(&m[1], hin + ri * kFusedWidth, rb, kFusedWidth, LDC, BB)) != cudaSuccess)
         return e;
       if constexpr (kRegisters)
-        return launch_kernel(head_pingpong, grid, kPPThreads, hpp_smem_bytes(), st, m[0], m[1], hin, w, b, wl, bl, pw,
-                             bw, tg, nu, gm, bc, dl, hpart, g);
-      else
-        return launch_kernel(head_pingpong_staged<BO, HEAD>, grid, kPPThreads, hpp_staged_smem_bytes<NF>(), st, m[0],
+        return launch_kernel(head_pingpong<kHeadGroups>, grid, kPPThreads, hpp_smem_bytes<kHeadGroups>(), st, m[0],
                              m[1], hin, w, b, wl, bl, pw, bw, tg, nu, gm, bc, dl, hpart, g);
+      else
+        return launch_kernel(head_pingpong_staged<BO, HEAD, kHeadGroups>, grid, kPPThreads,
+                             hpp_staged_smem_bytes<NF, kHeadGroups>(), st, m[0], m[1], hin, w, b, wl, bl, pw, bw, tg,
+                             nu, gm, bc, dl, hpart, g);
     } else {
       return launch_kernel(fwd_head<DIM, BO, HEAD>, grid, HeadTile<DIM>::THREADS, fwd_head_smem_bytes<DIM, NF>(), st,
                            hin, w, b, wl, bl, pw, bw, tg, nu, gm, bc, dl, hpart, g);

@@ -1,42 +1,50 @@
-"""CPU: the turn protocol of the two-group kernels (bwd_pingpong, fwd_pingpong,
-head_pingpong in flashns_b200/csrc/eval.cu) never deadlocks and leaves no barrier with
-pending arrivals, for every number of half tiles a CTA can own.
+"""CPU: the turn protocol of the turn-taking kernels in flashns_b200/csrc/eval.cu never
+deadlocks and leaves no barrier with pending arrivals, for every number of tiles a CTA can
+own.  Two groups with a hand-written closing: bwd_pingpong, fwd_pingpong; the ring
+`Ring<NG>` of head_pingpong and head_pingpong_staged: four groups (kHeadGroups).
 
-The kernels' barrier sequence, per group (group 0 takes the CTA's even half tiles, group
-1 the odd ones, n0 = ceil(m / 2) and n1 = floor(m / 2)):
+The barrier sequence, per group g of NG (group g takes the CTA's tiles k = g, g + NG, ...,
+so it owns n_g = ceil((m - g) / NG) of m):
 
-    group 1 first arrives on "turn 0";
-    for each of its half tiles: sync on its own turn barrier, MMAs, arrive on the other's;
-    closing: group 0 syncs "turn 0" once more when n0 == n1,
-             group 1 syncs "turn 1" once more when n0 == n1 + 1.
+    group NG - 1 first arrives on "turn 0";
+    for each of its tiles: sync on "turn g", MMAs, arrive on "turn (g + 1) % NG";
+    closing: one more sync on "turn g" when its predecessor arrived there more often
+             than it synced (n_{NG-1} + 1 arrivals for group 0, n_{g-1} for the others).
 
-A barrier generation completes when both groups have arrived (one syncing, one arriving
+For two groups this is the kernels' hand-written form: group 0 syncs "turn 0" once more
+when n0 == n1, group 1 syncs "turn 1" once more when n0 == n1 + 1.
+
+A barrier generation completes when two groups have arrived (one syncing, one arriving
 or syncing).  The model also rejects a group arriving twice in one generation, which on
 the hardware would complete the barrier without the other group.
 """
 
+import itertools
+
 import pytest
 
 
-def program(group, n0, n1):
-    ops = [("arrive", "turn0")] if group == 1 else []
-    own, other = ("turn0", "turn1") if group == 0 else ("turn1", "turn0")
-    for _ in range(n0 if group == 0 else n1):
-        ops += [("sync", own), ("arrive", other)]
-    if group == 0 and n0 == n1:
-        ops.append(("sync", "turn0"))
-    if group == 1 and n0 == n1 + 1:
-        ops.append(("sync", "turn1"))
+def count(m, g, ng):
+    return (m - 1 - g) // ng + 1 if m > g else 0
+
+
+def program(g, m, ng):
+    ops = [("arrive", 0)] if g == ng - 1 else []
+    for _ in range(count(m, g, ng)):
+        ops += [("sync", g), ("arrive", (g + 1) % ng)]
+    arrivals = count(m, ng - 1, ng) + 1 if g == 0 else count(m, g - 1, ng)
+    if arrivals > count(m, g, ng):
+        ops.append(("sync", g))
     return ops
 
 
-def run(m, prefer):
-    """Execute both programs, always advancing group `prefer` while it can."""
-    n0, n1 = (m + 1) // 2, m // 2
-    progs = [program(0, n0, n1), program(1, n0, n1)]
-    pc, waiting = [0, 0], [None, None]
-    pending = {"turn0": set(), "turn1": set()}
-    generation = {"turn0": 0, "turn1": 0}
+def run(m, order, ng, make=None):
+    """Execute every group's program, always advancing the first group of `order` that can."""
+    make = make or program
+    progs = [make(g, m, ng) for g in range(ng)]
+    pc, waiting = [0] * ng, [None] * ng
+    pending = {b: set() for b in range(ng)}
+    generation = dict.fromkeys(range(ng), 0)
 
     def step(u):
         if waiting[u] is not None:
@@ -49,7 +57,7 @@ def run(m, prefer):
         if pc[u] >= len(progs[u]):
             return False
         op, bar = progs[u][pc[u]]
-        assert u not in pending[bar], f"m={m}: group {u} arrives twice in one generation of {bar}"
+        assert u not in pending[bar], f"m={m}: group {u} arrives twice in one generation of turn {bar}"
         pending[bar].add(u)
         gen = generation[bar]
         if len(pending[bar]) == 2:
@@ -61,31 +69,41 @@ def run(m, prefer):
             waiting[u] = (bar, gen)
         return True
 
-    order = (prefer, 1 - prefer)
-    while step(order[0]) or step(order[1]):
+    while any(step(u) for u in order):
         pass
-    assert pc == [len(progs[0]), len(progs[1])], f"m={m}: deadlock at {pc}"
-    assert not pending["turn0"] and not pending["turn1"], f"m={m}: pending arrivals {pending}"
+    assert pc == [len(p) for p in progs], f"m={m}: deadlock at {pc}"
+    assert not any(pending.values()), f"m={m}: pending arrivals {pending}"
 
 
-@pytest.mark.parametrize("prefer", [0, 1])
-def test_turn_barriers_balance_for_every_tile_count(prefer):
+@pytest.mark.parametrize("ng", [2, 4])
+def test_turn_barriers_balance_for_every_tile_count(ng):
+    for order in itertools.permutations(range(ng)):
+        for m in range(0, 65):
+            run(m, order, ng)
+
+
+@pytest.mark.parametrize("ng", [2, 4])
+def test_groups_take_every_tile_once(ng):
     for m in range(0, 65):
-        run(m, prefer)
+        assert sum(count(m, g, ng) for g in range(ng)) == m
 
 
-def test_model_catches_an_unbalanced_closing():
-    """The closing sync is what balances "turn 0" when the groups own as many tiles."""
-    global program
-    original = program
+def test_two_group_ring_is_the_hand_written_closing():
+    """For NG = 2 the ring's closing syncs are the two-group kernels' explicit conditions."""
+    for m in range(0, 65):
+        n0, n1 = (m + 1) // 2, m // 2
+        assert (program(0, m, 2)[-1:] == [("sync", 0)] and len(program(0, m, 2)) % 2 == 1) == (n0 == n1)
+        assert (len(program(1, m, 2)) % 2 == 0) == (n0 == n1 + 1)
 
-    def without_closing(group, n0, n1):
-        ops = original(group, n0, n1)
-        return ops[:-1] if group == 0 and n0 == n1 else ops
 
-    program = without_closing
-    try:
-        with pytest.raises(AssertionError):
-            run(4, 0)
-    finally:
-        program = original
+@pytest.mark.parametrize("ng", [2, 4])
+def test_model_catches_an_unbalanced_closing(ng):
+    """The closing sync is what balances a turn whose predecessor owns one tile more."""
+
+    def without_closing(g, m, n):
+        ops = program(g, m, n)
+        return ops[:-1] if len(ops) % 2 == (0 if g == n - 1 else 1) else ops
+
+    with pytest.raises(AssertionError):
+        for m in range(0, 2 * ng + 1):
+            run(m, tuple(range(ng)), ng, without_closing)
