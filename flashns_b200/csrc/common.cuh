@@ -88,6 +88,21 @@ __device__ __forceinline__ bool named_sync_or(int id, int count, bool v) {
 // async-proxy (TMA) ones
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
 
+// 2-D tiled TMA store (no multicast) of the box at `smem` (laid out as the tensor map's
+// swizzle mode says) to coordinates (x = column, y = row); rows and columns past the map's
+// extent are not written.  x * 8 bytes is a multiple of 16 and x, y >= 0.  Tracked by the
+// issuing thread's bulk group (bulk_commit, bulk_wait_read, bulk_wait).
+__device__ __forceinline__ void tma_store_2d(const void* tensor_map, int x, int y, const void* smem) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];\n" ::"l"(tensor_map),
+               "r"(x), "r"(y), "r"(smem_u32(smem))
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
+// every bulk store this thread issued has finished reading its shared-memory source
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory"); }
+// every bulk store this thread issued has completed its writes
+__device__ __forceinline__ void bulk_wait() { asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory"); }
+
 // 2-D tiled TMA load (no multicast): box at coordinates (x = column, y = row) of the tensor
 // map into shared memory, completing its bytes on `bar`.  x * 8 bytes is a multiple of 16.
 __device__ __forceinline__ void tma_load_2d(void* smem, const void* tensor_map, int x, int y, uint64_t* bar) {

@@ -1372,16 +1372,21 @@ __global__ void __launch_bounds__(kPPThreads, 1)
 // stores of H_{l+1} and a1) overlaps the other group's mainloop.  A group's half tile (80
 // rows, 8 thread columns) arrives by 2-D TMA boxes in global row order (split boundary
 // tiles by cp.async), the permutation folded into the fragment addresses.
+// A warp's store box of an interior half tile: H_{l+1} of its 4 points x Q rows and 16
+// channels, 128-byte rows in the TMA 128-byte swizzle (16-byte chunk c of row r at chunk
+// c ^ (r & 7)), on a 1024-byte boundary.
+constexpr int kFppBox = 4 * 10 * 16;
 constexpr size_t fpp_smem_bytes() {
   constexpr size_t planes = size_t(kFusedWidth / KC) * size_t(PPTile::TR) * LDC;  // one half tile
+  constexpr size_t boxes = size_t(kPPThreads / 32) * kFppBox + 128;              // + 1024-byte alignment slack
   constexpr size_t wres = size_t(kFusedWidth) * (kFusedWidth + 4);
-  return sizeof(double) * (kPPGroups * planes + wres + kPPGroups);  // + one mbarrier per group
+  return sizeof(double) * (kPPGroups * planes + boxes + wres + kPPGroups);  // + one mbarrier per group
 }
 
 template <int BO>
 __global__ void __launch_bounds__(kPPThreads, 1)
     fwd_pingpong(const __grid_constant__ CUtensorMap tm_in_i, const __grid_constant__ CUtensorMap tm_in_b,
-                 const double* __restrict__ hin, const double* __restrict__ w, const double* __restrict__ bias,
+                 const __grid_constant__ CUtensorMap tm_out, const double* __restrict__ hin, const double* __restrict__ w, const double* __restrict__ bias,
                  double* __restrict__ hout, double* __restrict__ a1out, Geometry geo) {
   constexpr int DIM = 2, CP = kFusedWidth;
   using T = PPTile;
@@ -1403,7 +1408,11 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   const int gp = warp / T::NWARPS, lw = warp % T::NWARPS, gtid = tid % GT;
   const int wc = lw % T::WC, wr = lw / T::WC;
   double* sB = smem + gp * PLANES;                               // this group's input planes
-  double* sW = smem + kPPGroups * PLANES;                        // W_l [CP][LDW] (row = output channel)
+  // this warp's store box (1024-byte aligned inside the slack), then W_l [CP][LDW]
+  double* boxes = smem + kPPGroups * PLANES;
+  boxes += ((1024u - (smem_u32(boxes) & 1023u)) & 1023u) / sizeof(double);
+  double* box = boxes + warp * kFppBox;
+  double* sW = smem + kPPGroups * PLANES + kPPThreads / 32 * kFppBox + 128;  // row = output channel
   uint64_t* bars = reinterpret_cast<uint64_t*>(sW + CP * LDW);  // one per group
   uint64_t* bar_in = bars + gp;
   const int bar_group = kPPBarGroup + gp;
@@ -1496,9 +1505,16 @@ __global__ void __launch_bounds__(kPPThreads, 1)
     named_sync(bar_group, GT);                         // this group's input planes free
     if (k + 1 < nmy && !dead) load_tile(tile_of(k + 1));
     if (!dead) {
-      // epilogue: bias on the order-0 coefficient, stable tanh jet, store H_{l+1} and a1
+      // epilogue: bias on the order-0 coefficient, stable tanh jet, store H_{l+1} and a1.
+      // Interior H_{l+1} goes out through this warp's swizzled box as one TMA store (rows of
+      // points past the segment lie beyond the tensor map and are not written): bulk stores
+      // take far less from the other group's DMMAs than the same bytes as global stores.
       const int tc = wr * 4 + t;
       const bool interior = tile < nint;
+      if (interior) {
+        if (lane == 0) bulk_wait_read();  // the box's previous store has read it
+        __syncwarp();
+      }
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const int ch = wc * T::WCH + 8 * hh + g;
@@ -1511,9 +1527,11 @@ __global__ void __launch_bounds__(kPPThreads, 1)
             double hv[Q], a1;
             z[0] += bias_r[hh];
             Jet<DIM, 3>::fwd(z, hv, a1);
-            double* dst = hout + p * Q * CP + ch;
 #pragma unroll
-            for (int s = 0; s < Q; ++s) dst[int64_t(s) * CP] = hv[s];
+            for (int s = 0; s < Q; ++s) {
+              const int r = t * Q + s, c = 8 * hh + g;  // box row, column
+              box[r * 16 + ((((c >> 1) ^ r) & 7) << 1) + (c & 1)] = hv[s];
+            }
             a1out[p * CP + ch] = a1;
           }
         } else {
@@ -1534,8 +1552,17 @@ __global__ void __launch_bounds__(kPPThreads, 1)
           }
         }
       }
+      if (interior) {
+        fence_proxy_async();  // this thread's box writes before the TMA engine reads them
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tm_out, wc * T::WCH, int(tile * T::TC * Q + wr * 4 * Q), box);
+          bulk_commit();
+        }
+      }
     }
   }
+  if (lane == 0) bulk_wait();  // this warp's stores complete before the kernel ends
   // turn counts balanced as in bwd_pingpong
   if (gp == 0 && n0 == n1) named_sync(kPPBarTurn + 0, kPPThreads);
   if (gp == 1 && n0 == n1 + 1) named_sync(kPPBarTurn + 1, kPPThreads);
@@ -3235,7 +3262,8 @@ EncodeTiled tensor_map_encoder() {
 
 // [rows][cols] row-major FP64 segment read in boxes of box_rows x box_cols; boxes reaching
 // past the segment (rows or columns) read zeros
-cudaError_t row_tensor_map(CUtensorMap* m, const double* base, int64_t rows, int cols, int box_cols, int box_rows) {
+cudaError_t row_tensor_map(CUtensorMap* m, const double* base, int64_t rows, int cols, int box_cols, int box_rows,
+                           CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE) {
   const EncodeTiled enc = tensor_map_encoder();
   if (!enc) return cudaErrorNotSupported;
   if ((reinterpret_cast<uintptr_t>(base) & 15) || (cols * sizeof(double)) % 16 || (box_cols * sizeof(double)) % 16)
@@ -3245,7 +3273,7 @@ cudaError_t row_tensor_map(CUtensorMap* m, const double* base, int64_t rows, int
   const cuuint32_t box[2] = {cuuint32_t(box_cols), cuuint32_t(box_rows)};
   const cuuint32_t elem[2] = {1, 1};
   const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT64, 2, const_cast<double*>(base), dims, strides, box, elem,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
@@ -3301,13 +3329,14 @@ struct FwdOps {
         constexpr int TR = PPTile::TR, BB = pp_boundary_box_rows<BO>();
         const int64_t ri = g.ni * TL::Q, rb = g.nb * TL::QB;  // interior / boundary segment rows
         if (ri > INT32_MAX - TR || rb > INT32_MAX - TR) return cudaErrorInvalidValue;  // TMA rows are int32
-        CUtensorMap m[2];
+        CUtensorMap m[3];
         cudaError_t e;
         if ((e = row_tensor_map(&m[0], hin, ri, kFusedWidth, LDC, TR)) != cudaSuccess ||
-            (e = row_tensor_map(&m[1], hin + ri * kFusedWidth, rb, kFusedWidth, LDC, BB)) != cudaSuccess)
+            (e = row_tensor_map(&m[1], hin + ri * kFusedWidth, rb, kFusedWidth, LDC, BB)) != cudaSuccess ||
+            (e = row_tensor_map(&m[2], hout, ri, kFusedWidth, 16, 4 * TL::Q, CU_TENSOR_MAP_SWIZZLE_128B)) != cudaSuccess)
           return e;
-        return launch_kernel(fwd_pingpong<BO>, grid, kPPThreads, fpp_smem_bytes(), st, m[0], m[1], hin, w, b, hout,
-                             a1, g);
+        return launch_kernel(fwd_pingpong<BO>, grid, kPPThreads, fpp_smem_bytes(), st, m[0], m[1], m[2], hin, w, b,
+                             hout, a1, g);
       }
     }
     return launch_kernel(fwd_layer<DIM, CP, BO>, grid, T::THREADS, fwd_smem_bytes<DIM, CP>(kin), st, hin, kin, w, b,
