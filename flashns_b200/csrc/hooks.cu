@@ -776,7 +776,9 @@ int flashns_stable_dgrad_vjp(int dim, bool fused, const double* d, const double*
   // 64 -> 64 (the reference's nets): the evaluation's TMA-fed backward kernels without
   // their weight gradient; other shapes: the general kernel above
   const auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-  if (cout == 64 && cin == 64 && aligned(d) && aligned(w) && (!fused || aligned(h)) &&
+  // (TMA reads d, cp.async w; the fused kernels prefetch rows of h and aux into L2 in bulk,
+  // which wants 16-byte aligned addresses)
+  if (cout == 64 && cin == 64 && aligned(d) && aligned(w) && (!fused || (aligned(h) && aligned(aux))) &&
       int64_t(batch) * (dim == 2 ? 10 : 20) <= INT32_MAX / 2)
     return int(flashns_b200::dense_dgrad_64(dim, fused, d, w, h, aux, out, batch, stream));
   if (dim == 2 && fused) return int(launch_dense_dgrad<2, true>(d, w, h, aux, out, batch, cout, cin, stream));

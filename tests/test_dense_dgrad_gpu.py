@@ -92,3 +92,35 @@ def test_dense_dgrad_rejects_bad_arguments(cuda):
     assert lib.flashns_stable_dgrad_vjp(2, True, p, p, None, None, _ptr(x[32:]), 1, 1, 1, None) == 1
     assert lib.flashns_stable_dgrad_vjp(2, False, p, p, None, None, None, 0, 1, 1, None) == 0  # empty
     assert lib.flashns_stable_dgrad_shared_bytes() > 0
+
+
+@pytest.mark.parametrize("dim", [2, 3])
+def test_dense_dgrad_with_h_and_a1_views_off_a_16_byte_boundary(cuda, dim):
+    """64 -> 64 with H and a1 passed as views one double into larger buffers (8-byte but not
+    16-byte aligned): the hook takes the general kernel instead of the fused kernels, whose
+    bulk L2 prefetches want 16-byte aligned rows, and the values still match the oracle."""
+    from flashns_b200 import _lib
+    from oracle import jets as J
+    lib = _lib.library()
+    rng = np.random.default_rng(4242 + dim)
+    q, batch = J.q(dim), 129
+    z = rng.normal(size=(batch, q, 64)) * 0.5
+    h, a1 = J.tanh_jet(z, dim)
+    d = rng.normal(size=(batch, q, 64))
+    w = rng.normal(size=(64, 64)) / 8.0
+    T = lambda a: torch.tensor(np.ascontiguousarray(a), dtype=torch.float64, device=cuda)
+    hbuf = torch.zeros(h.size + 1, dtype=torch.float64, device=cuda)
+    abuf = torch.zeros(a1.size + 1, dtype=torch.float64, device=cuda)
+    hbuf[1:] = T(h).reshape(-1)
+    abuf[1:] = T(a1).reshape(-1)
+    hv, av = hbuf[1:], abuf[1:]
+    assert hv.data_ptr() % 16 == 8 and av.data_ptr() % 16 == 8
+    dg, wg = T(d), T(w)
+    out = torch.full((batch * q * 64,), float("nan"), dtype=torch.float64, device=cuda)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)
+    assert lib.flashns_stable_dgrad_vjp(dim, True, _ptr(dg), _ptr(wg), _ptr(hv), _ptr(av), _ptr(out), batch, 64, 64,
+                                        stream) == 0
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().reshape(batch, q, 64)
+    assert np.isfinite(got).all()
+    assert close_ratio(got, J.tanh_vjp(h, a1, d @ w, dim)) <= 1.0
