@@ -250,6 +250,9 @@ CONFIGS = {
     "cfg3": dict(kind="taylor_green", interior=262144, boundary=65536, widths=[3] + [128] * 5 + [2]),
     "ref16k": dict(kind="reference_case", interior=16384, boundary=0, widths=[2, 64, 64, 3], head="uvp",
                    boundary_order=0, gamma=0.2, init="reference"),
+    # not a benchmark configuration: a space-time net 64 wide, the one shape that runs the
+    # 3-D 64-wide kernels (fwd_head, bwd_fused); for their profiles
+    "tgv64": dict(kind="taylor_green", interior=16384, boundary=4096, widths=[3, 64, 64, 64, 64, 2]),
 }
 
 
