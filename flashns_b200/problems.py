@@ -253,6 +253,9 @@ CONFIGS = {
     # not a benchmark configuration: a space-time net 64 wide, the one shape that runs the
     # 3-D 64-wide kernels (fwd_head, bwd_fused); for their profiles
     "tgv64": dict(kind="taylor_green", interior=16384, boundary=4096, widths=[3, 64, 64, 64, 64, 2]),
+    # not a benchmark configuration: cfg1's net on 64 times its points (1,048,576 interior,
+    # 262,144 boundary), the top of the 16K-1M range the throughput target names
+    "cfg1x64": dict(kind="kovasznay", interior=1048576, boundary=262144, widths=[2, 64, 64, 64, 64, 2]),
 }
 
 
