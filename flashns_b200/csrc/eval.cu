@@ -2241,13 +2241,13 @@ __global__ void __launch_bounds__(HeadTile<DIM>::THREADS, HeadTile<DIM>::MINB)
   }
 }
 
-// Two-group ("ping-pong") form of fwd_head for 2-D, staged through shared memory: the last
-// hidden layer, the output layer, the residual seeds, the output-layer gradients and the
-// VJP into layer L, with the CTA's 16 warps in two 8-warp groups that take turns on the
-// tensor pipe as in bwd_pingpong.  Each group has its own input planes (TMA, rows in global
-// order), H_L tile, Y and dY; W_{L-1} and W_L are shared.  A group's mainloop runs while it
-// holds the turn; its whole epilogue (jet, output contraction, seeds, output gradients,
-// VJP and the stores of D_L) overlaps the other group's mainloop.  This form serves the
+// Turn-taking form of fwd_head for 2-D, staged through shared memory: the last hidden
+// layer, the output layer, the residual seeds, the output-layer gradients and the VJP into
+// layer L, with the CTA's 16 warps in NG groups (Ring<NG>; kHeadGroups = 4 groups of 4
+// warps, 40-row tiles) that take turns on the tensor pipe.  Each group has its own input
+// planes (TMA, rows in global order), H_L tile, Y and dY; W_{L-1} and W_L are shared.  A
+// group's mainloop runs while it holds the turn; its epilogue (jet, output contraction,
+// seeds, output gradients, VJP and the stores of D_L) overlaps the other groups' mainloops.  This form serves the
 // (u, v, p) head, whose seed reads 25 outputs (one thread per point forms it from the
 // staged outputs), and value boundary rows, where a thread column holds ten points; the
 // stream-function head with first-order rows runs head_pingpong below.
@@ -3494,7 +3494,7 @@ struct HeadOps {
 template <int DIM, int BO, int HEAD>
 struct FwdHeadOps {
   static constexpr int NF = HeadTraits<HEAD>::NF;
-  static constexpr bool kPingPong = DIM == 2;  // 2-D: the two-group kernel over 80-row half tiles
+  static constexpr bool kPingPong = DIM == 2;  // 2-D: the turn-taking kernels (four groups, 40-row tiles)
   // the stream-function head with first-order boundary rows keeps its epilogue in registers
   static constexpr bool kRegisters = BO == 1 && HEAD == FLASHNS_B200_HEAD_PSI;
   static constexpr int kGroups = kHeadGroups;  // turn-taking groups of the 2-D kernels
