@@ -233,3 +233,20 @@ def test_compulsory_bytes_per_kernel_match_the_cfg1_profile():
     r = kernel_rooflines(times, flops, b, 37.1, 6552.6)
     assert 25 < r["backward"]["tflops"] < 27 and abs(r["backward"]["fp64_frac"] - r["backward"]["tflops"] / 37.1) < 1e-12
     assert 2000 < r["backward"]["gbs"] < 2500 and r["reduce"] == {"avg_ms": 0.0101}
+
+
+def test_bench_configurations_are_the_configuration_table():
+    """bench.py --config offers exactly the configurations of flashns_b200.problems, and the
+    two profile-only ones have the sizes their profiles state."""
+    import re
+    from pathlib import Path
+
+    from flashns_b200.problems import CONFIGS, config_points
+    src = (Path(__file__).resolve().parent.parent / "bench.py").read_text()
+    m = re.search(r'"--config", default="cfg1",\s*choices=\[([^\]]*)\]', src)
+    assert m, "bench.py --config choices not found"
+    assert set(re.findall(r'"([a-z0-9]+)"', m.group(1))) == set(CONFIGS)
+    assert CONFIGS["tgv64"]["widths"] == [3, 64, 64, 64, 64, 2]
+    big = config_points("cfg1x64")
+    assert big.interior_count == 1 << 20 and len(big.x) == (1 << 20) + (1 << 18)
+    assert CONFIGS["cfg1x64"]["widths"] == CONFIGS["cfg1"]["widths"]
