@@ -8,7 +8,8 @@ per CTA of the two-group kernels, each with its turn hand-over), which the small
 * cfg1 in full: 16,384 + 4,096 points, the same net;
 * cfg2's widths, 2-128x6-2, on 8,192 + 2,048 points;
 * cfg3's widths, 3-128x5-2 with Q20 space-time jets and Taylor-Green targets, on
-  4,096 + 1,024 points.
+  4,096 + 1,024 points;
+* the profile-only tgv64 net, 3-64x4-2 (the 3-D 64-wide kernels), on 4,096 + 1,024 points.
 
 Points are uniform from seed 1, weights Xavier-normal from seed 0, boundary rows first
 order, as in the benchmark.  Every value of ``[grad, loss]`` must meet the reference
@@ -31,6 +32,9 @@ CASES = {
     "cfg1": ("kovasznay", 16384, 4096, [2, 64, 64, 64, 64, 2]),
     "cfg2_widths": ("kovasznay", 8192, 2048, [2] + [128] * 6 + [2]),
     "cfg3_widths": ("taylor_green", 4096, 1024, [3] + [128] * 5 + [2]),
+    # the 3-D 64-wide kernels (fwd_head, bwd_fused on inner and first layers), which no
+    # benchmark configuration reaches: tgv64's net
+    "tgv64_widths": ("taylor_green", 4096, 1024, [3, 64, 64, 64, 64, 2]),
 }
 
 
